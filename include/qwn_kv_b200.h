@@ -1,0 +1,241 @@
+#ifndef QWN_KV_B200_H
+#define QWN_KV_B200_H
+
+/*
+ * Paged, batched, device-resident quantized KV-cache entry points of
+ * qwn_cuda.so (extension of ABI version 1).
+ *
+ * The reference keeps the quantized caches as contiguous per-layer arrays on
+ * the host (c/qwanto_turboquant.c:515-543, :588-615) and pages only its fp16
+ * cache (c/qwn_paged_kv.c:42-198); its GPU ABI moves host buffers on every
+ * call (c/cuda/qwn_cuda_abi.h:130-149).  These entry points compose the
+ * reference block table with the reference codecs on the GPU:
+ *
+ *   qwn_kv_pool_*      <- QwnKVBlockPool / qwn_kv_pool_init/free
+ *                         (c/qwn_paged_kv.h:15-25, :44-53)
+ *   qwn_kv_seq_append  <- qwn_block_table_append_token, once per sequence in
+ *                         batch order (c/qwn_paged_kv.c:115-138)
+ *   qwn_kv_decode      <- qwn_q8_cache_append + qwn_q8_cache_attention_head
+ *                         (c/qwanto_turboquant.c:632-705) and the TurboQuant
+ *                         pair qwn_turboquant_quantize_token +
+ *                         qwn_turboquant_attention_head (:162-213, :707-768),
+ *                         for every sequence and query head of one layer
+ *   qwn_kv_evict       <- qwn_paged_eviction_update_scores/prune
+ *                         (c/qwanto_pagedeviction.c:54-93), lifted to pages
+ *
+ * All pointers named *_dev are device pointers; host_* are host pointers.
+ * Calls that take a stream enqueue work and return without synchronising;
+ * device-side failures (pool exhausted, bad page id, a wait that timed out)
+ * are latched in a status word read by qwn_kv_pool_check().
+ * Status codes are QwnCudaStatus (qwn_cuda_abi.h).
+ */
+
+#include "qwn_cuda_abi.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QWN_KV_B200_VERSION 1u
+
+/* capability bits reported by qwn_cuda_abi_query in addition to ABI v1's */
+enum {
+    QWN_CUDA_CAP_PAGED_KV = 1ull << 6,        /* qwn_kv_pool_* / qwn_kv_decode */
+    QWN_CUDA_CAP_TQ_KV = 1ull << 7,           /* 4-bit and 3.5-bit codecs */
+    QWN_CUDA_CAP_BATCHED_DEVICE = 1ull << 8,  /* device-pointer batched decode */
+    QWN_CUDA_CAP_SPLIT_KV_MERGE = 1ull << 9,  /* partial (m,l,o) export + merge */
+    QWN_CUDA_CAP_PAGE_EVICTION = 1ull << 10   /* page scores, eviction, compaction */
+};
+
+typedef enum {
+    QWN_KV_CODEC_Q8_B64_F32 = 1,  /* reference Q8: fp32 scale per 64 channels */
+    QWN_KV_CODEC_Q8_HEAD_F16 = 2, /* int8 per token-head, fp16 absmax scale */
+    QWN_KV_CODEC_TQ35_G64 = 3,    /* reference TurboQuant 4/3-bit, groups of 64 */
+    QWN_KV_CODEC_Q4_G32 = 4       /* 4-bit, groups of 32, fp16 range + fp16 min */
+} QwnKvCodec;
+
+/* device status bits latched by kernels */
+enum {
+    QWN_KV_STATUS_POOL_EXHAUSTED = 1u << 0,
+    QWN_KV_STATUS_TABLE_OVERFLOW = 1u << 1,
+    QWN_KV_STATUS_BAD_PAGE = 1u << 2,
+    QWN_KV_STATUS_BAD_SEQUENCE = 1u << 3,
+    QWN_KV_STATUS_WAIT_TIMEOUT = 1u << 4,
+    QWN_KV_STATUS_BAD_LENGTH = 1u << 5
+};
+
+typedef struct {
+    QwnCudaAbiHeader header;
+    int32_t device_id;
+    uint32_t codec;             /* QwnKvCodec */
+    uint32_t layers;
+    uint32_t kv_heads;
+    uint32_t head_dim;          /* must be 128 */
+    uint32_t page_tokens;       /* multiple of 16 (16 = QWN_PAGE_BLOCK_SIZE) */
+    uint32_t total_pages;       /* physical pages in the pool */
+    uint32_t max_seqs;          /* sequence slots (block tables) */
+    uint32_t max_pages_per_seq;
+    uint32_t max_query_heads;   /* largest query_heads used with this pool */
+    uint64_t permutation_seed;  /* 0: free stack total-1-i, as qwn_kv_pool_init;
+                                   else a seeded Fisher-Yates permutation of it */
+    uint64_t memory_budget_bytes; /* 0: no budget beyond the device's free memory */
+} QwnKvPoolOptions;
+
+typedef struct { QwnCudaAbiHeader header; void *opaque; } QwnKvPoolHandle;
+
+typedef struct {
+    QwnCudaAbiHeader header;
+    void *pages_dev;            /* [total_pages][layers][kv_heads][page_tokens/16][tile_bytes] */
+    int32_t *page_table_dev;    /* [max_seqs][max_pages_per_seq], -1 = none */
+    int32_t *seq_lens_dev;      /* [max_seqs] tokens */
+    int32_t *seq_pages_dev;     /* [max_seqs] pages held */
+    int32_t *free_stack_dev;    /* [total_pages] */
+    int32_t *free_top_dev;      /* [1] */
+    float *page_scores_dev;     /* [max_seqs][max_pages_per_seq] eviction EMA */
+    uint32_t *status_dev;       /* [1] QWN_KV_STATUS_* bits */
+    uint64_t tile_bytes, page_bytes, pool_bytes, scratch_bytes;
+    uint32_t attention_ctas, attention_warps; /* persistent grid of qwn_kv_decode */
+    uint32_t reserved;
+} QwnKvPoolInfo;
+
+QWN_CUDA_ABI_API int qwn_kv_pool_create(const QwnKvPoolOptions *options, QwnKvPoolHandle *pool);
+QWN_CUDA_ABI_API int qwn_kv_pool_destroy(QwnKvPoolHandle *pool);
+QWN_CUDA_ABI_API int qwn_kv_pool_get_info(const QwnKvPoolHandle *pool, QwnKvPoolInfo *info);
+/* empty every sequence and rebuild the free stack; synchronous */
+QWN_CUDA_ABI_API int qwn_kv_pool_reset(QwnKvPoolHandle *pool);
+/* synchronise the pool's work, return and clear the latched status bits */
+QWN_CUDA_ABI_API int qwn_kv_pool_check(QwnKvPoolHandle *pool, uint32_t *status_bits);
+
+/* Grow sequences: sequence seq_ids[i] gains counts[i] tokens (1 when
+ * counts_dev is NULL; seq_ids_dev NULL means 0..num_seqs-1).  Pages are
+ * popped from the LIFO free stack in batch order.  All-or-nothing: when the
+ * pool cannot hold the request nothing changes and POOL_EXHAUSTED latches. */
+QWN_CUDA_ABI_API int qwn_kv_seq_append(QwnKvPoolHandle *pool, uint32_t num_seqs,
+                                       const int32_t *seq_ids_dev, const int32_t *counts_dev,
+                                       void *stream);
+
+typedef struct {
+    QwnCudaAbiHeader header;
+    uint32_t layer;
+    uint32_t num_seqs;
+    const int32_t *seq_ids_dev; /* [num_seqs] or NULL = 0..num_seqs-1 */
+    uint32_t query_heads;       /* multiple of kv_heads, at most 8 per kv head */
+    float scale;                /* softmax scale; 0 = 1/sqrt(128) */
+    const float *query_dev;     /* [num_seqs][query_heads][128] fp32 */
+    const float *key_dev;       /* [num_seqs][kv_heads][128] fp32 of the newest token, or NULL */
+    const float *value_dev;     /* same shape as key_dev */
+    float *output_dev;          /* [num_seqs][query_heads][128] fp32 */
+    float *page_mass_dev;       /* optional [max_seqs][max_pages_per_seq]: per-page
+                                   attention mass summed over query heads */
+    uint32_t attend_limit;      /* attend tokens [0, min(len, attend_limit)); 0 = len */
+    uint32_t reserved;
+    void *stream;               /* cudaStream_t; NULL = the pool's stream */
+} QwnKvDecodeRequest;
+
+/* One layer of decode for a batch: when key_dev/value_dev are given, the
+ * newest token of each sequence (position len-1, reserved by
+ * qwn_kv_seq_append) is quantized into its page; then GQA attention over the
+ * sequence's pages (query head h reads kv head h / (query_heads/kv_heads)). */
+QWN_CUDA_ABI_API int qwn_kv_decode(QwnKvPoolHandle *pool, const QwnKvDecodeRequest *request);
+
+/* Quantize-on-append only: the newest token (position len-1) of each
+ * sequence of the batch, for one layer (qwn_q8_cache_append /
+ * qwn_turboquant_quantize_token, c/qwanto_turboquant.c:632-646, :162-213).
+ * key/value: [num_seqs][kv_heads][128] fp32 device arrays. */
+QWN_CUDA_ABI_API int qwn_kv_append(QwnKvPoolHandle *pool, uint32_t layer, uint32_t num_seqs,
+                                   const int32_t *seq_ids_dev, const float *key_dev,
+                                   const float *value_dev, void *stream);
+
+/* Partial attention for split-KV across devices: like qwn_kv_decode without
+ * append over tokens [t_begin, t_end), writing the base-2 partial state
+ * m[q_head], l[q_head], o[q_head][128] (o unnormalised) per sequence. */
+typedef struct {
+    QwnCudaAbiHeader header;
+    uint32_t layer, num_seqs;
+    const int32_t *seq_ids_dev;
+    uint32_t query_heads;
+    float scale;
+    const float *query_dev;
+    float *m_dev;               /* [num_seqs][query_heads] */
+    float *l_dev;               /* [num_seqs][query_heads] */
+    float *o_dev;               /* [num_seqs][query_heads][128] */
+    uint32_t t_begin, t_end;    /* token range; t_end 0 = len */
+    void *stream;
+} QwnKvPartialRequest;
+QWN_CUDA_ABI_API int qwn_kv_partial(QwnKvPoolHandle *pool, const QwnKvPartialRequest *request);
+
+/* out[s][h][:] = merge over parts p of (m, l, o)[p][s][h] */
+QWN_CUDA_ABI_API int qwn_kv_merge_partials(uint32_t parts, uint32_t rows, const float *m_dev,
+                                           const float *l_dev, const float *o_dev,
+                                           float *out_dev, void *stream);
+
+/* Store tokens [first_pos, first_pos+n_tokens) of one sequence and layer
+ * (already reserved with qwn_kv_seq_append): key/value [n_tokens][kv_heads][128]. */
+QWN_CUDA_ABI_API int qwn_kv_store_tokens(QwnKvPoolHandle *pool, int32_t seq_id, uint32_t layer,
+                                         uint32_t first_pos, uint32_t n_tokens,
+                                         const float *key_dev, const float *value_dev,
+                                         void *stream);
+
+/* Synthetic inputs: x = Irwin-Hall(12) sample of the counter-based
+ * generator (seed, kind, seq, layer, index); kind 1 = Q, 2 = K, 3 = V.
+ * Row i of out_dev is position pos_dev[i] of sequence seq_ids_dev[i]:
+ * out[i][c] = x(index = pos*width + c), times 8 where outlier_mask_dev[c]. */
+QWN_CUDA_ABI_API int qwn_kv_generate_rows(float *out_dev, uint32_t rows, uint32_t width,
+                                          uint32_t kind, uint64_t seed, uint32_t layer,
+                                          const int32_t *seq_ids_dev, const int32_t *pos_dev,
+                                          const uint8_t *outlier_mask_dev, void *stream);
+/* Grow sequences to lens (pages in batch order, like qwn_kv_seq_append) and
+ * fill every layer with quantized synthetic K/V of those positions.
+ * outlier_mask_host: optional [layers][kv_heads*128] (1 = K channel x8). */
+QWN_CUDA_ABI_API int qwn_kv_prefill_synthetic(QwnKvPoolHandle *pool, uint32_t num_seqs,
+                                              const int32_t *host_seq_ids,
+                                              const int32_t *host_lens, uint64_t seed,
+                                              const uint8_t *outlier_mask_host, void *stream);
+
+typedef struct {
+    QwnCudaAbiHeader header;
+    uint32_t num_seqs;
+    const int32_t *seq_ids_dev;   /* or NULL = 0..num_seqs-1 */
+    const float *page_mass_dev;   /* [max_seqs][max_pages_per_seq] from qwn_kv_decode */
+    const uint8_t *flags_dev;     /* [num_seqs]: 1 = evict this sequence now */
+    uint32_t token_budget;
+    uint32_t reserved;
+    void *stream;
+} QwnKvEvictRequest;
+/* score = 0.8*score + 0.2*mass on every page of the batch; then for each
+ * flagged sequence longer than the budget, evict its lowest-score pages
+ * (page 0 and the last page protected, ties to the lower index) until
+ * len <= budget, compact the table and push the freed pages on the free
+ * stack in ascending logical order, sequences in batch order. */
+QWN_CUDA_ABI_API int qwn_kv_evict(QwnKvPoolHandle *pool, const QwnKvEvictRequest *request);
+
+/* End-to-end decode step through host buffers (the plugin path with copies
+ * inside): grows every sequence 0..num_seqs-1 by one token, copies each
+ * layer's inputs host->device, runs qwn_kv_decode per layer and copies the
+ * outputs back; returns after the last copy.  Host arrays are
+ * [layers][num_seqs][heads][128] fp32 (heads = query_heads for query/output,
+ * kv_heads for key/value); pinned host memory gives overlapped copies. */
+typedef struct {
+    QwnCudaAbiHeader header;
+    uint32_t num_layers, num_seqs, query_heads;
+    float scale;
+    const float *host_query;
+    const float *host_key;
+    const float *host_value;
+    float *host_output;
+} QwnKvHostStepRequest;
+QWN_CUDA_ABI_API int qwn_kv_decode_step_host(QwnKvPoolHandle *pool,
+                                             const QwnKvHostStepRequest *request,
+                                             QwnCudaTelemetry *telemetry);
+
+/* copy a device range to/from host (tests and tools without a CUDA runtime) */
+QWN_CUDA_ABI_API int qwn_kv_memcpy_d2h(void *host, const void *dev, uint64_t bytes);
+QWN_CUDA_ABI_API int qwn_kv_memcpy_h2d(void *dev, const void *host, uint64_t bytes);
+/* kernel launches issued by this library since load (for evidence in runs) */
+QWN_CUDA_ABI_API uint64_t qwn_kv_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWN_KV_B200_H */

@@ -1,0 +1,878 @@
+// GQA decode attention over the quantized paged pool, split-KV.
+//
+// Work decomposition ("stream-K" over tiles): the units of work are
+// (sequence, kv head, 16-token tile).  A persistent grid of warps splits the
+// T units of the batch into W equal contiguous ranges, so every warp streams
+// the same number of tiles whatever the mix of context lengths.  A warp
+// keeps the online-softmax state (m, l, o) of the segment (sequence, kv head)
+// it is in; at a segment boundary it either writes the final output (when it
+// covered the whole segment) or a partial, and the last warp to finish a
+// segment merges the partials in warp order (deterministic).
+//
+// Each warp owns a private pipeline of kStages shared-memory stages filled by
+// 1-D cp.async.bulk copies (no multicast) completed on per-stage mbarriers.
+// The tile layout in HBM is arranged so that each lane's mma.sync fragments
+// are a few conflict-free 128-bit shared loads.  Dequantisation happens in
+// registers: biased int8 / 4-bit codes become exact f16 by byte permutes, the
+// query is split hi+lo into f16 rows 0-7 / 8-15 of the m16n8k16 A operand (the
+// GQA group of G<=8 query heads uses rows 0..G-1), scales and zero points are
+// applied in fp32 outside the MMA, so the result tracks the reference's fp32
+// arithmetic (c/qwanto_turboquant.c:648-705, :218-288) within ~1e-6.
+#include "kv_internal.cuh"
+
+#include <float.h>
+
+namespace qkv {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kNuInit = 7.888609052210118e-31f;  // 2^-100
+
+struct AttnArgs {
+    const uint8_t *pages;
+    uint64_t page_bytes;
+    uint32_t tile_bytes, tpp, page_tokens;
+    const int32_t *page_table;
+    uint32_t mp, total_pages, max_seqs;
+    const int32_t *seq_lens;
+    const int32_t *seq_ids;
+    uint32_t num_seqs, kv_heads, group, layer;
+    uint32_t attend_limit, t_begin, t_end;
+    const float *query;
+    float *output;
+    float scale_log2;
+    float *partials;
+    uint32_t *counters;
+    float2 *tile_mass;
+    float2 *seg_ml;
+    float *part_m, *part_l, *part_o;  // non-null: export unnormalised (m, l, o)
+    uint32_t *status;
+};
+
+__device__ __forceinline__ float pow2ceil(float x) {
+    uint32_t b = __float_as_uint(x);
+    if (b & 0x7FFFFFu) b = (b & 0x7F800000u) + 0x00800000u;
+    return __uint_as_float(b);
+}
+__device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w & 0xFFFF))); }
+__device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w >> 16))); }
+
+__device__ __forceinline__ void split_hilo(float x, __half &hi, __half &lo) {
+    hi = __float2half_rn(x);
+    lo = __float2half_rn(x - __half2float(hi));
+}
+__device__ __forceinline__ uint32_t pack2(__half a, __half b) {
+    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+// A-operand rows gid (hi) and gid+8 (lo) for four values at k-positions
+// (2tig, 2tig+1) and (2tig+8, 2tig+9)
+__device__ __forceinline__ void make_a(const float (&v)[4], uint32_t (&a)[4]) {
+    __half h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) split_hilo(v[i], h[i], l[i]);
+    a[0] = pack2(h[0], h[1]);
+    a[1] = pack2(l[0], l[1]);
+    a[2] = pack2(h[2], h[3]);
+    a[3] = pack2(l[2], l[3]);
+}
+
+// ---------------------------------------------------------------------------
+// softmax bookkeeping shared by the codecs.  s[i]: base-2 scores of this
+// lane's four tokens (4tig+i) for row gid, -inf when masked.  Returns the
+// probabilities p[i] after rescaling the accumulators when the max grows.
+// ---------------------------------------------------------------------------
+template <class Acc>
+__device__ __forceinline__ void online_softmax(const float (&s)[4], float (&p)[4], float &m, float &l,
+                                               Acc &acc) {
+    float tmax = fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3]));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+    float m_new = fmaxf(m, tmax);
+    if (__any_sync(0xffffffffu, m_new > m)) {
+        float alpha = ex2(m - m_new);
+        l *= alpha;
+        acc.rescale_all(alpha);
+        m = m_new;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) p[i] = ex2(s[i] - m);
+    l += (p[0] + p[1]) + (p[2] + p[3]);
+}
+
+// value normaliser: keep nu >= every value scale seen so that p*scale/nu <= 1
+template <class Acc>
+__device__ __forceinline__ void update_nu(float vmax, int x, Acc &acc) {
+    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+    if (vmax > acc.nu[x]) {
+        float nn = pow2ceil(vmax);
+        acc.rescale_part(x, acc.nu[x] / nn);
+        acc.nu[x] = nn;
+        acc.inv_nu[x] = 1.0f / nn;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// codecs
+// ---------------------------------------------------------------------------
+template <int CODEC> struct Codec;
+
+// int8 codes, per-token-head fp16 scale (4160-byte tile)
+template <> struct Codec<QWN_KV_CODEC_Q8_HEAD_F16> {
+    static constexpr int kBytes = 4160, kStages = 4, kNu = 1;
+    struct Frag { uint32_t a[8][4]; };
+    struct Acc {
+        float o[16][4];
+        float nu[kNu], inv_nu[kNu];
+        __device__ void reset() {
+#pragma unroll
+            for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+            nu[0] = kNuInit; inv_nu[0] = 1.0f / kNuInit;
+        }
+        __device__ void rescale_all(float f) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) { o[j][0] *= f; o[j][1] *= f; o[j][2] *= f; o[j][3] *= f; }
+        }
+        __device__ void rescale_part(int, float f) { rescale_all(f); }
+    };
+    __device__ static int dim_of(int j, int tig, int c) { return 8 * j + 2 * tig + c; }
+    // k-step s covers dims 64(s>>2) + 16tig + 4(s&3) + {0,1 | 2,3}
+    __device__ static void load_q(Frag &f, const float *q, int tig) {
+#pragma unroll
+        for (int s = 0; s < 8; s++) {
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (q) {
+                float4 x = *reinterpret_cast<const float4 *>(q + 64 * (s >> 2) + 16 * tig + 4 * (s & 3));
+                v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+            }
+            make_a(v, f.a[s]);
+        }
+    }
+    __device__ static float out_value(const Acc &acc, int j, int c, float) {
+        return (acc.o[j][c] + acc.o[j][c + 2]) * acc.nu[0];
+    }
+    __device__ static void compute(const uint8_t *tile, const Frag &f, Acc &acc, float &m, float &l,
+                                   int t_lo, int t_hi, float scale_log2, float &tile_u) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        float s[4];
+        const uint2 ksr = *reinterpret_cast<const uint2 *>(tile + 4096 + 8 * tig);
+        const float ks[4] = {half_lo(ksr.x), half_hi(ksr.x), half_lo(ksr.y), half_hi(ksr.y)};
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float acc_k[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint4 *kp = reinterpret_cast<const uint4 *>(tile + h * 1024 + lane * 32);
+            const uint4 w0 = kp[gid & 1], w1 = kp[(gid & 1) ^ 1];
+            const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int st = 0; st < 8; st++) {
+                uint32_t b0, b1;
+                u8x4_to_h2x2(wd[st], b0, b1);
+                mma16816(acc_k, f.a[st], b0, b1);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int i = 2 * h + j, t = 4 * tig + i;
+                const float raw = acc_k[j] + acc_k[j + 2];
+                s[i] = (t >= t_lo && t < t_hi) ? raw * ks[i] * scale_log2 : -INFINITY;
+            }
+        }
+        float p[4];
+        online_softmax(s, p, m, l, acc);
+        const uint2 vsr = *reinterpret_cast<const uint2 *>(tile + 4128 + 8 * tig);
+        float vs[4] = {half_lo(vsr.x), half_hi(vsr.x), half_lo(vsr.y), half_hi(vsr.y)};
+        float vmax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int t = 4 * tig + i;
+            if (!(t >= t_lo && t < t_hi)) vs[i] = 0.f;
+            vmax = fmaxf(vmax, vs[i]);
+        }
+        update_nu(vmax, 0, acc);
+        float pt[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) pt[i] = p[i] * vs[i] * acc.inv_nu[0];
+        uint32_t a[4];
+        make_a(pt, a);
+        const uint8_t *vt = tile + 2048 + lane * 64;
+        const int sw = (lane >> 1) & 3;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint4 c = *reinterpret_cast<const uint4 *>(vt + ((q ^ sw) << 4));
+            const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                uint32_t b0, b1;
+                u8x4_to_h2x2(wv[r], b0, b1);
+                mma16816(acc.o[4 * q + r], a, b0, b1);
+            }
+        }
+        tile_u = (p[0] + p[1]) + (p[2] + p[3]);
+    }
+};
+
+// int8 codes, fp32 scale per 64 channels: the reference Q8 (4352-byte tile)
+template <> struct Codec<QWN_KV_CODEC_Q8_B64_F32> {
+    static constexpr int kBytes = 4352, kStages = 4, kNu = 2;
+    using Frag = Codec<QWN_KV_CODEC_Q8_HEAD_F16>::Frag;
+    struct Acc {
+        float o[16][4];
+        float nu[kNu], inv_nu[kNu];
+        __device__ void reset() {
+#pragma unroll
+            for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+            nu[0] = nu[1] = kNuInit; inv_nu[0] = inv_nu[1] = 1.0f / kNuInit;
+        }
+        __device__ void rescale_all(float f) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) { o[j][0] *= f; o[j][1] *= f; o[j][2] *= f; o[j][3] *= f; }
+        }
+        __device__ void rescale_part(int x, float f) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int jj = 8 * x + j;
+                o[jj][0] *= f; o[jj][1] *= f; o[jj][2] *= f; o[jj][3] *= f;
+            }
+        }
+    };
+    __device__ static int dim_of(int j, int tig, int c) { return 8 * j + 2 * tig + c; }
+    __device__ static void load_q(Frag &f, const float *q, int tig) {
+        Codec<QWN_KV_CODEC_Q8_HEAD_F16>::load_q(f, q, tig);
+    }
+    __device__ static float out_value(const Acc &acc, int j, int c, float) {
+        return (acc.o[j][c] + acc.o[j][c + 2]) * acc.nu[j >> 3];
+    }
+    __device__ static void compute(const uint8_t *tile, const Frag &f, Acc &acc, float &m, float &l,
+                                   int t_lo, int t_hi, float scale_log2, float &tile_u) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        float s[4];
+        const float4 k0 = *reinterpret_cast<const float4 *>(tile + 4096 + 16 * tig);
+        const float4 k1 = *reinterpret_cast<const float4 *>(tile + 4096 + 64 + 16 * tig);
+        const float ks0[4] = {k0.x, k0.y, k0.z, k0.w}, ks1[4] = {k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint4 *kp = reinterpret_cast<const uint4 *>(tile + h * 1024 + lane * 32);
+            const uint4 w0 = kp[gid & 1], w1 = kp[(gid & 1) ^ 1];
+            const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int st = 0; st < 4; st++) {
+                uint32_t b0, b1;
+                u8x4_to_h2x2(wd[st], b0, b1);
+                mma16816(a0, f.a[st], b0, b1);
+                u8x4_to_h2x2(wd[st + 4], b0, b1);
+                mma16816(a1, f.a[st + 4], b0, b1);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int i = 2 * h + j, t = 4 * tig + i;
+                const float raw = (a0[j] + a0[j + 2]) * ks0[i] + (a1[j] + a1[j + 2]) * ks1[i];
+                s[i] = (t >= t_lo && t < t_hi) ? raw * scale_log2 : -INFINITY;
+            }
+        }
+        float p[4];
+        online_softmax(s, p, m, l, acc);
+        uint32_t a[2][4];
+#pragma unroll
+        for (int x = 0; x < 2; x++) {
+            const float4 v4 = *reinterpret_cast<const float4 *>(tile + 4224 + 64 * x + 16 * tig);
+            float vs[4] = {v4.x, v4.y, v4.z, v4.w};
+            float vmax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int t = 4 * tig + i;
+                if (!(t >= t_lo && t < t_hi)) vs[i] = 0.f;
+                vmax = fmaxf(vmax, vs[i]);
+            }
+            update_nu(vmax, x, acc);
+            float pt[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) pt[i] = p[i] * vs[i] * acc.inv_nu[x];
+            make_a(pt, a[x]);
+        }
+        const uint8_t *vt = tile + 2048 + lane * 64;
+        const int sw = (lane >> 1) & 3;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint4 c = *reinterpret_cast<const uint4 *>(vt + ((q ^ sw) << 4));
+            const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                uint32_t b0, b1;
+                u8x4_to_h2x2(wv[r], b0, b1);
+                mma16816(acc.o[4 * q + r], a[q >> 1], b0, b1);
+            }
+        }
+        tile_u = (p[0] + p[1]) + (p[2] + p[3]);
+    }
+};
+
+// 4-bit codes, groups of 32 with fp16 range + fp16 min (2560-byte tile)
+template <> struct Codec<QWN_KV_CODEC_Q4_G32> {
+    static constexpr int kBytes = 2560, kStages = 6, kNu = 4;
+    struct Frag { uint32_t a[8][4]; float qsum[4]; };
+    struct Acc {
+        float o[16][4];
+        float z[4];  // sum_t p_t * min_t,g (this lane's tokens, row gid)
+        float nu[kNu], inv_nu[kNu];
+        __device__ void reset() {
+#pragma unroll
+            for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+#pragma unroll
+            for (int g = 0; g < 4; g++) { z[g] = 0.f; nu[g] = kNuInit; inv_nu[g] = 1.0f / kNuInit; }
+        }
+        __device__ void rescale_all(float f) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) { o[j][0] *= f; o[j][1] *= f; o[j][2] *= f; o[j][3] *= f; }
+#pragma unroll
+            for (int g = 0; g < 4; g++) z[g] *= f;
+        }
+        __device__ void rescale_part(int g, float f) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int jj = 4 * g + j;
+                o[jj][0] *= f; o[jj][1] *= f; o[jj][2] *= f; o[jj][3] *= f;
+            }
+        }
+    };
+    __device__ static int dim_of(int j, int tig, int c) { return 8 * j + 2 * tig + c; }
+    // k-step s: group g = s>>1, dims 32g + 16(s&1) + 4tig + {0,1 | 2,3}
+    __device__ static void load_q(Frag &f, const float *q, int tig) {
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            float part = 0.f;
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                float v[4] = {0.f, 0.f, 0.f, 0.f};
+                if (q) {
+                    float4 x = *reinterpret_cast<const float4 *>(q + 32 * g + 16 * e + 4 * tig);
+                    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+                }
+                part += (v[0] + v[1]) + (v[2] + v[3]);
+                make_a(v, f.a[2 * g + e]);
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            f.qsum[g] = part;
+        }
+    }
+    // z[] must be reduced across the four lanes of a row before this is used
+    __device__ static float out_value(const Acc &acc, int j, int c, float zsum) {
+        return (acc.o[j][c] + acc.o[j][c + 2]) * acc.nu[j >> 2] + zsum;
+    }
+    __device__ static void compute(const uint8_t *tile, const Frag &f, Acc &acc, float &m, float &l,
+                                   int t_lo, int t_hi, float scale_log2, float &tile_u) {
+        const int lane = threadIdx.x & 31, tig = lane & 3;
+        float s[4];
+        float kr[4][4], km[4][4];  // [group][token i]
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            const uint4 kp = *reinterpret_cast<const uint4 *>(tile + 2048 + 64 * g + 16 * tig);
+            const uint32_t w[4] = {kp.x, kp.y, kp.z, kp.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                kr[g][i] = half_lo(w[i]) * (1.0f / 15.0f);
+                km[g][i] = half_hi(w[i]);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint4 kw = *reinterpret_cast<const uint4 *>(tile + h * 512 + lane * 16);
+            const uint32_t wd[4] = {kw.x, kw.y, kw.z, kw.w};
+            float raw[2] = {0.f, 0.f};
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                float acc_k[4] = {0.f, 0.f, 0.f, 0.f};
+                uint32_t r[4];
+                nib8_to_h2x4(wd[g], r);
+                mma16816(acc_k, f.a[2 * g], r[0], r[1]);
+                mma16816(acc_k, f.a[2 * g + 1], r[2], r[3]);
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int i = 2 * h + j;
+                    raw[j] += kr[g][i] * (acc_k[j] + acc_k[j + 2]) + km[g][i] * f.qsum[g];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int i = 2 * h + j, t = 4 * tig + i;
+                s[i] = (t >= t_lo && t < t_hi) ? raw[j] * scale_log2 : -INFINITY;
+            }
+        }
+        float p[4];
+        online_softmax(s, p, m, l, acc);
+        uint32_t a[4][4];
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            const uint4 vp = *reinterpret_cast<const uint4 *>(tile + 2304 + 64 * g + 16 * tig);
+            const uint32_t w[4] = {vp.x, vp.y, vp.z, vp.w};
+            float vs[4], vmax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int t = 4 * tig + i;
+                const bool ok = t >= t_lo && t < t_hi;
+                vs[i] = ok ? half_lo(w[i]) * (1.0f / 15.0f) : 0.f;
+                const float mn = ok ? half_hi(w[i]) : 0.f;
+                acc.z[g] += p[i] * mn;
+                vmax = fmaxf(vmax, vs[i]);
+            }
+            update_nu(vmax, g, acc);
+            float pt[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) pt[i] = p[i] * vs[i] * acc.inv_nu[g];
+            make_a(pt, a[g]);
+        }
+        const uint8_t *vt = tile + 1024 + lane * 32;
+        const int sw = (lane >> 2) & 1;
+#pragma unroll
+        for (int cc = 0; cc < 2; cc++) {
+            const uint4 c = *reinterpret_cast<const uint4 *>(vt + ((cc ^ sw) << 4));
+            const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const int wi = 4 * cc + r;  // n-tiles 2wi, 2wi+1 (group wi>>1)
+                uint32_t b[4];
+                nib8_to_h2x4(wv[r], b);
+                mma16816(acc.o[2 * wi], a[wi >> 1], b[0], b[1]);
+                mma16816(acc.o[2 * wi + 1], a[wi >> 1], b[2], b[3]);
+            }
+        }
+        tile_u = (p[0] + p[1]) + (p[2] + p[3]);
+    }
+};
+
+// ---------------------------------------------------------------------------
+// batch geometry
+// ---------------------------------------------------------------------------
+struct Geo {
+    int32_t seq, tok_lo, tok_hi;
+    uint32_t tile0, ntiles;
+};
+
+__device__ __forceinline__ Geo geo_of(const AttnArgs &A, uint32_t i) {
+    Geo g;
+    g.seq = A.seq_ids ? A.seq_ids[i] : (int32_t)i;
+    g.tok_lo = g.tok_hi = 0;
+    g.tile0 = g.ntiles = 0;
+    if (g.seq < 0 || (uint32_t)g.seq >= A.max_seqs) {
+        latch(A.status, QWN_KV_STATUS_BAD_SEQUENCE);
+        return g;
+    }
+    int32_t hi = A.seq_lens[g.seq];
+    if (A.attend_limit && hi > (int32_t)A.attend_limit) hi = (int32_t)A.attend_limit;
+    if (A.t_end && hi > (int32_t)A.t_end) hi = (int32_t)A.t_end;
+    int32_t lo = (int32_t)A.t_begin;
+    if (hi > (int32_t)(A.mp * A.page_tokens)) {
+        latch(A.status, QWN_KV_STATUS_BAD_LENGTH);
+        hi = (int32_t)(A.mp * A.page_tokens);
+    }
+    if (hi > lo) {
+        g.tok_lo = lo;
+        g.tok_hi = hi;
+        g.tile0 = (uint32_t)lo / 16u;
+        g.ntiles = ((uint32_t)hi + 15u) / 16u - g.tile0;
+    }
+    return g;
+}
+
+// position of a unit: batch entry i, kv head h, tile within the entry
+struct Walk {
+    uint32_t i, h, tile;
+    uint64_t seg_base;  // global unit index of (i, h, tile 0)
+    Geo geo;
+};
+
+__device__ __forceinline__ void walk_next_segment(const AttnArgs &A, Walk &w) {
+    w.seg_base += w.geo.ntiles;
+    w.tile = 0;
+    if (++w.h == A.kv_heads) {
+        w.h = 0;
+        do {
+            ++w.i;
+            if (w.i >= A.num_seqs) { w.geo.ntiles = 0; return; }
+            w.geo = geo_of(A, w.i);
+        } while (w.geo.ntiles == 0);
+    }
+}
+__device__ __forceinline__ void walk_advance(const AttnArgs &A, Walk &w, uint32_t k) {
+    while (k > 0) {
+        const uint32_t rem = w.geo.ntiles - w.tile;
+        if (k < rem) { w.tile += k; return; }
+        k -= rem;
+        walk_next_segment(A, w);
+        if (w.i >= A.num_seqs) return;
+    }
+}
+__device__ __forceinline__ const uint8_t *unit_addr(const AttnArgs &A, const Walk &w) {
+    const uint32_t tg = w.geo.tile0 + w.tile;
+    const uint32_t lp = tg / A.tpp, tin = tg % A.tpp;
+    int32_t pg = -1;
+    if (lp < A.mp) pg = A.page_table[(size_t)w.geo.seq * A.mp + lp];
+    if (pg < 0 || (uint32_t)pg >= A.total_pages) {
+        latch(A.status, QWN_KV_STATUS_BAD_PAGE);
+        pg = 0;  // stay in bounds; the latched status marks the result invalid
+    }
+    return A.pages + (size_t)pg * A.page_bytes +
+           ((size_t)(A.layer * A.kv_heads + w.h) * A.tpp + tin) * A.tile_bytes;
+}
+
+__device__ __forceinline__ uint32_t warp_incl_scan(uint32_t v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int CODEC>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnArgs A) {
+    using CD = Codec<CODEC>;
+    constexpr int S = CD::kStages, B = CD::kBytes;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    uint8_t *wsm = smem + (size_t)warp * S * B;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)kWarpsPerCta * S * B) + warp * S;
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < S; st++) mbar_init(&bars[st], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+
+    const uint32_t HK = A.kv_heads, G = A.group, Hq = HK * G;
+    const uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
+    const uint64_t wid = (uint64_t)blockIdx.x * kWarpsPerCta + warp;
+
+    // total units of the batch
+    uint64_t T = 0;
+    for (uint32_t base = 0; base < A.num_seqs; base += 32) {
+        const uint32_t i = base + lane;
+        uint32_t u = i < A.num_seqs ? geo_of(A, i).ntiles * HK : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
+        T += u;
+    }
+    if (T == 0) return;
+    const uint64_t u0 = wid * T / W, u1 = (wid + 1) * T / W;
+    if (u0 >= u1) return;
+
+    // locate u0
+    Walk cons;
+    {
+        uint64_t acc = 0;
+        for (uint32_t base = 0; base < A.num_seqs; base += 32) {
+            const uint32_t i = base + lane;
+            const uint32_t u = i < A.num_seqs ? geo_of(A, i).ntiles * HK : 0;
+            const uint32_t incl = warp_incl_scan(u);
+            const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
+            if (u0 < acc + tot) {
+                const uint32_t ball = __ballot_sync(0xffffffffu, acc + incl > u0);
+                const int L = __ffs(ball) - 1;
+                const uint32_t excl = __shfl_sync(0xffffffffu, incl - u, L);
+                cons.i = base + L;
+                cons.geo = geo_of(A, cons.i);
+                const uint64_t rem = u0 - (acc + excl);
+                cons.h = (uint32_t)(rem / cons.geo.ntiles);
+                cons.tile = (uint32_t)(rem % cons.geo.ntiles);
+                cons.seg_base = acc + excl + (uint64_t)cons.h * cons.geo.ntiles;
+                break;
+            }
+            acc += tot;
+        }
+    }
+
+    // address window: lane L holds the source of unit win_base + L
+    Walk win = cons;
+    uint64_t win_base = u0;
+    const uint8_t *my_src = nullptr;
+    {
+        Walk t = win;
+        walk_advance(A, t, lane);
+        if (win_base + lane < u1) my_src = unit_addr(A, t);
+    }
+#pragma unroll
+    for (int st = 0; st < S; st++) {
+        const uint64_t j = u0 + st;
+        const uint8_t *src = (const uint8_t *)__shfl_sync(0xffffffffu, (unsigned long long)my_src, st);
+        if (j < u1 && lane == 0) {
+            mbar_expect_tx(&bars[st], B);
+            bulk_g2s(wsm + st * B, src, B, &bars[st]);
+        }
+    }
+
+    typename CD::Frag frag;
+    typename CD::Acc acc;
+    float m = -INFINITY, l = 0.f;
+    const float2 *no_mass = nullptr;
+    (void)no_mass;
+
+    for (uint64_t c = u0; c < u1; ++c) {
+        const uint32_t st = (uint32_t)((c - u0) % S);
+        const uint32_t par = (uint32_t)(((c - u0) / S) & 1);
+        if (cons.tile == 0 || c == u0) {
+            const float *q = nullptr;
+            if ((uint32_t)gid < G)
+                q = A.query + ((size_t)cons.i * Hq + (size_t)cons.h * G + gid) * kHeadDim;
+            CD::load_q(frag, q, tig);
+            acc.reset();
+            m = -INFINITY;
+            l = 0.f;
+        }
+        if (!mbar_wait_bounded(&bars[st], par)) {
+            if (lane == 0) latch(A.status, QWN_KV_STATUS_WAIT_TIMEOUT);
+            // wait (bounded) for the copies still in flight into this warp's stages
+            for (uint64_t d = c + 1; d < u1 && d < c + S; ++d) {
+                const uint32_t s2 = (uint32_t)((d - u0) % S), p2 = (uint32_t)(((d - u0) / S) & 1);
+                mbar_wait_bounded(&bars[s2], p2);
+            }
+            return;
+        }
+        const int tile_tok0 = (int)(cons.geo.tile0 + cons.tile) * 16;
+        const int t_lo = max(cons.geo.tok_lo - tile_tok0, 0);
+        const int t_hi = min(cons.geo.tok_hi - tile_tok0, 16);
+        float tile_u;
+        CD::compute(wsm + st * B, frag, acc, m, l, t_lo, t_hi, A.scale_log2, tile_u);
+        if (A.tile_mass) {
+            tile_u += __shfl_xor_sync(0xffffffffu, tile_u, 1);
+            tile_u += __shfl_xor_sync(0xffffffffu, tile_u, 2);
+            if (tig == 0 && (uint32_t)gid < G) A.tile_mass[c * kMaxGroup + gid] = make_float2(tile_u, m);
+        }
+        __syncwarp();
+
+        // refill this stage with unit c + S
+        const uint64_t j = c + S;
+        if (j < u1) {
+            if (j >= win_base + 32) {
+                walk_advance(A, win, 32);
+                win_base += 32;
+                Walk t = win;
+                walk_advance(A, t, lane);
+                my_src = (win_base + lane < u1) ? unit_addr(A, t) : nullptr;
+            }
+            const uint8_t *src =
+                (const uint8_t *)__shfl_sync(0xffffffffu, (unsigned long long)my_src, (int)(j - win_base));
+            if (lane == 0) {
+                fence_proxy_async_shared();
+                mbar_expect_tx(&bars[st], B);
+                bulk_g2s(wsm + st * B, src, B, &bars[st]);
+            }
+        }
+
+        // end of this warp's share of the segment?
+        if (cons.tile + 1 == cons.geo.ntiles || c + 1 == u1) {
+            const uint32_t s_idx = cons.i * HK + cons.h;
+            const uint64_t Us = cons.seg_base, ns = cons.geo.ntiles;
+            const uint64_t wa = ((Us + 1) * W - 1) / T, wb = ((Us + ns) * W - 1) / T;
+            float lr = l;
+            lr += __shfl_xor_sync(0xffffffffu, lr, 1);
+            lr += __shfl_xor_sync(0xffffffffu, lr, 2);
+            float zs[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (CODEC == QWN_KV_CODEC_Q4_G32) {
+#pragma unroll
+                for (int g = 0; g < 4; g++) {
+                    float z = acc.z[g];
+                    z += __shfl_xor_sync(0xffffffffu, z, 1);
+                    z += __shfl_xor_sync(0xffffffffu, z, 2);
+                    zs[g] = z;
+                }
+            }
+            const size_t row0 = (size_t)cons.i * Hq + (size_t)cons.h * G;
+            if (wa == wb) {
+                // this warp saw the whole segment: final output
+                if ((uint32_t)gid < G) {
+                    const size_t row = row0 + gid;
+                    if (A.part_o) {
+                        float *o = A.part_o + row * kHeadDim;
+#pragma unroll
+                        for (int jn = 0; jn < 16; jn++)
+#pragma unroll
+                            for (int cc = 0; cc < 2; cc++)
+                                o[CD::dim_of(jn, tig, cc)] = CD::out_value(acc, jn, cc, zs[jn >> 2]);
+                        if (tig == 0) { A.part_m[row] = m; A.part_l[row] = lr; }
+                    } else {
+                        const float inv = lr > 0.f ? 1.0f / lr : 0.f;
+                        float *o = A.output + row * kHeadDim;
+#pragma unroll
+                        for (int jn = 0; jn < 16; jn++)
+#pragma unroll
+                            for (int cc = 0; cc < 2; cc++)
+                                o[CD::dim_of(jn, tig, cc)] = CD::out_value(acc, jn, cc, zs[jn >> 2]) * inv;
+                    }
+                    if (A.seg_ml && tig == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + gid] = make_float2(m, lr);
+                }
+            } else {
+                float *slot = A.partials + (size_t)(wid + s_idx) * kPartialFloats;
+                if ((uint32_t)gid < G) {
+#pragma unroll
+                    for (int jn = 0; jn < 16; jn++)
+#pragma unroll
+                        for (int cc = 0; cc < 2; cc++)
+                            slot[gid * kHeadDim + CD::dim_of(jn, tig, cc)] =
+                                CD::out_value(acc, jn, cc, zs[jn >> 2]);
+                    if (tig == 0) {
+                        slot[kMaxGroup * kHeadDim + gid] = m;
+                        slot[kMaxGroup * kHeadDim + kMaxGroup + gid] = lr;
+                    }
+                }
+                __threadfence();
+                __syncwarp();
+                uint32_t old = 0;
+                if (lane == 0) old = atomicAdd(&A.counters[s_idx], 1u);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old == (uint32_t)(wb - wa)) {
+                    __threadfence();
+                    const uint32_t nparts = (uint32_t)(wb - wa + 1);
+                    for (uint32_t g = 0; g < G; g++) {
+                        float ms = -INFINITY;
+                        for (uint32_t pp = 0; pp < nparts; pp++) {
+                            const float *sl = A.partials + (size_t)(wa + pp + s_idx) * kPartialFloats;
+                            ms = fmaxf(ms, __ldcg(sl + kMaxGroup * kHeadDim + g));
+                        }
+                        float ls = 0.f;
+                        float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (uint32_t pp = 0; pp < nparts; pp++) {
+                            const float *sl = A.partials + (size_t)(wa + pp + s_idx) * kPartialFloats;
+                            const float wgt = ex2(__ldcg(sl + kMaxGroup * kHeadDim + g) - ms);
+                            ls += __ldcg(sl + kMaxGroup * kHeadDim + kMaxGroup + g) * wgt;
+                            const float4 v = __ldcg(reinterpret_cast<const float4 *>(sl + g * kHeadDim) + lane);
+                            o4.x += v.x * wgt; o4.y += v.y * wgt; o4.z += v.z * wgt; o4.w += v.w * wgt;
+                        }
+                        const size_t row = row0 + g;
+                        if (A.part_o) {
+                            reinterpret_cast<float4 *>(A.part_o + row * kHeadDim)[lane] = o4;
+                            if (lane == 0) { A.part_m[row] = ms; A.part_l[row] = ls; }
+                        } else {
+                            const float inv = ls > 0.f ? 1.0f / ls : 0.f;
+                            reinterpret_cast<float4 *>(A.output + row * kHeadDim)[lane] =
+                                make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
+                        }
+                        if (A.seg_ml && lane == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + g] = make_float2(ms, ls);
+                    }
+                    if (lane == 0) A.counters[s_idx] = 0u;
+                }
+            }
+        }
+        // next unit
+        if (c + 1 < u1) {
+            if (++cons.tile == cons.geo.ntiles) walk_next_segment(A, cons);
+        }
+    }
+}
+
+// merge of partial states produced on several devices (base-2 domain)
+__global__ void merge_kernel(uint32_t parts, uint32_t rows, const float *m, const float *l,
+                             const float *o, float *out) {
+    const uint32_t row = blockIdx.x;
+    const uint32_t d = threadIdx.x;
+    if (row >= rows || d >= kHeadDim) return;
+    float ms = -INFINITY;
+    for (uint32_t p = 0; p < parts; p++) ms = fmaxf(ms, m[(size_t)p * rows + row]);
+    float ls = 0.f, acc = 0.f;
+    for (uint32_t p = 0; p < parts; p++) {
+        const float mp = m[(size_t)p * rows + row];
+        const float w = mp == -INFINITY ? 0.f : ex2(mp - ms);
+        ls += l[(size_t)p * rows + row] * w;
+        acc += o[((size_t)p * rows + row) * kHeadDim + d] * w;
+    }
+    out[(size_t)row * kHeadDim + d] = ls > 0.f ? acc / ls : 0.f;
+}
+
+template <int CODEC>
+cudaError_t launch_codec(Pool *p, const AttnArgs &A, cudaStream_t s) {
+    using CD = Codec<CODEC>;
+    const size_t smem = (size_t)kWarpsPerCta * CD::kStages * CD::kBytes +
+                        (size_t)kWarpsPerCta * CD::kStages * sizeof(uint64_t);
+    static bool configured[64] = {false};
+    if (!configured[p->device & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured[p->device & 63] = true;
+    }
+    attn_kernel<CODEC><<<p->attn_ctas, kWarpsPerCta * 32, smem, s>>>(A);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t attention_smem_bytes(uint32_t codec) {
+    switch (codec) {
+        case QWN_KV_CODEC_Q8_HEAD_F16: {
+            using CD = Codec<QWN_KV_CODEC_Q8_HEAD_F16>;
+            return (size_t)kWarpsPerCta * CD::kStages * (CD::kBytes + 8);
+        }
+        case QWN_KV_CODEC_Q8_B64_F32: {
+            using CD = Codec<QWN_KV_CODEC_Q8_B64_F32>;
+            return (size_t)kWarpsPerCta * CD::kStages * (CD::kBytes + 8);
+        }
+        case QWN_KV_CODEC_Q4_G32: {
+            using CD = Codec<QWN_KV_CODEC_Q4_G32>;
+            return (size_t)kWarpsPerCta * CD::kStages * (CD::kBytes + 8);
+        }
+        default: return 0;
+    }
+}
+
+const void *attention_kernel_ptr(uint32_t codec) {
+    switch (codec) {
+        case QWN_KV_CODEC_Q8_HEAD_F16: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16>;
+        case QWN_KV_CODEC_Q8_B64_F32: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32>;
+        case QWN_KV_CODEC_Q4_G32: return (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32>;
+        default: return nullptr;
+    }
+}
+
+cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
+    if (a.num_seqs == 0) return cudaSuccess;
+    AttnArgs A{};
+    A.pages = p->pages;
+    A.page_bytes = p->page_bytes;
+    A.tile_bytes = (uint32_t)p->tile_bytes;
+    A.tpp = p->tiles_per_page;
+    A.page_tokens = p->page_tokens;
+    A.page_table = p->page_table;
+    A.mp = p->max_pages_per_seq;
+    A.total_pages = p->total_pages;
+    A.max_seqs = p->max_seqs;
+    A.seq_lens = p->seq_lens;
+    A.seq_ids = a.seq_ids;
+    A.num_seqs = a.num_seqs;
+    A.kv_heads = p->kv_heads;
+    A.group = a.query_heads / p->kv_heads;
+    A.layer = a.layer;
+    A.attend_limit = a.attend_limit;
+    A.t_begin = a.t_begin;
+    A.t_end = a.t_end;
+    A.query = a.query;
+    A.output = a.output;
+    A.scale_log2 = a.scale * kLog2e;
+    A.partials = p->partials;
+    A.counters = p->counters;
+    A.tile_mass = a.page_mass ? p->tile_mass : nullptr;
+    A.seg_ml = a.page_mass ? p->seg_ml : nullptr;
+    A.part_m = a.part_m;
+    A.part_l = a.part_l;
+    A.part_o = a.part_o;
+    A.status = p->status;
+    switch (p->codec) {
+        case QWN_KV_CODEC_Q8_HEAD_F16: return launch_codec<QWN_KV_CODEC_Q8_HEAD_F16>(p, A, s);
+        case QWN_KV_CODEC_Q8_B64_F32: return launch_codec<QWN_KV_CODEC_Q8_B64_F32>(p, A, s);
+        case QWN_KV_CODEC_Q4_G32: return launch_codec<QWN_KV_CODEC_Q4_G32>(p, A, s);
+        default: return cudaErrorNotSupported;
+    }
+}
+
+cudaError_t launch_merge(uint32_t parts, uint32_t rows, const float *m, const float *l,
+                         const float *o, float *out, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    merge_kernel<<<rows, kHeadDim, 0, s>>>(parts, rows, m, l, o, out);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace qkv

@@ -1,0 +1,1034 @@
+// Paged quantized KV pool: lifecycle, page allocation, quantize-on-append,
+// synthetic prefill and the exported qwn_kv_* entry points.
+#include <cub/block/block_scan.cuh>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "kv_internal.cuh"
+
+namespace qkv {
+
+std::atomic<uint64_t> g_launches{0};
+static std::mutex g_err_mu;
+static std::string g_last_error;
+
+void set_error(const char *msg) {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    g_last_error = msg ? msg : "qwn_cuda error";
+}
+void set_cuda_error(const char *what, cudaError_t e) {
+    char buf[256];
+    std::snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
+    set_error(buf);
+}
+std::string last_error() {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    return g_last_error;
+}
+
+size_t attention_smem_bytes(uint32_t codec);
+const void *attention_kernel_ptr(uint32_t codec);
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// quantize-on-append: one warp stores one token-head; lane holds dims
+// 4*lane .. 4*lane+3 of K and of V.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float absmax4(float4 v) {
+    float m = 0.f;
+    if (isfinite(v.x)) m = fmaxf(m, fabsf(v.x));
+    if (isfinite(v.y)) m = fmaxf(m, fabsf(v.y));
+    if (isfinite(v.z)) m = fmaxf(m, fabsf(v.z));
+    if (isfinite(v.w)) m = fmaxf(m, fabsf(v.w));
+    return m;
+}
+// c/qwanto_turboquant.c:555-560
+__device__ __forceinline__ int q8_round(float x) {
+    if (!isfinite(x)) return 0;
+    if (x >= 127.f) return 127;
+    if (x <= -127.f) return -127;
+    return __float2int_rn(x);
+}
+__device__ __forceinline__ uint32_t q8_pack4(float4 v, float s) {
+    const uint32_t b0 = (uint32_t)(q8_round(__fdiv_rn(v.x, s)) + 128);
+    const uint32_t b1 = (uint32_t)(q8_round(__fdiv_rn(v.y, s)) + 128);
+    const uint32_t b2 = (uint32_t)(q8_round(__fdiv_rn(v.z, s)) + 128);
+    const uint32_t b3 = (uint32_t)(q8_round(__fdiv_rn(v.w, s)) + 128);
+    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+}
+__device__ __forceinline__ uint16_t head_scale16(float m) {
+    const float s = m > 0.f ? __fdiv_rn(m, 127.f) : 1.f;
+    uint16_t h = __half_as_ushort(__float2half_rn(s));
+    if ((h & 0x7FFFu) == 0) h = 0x0001u;
+    if ((h & 0x7FFFu) >= 0x7C00u) h = 0x7BFFu;
+    return h;
+}
+__device__ __forceinline__ uint32_t k8_lane_off(int t, int lane) {
+    const int n = 2 * (t >> 2) + (t & 1), h = (t >> 1) & 1;
+    return (uint32_t)(h * 1024 + (n * 4 + ((lane >> 2) & 3)) * 32 + (((lane >> 4) ^ (n & 1)) << 4) +
+                      4 * (lane & 3));
+}
+__device__ __forceinline__ void store_v8(uint8_t *tile, int t, int lane, uint32_t packed) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) tile[v8_off(t, 4 * lane + i)] = (uint8_t)(packed >> (8 * i));
+}
+
+// min / max with the reference's first-occurrence tie rule over `width`
+// lanes (4 values per lane, index 4*lane+i): c/qwanto_turboquant.c:171-177
+__device__ __forceinline__ void minmax_first(float4 v, int lane, int width, float &mn, float &mx) {
+    float a[4] = {v.x, v.y, v.z, v.w};
+    float lo = a[0], hi = a[0];
+    int ilo = 4 * lane, ihi = 4 * lane;
+#pragma unroll
+    for (int i = 1; i < 4; i++) {
+        if (a[i] < lo) { lo = a[i]; ilo = 4 * lane + i; }
+        if (a[i] > hi) { hi = a[i]; ihi = 4 * lane + i; }
+    }
+    for (int o = 1; o < width; o <<= 1) {
+        const float lo2 = __shfl_xor_sync(0xffffffffu, lo, o);
+        const int il2 = __shfl_xor_sync(0xffffffffu, ilo, o);
+        const float hi2 = __shfl_xor_sync(0xffffffffu, hi, o);
+        const int ih2 = __shfl_xor_sync(0xffffffffu, ihi, o);
+        if (lo2 < lo || (lo2 == lo && il2 < ilo)) { lo = lo2; ilo = il2; }
+        if (hi2 > hi || (hi2 == hi && ih2 < ihi)) { hi = hi2; ihi = ih2; }
+    }
+    mn = lo;
+    mx = hi;
+}
+// one TurboQuant-style code: c/qwanto_turboquant.c:188-206
+__device__ __forceinline__ uint32_t tq_code(float x, float mn, float inv, float levels) {
+    float norm = __fmul_rn(__fsub_rn(x, mn), inv);
+    if (norm < 0.f) norm = 0.f;
+    if (norm > 1.f) norm = 1.f;
+    int q = (int)roundf(__fmul_rn(norm, levels));
+    const int top = (int)levels;
+    if (q > top) q = top;
+    if (q < 0) q = 0;
+    return (uint32_t)q;
+}
+__device__ __forceinline__ void put_bits(uint8_t *tile, uint32_t byte, uint32_t shift_in_byte,
+                                         uint32_t mask, uint32_t val) {
+    uint32_t *word = reinterpret_cast<uint32_t *>(tile + (byte & ~3u));
+    const uint32_t sh = (byte & 3u) * 8u + shift_in_byte;
+    atomicAnd(word, ~(mask << sh));
+    atomicOr(word, (val & mask) << sh);
+}
+
+template <int CODEC>
+__device__ void store_token(uint8_t *tile, int t, float4 k, float4 v, int lane);
+
+template <>
+__device__ void store_token<QWN_KV_CODEC_Q8_HEAD_F16>(uint8_t *tile, int t, float4 k, float4 v, int lane) {
+    const uint16_t sk = head_scale16(warp_max(absmax4(k)));
+    const uint16_t sv = head_scale16(warp_max(absmax4(v)));
+    const float fk = h2f(sk), fv = h2f(sv);
+    *reinterpret_cast<uint32_t *>(tile + k8_lane_off(t, lane)) = q8_pack4(k, fk);
+    store_v8(tile, t, lane, q8_pack4(v, fv));
+    if (lane == 0) {
+        *reinterpret_cast<uint16_t *>(tile + 4096 + 2 * t) = sk;
+        *reinterpret_cast<uint16_t *>(tile + 4128 + 2 * t) = sv;
+    }
+}
+
+template <>
+__device__ void store_token<QWN_KV_CODEC_Q8_B64_F32>(uint8_t *tile, int t, float4 k, float4 v, int lane) {
+    float mk = absmax4(k), mv = absmax4(v);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {  // within each half-warp (64 channels)
+        mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+        mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, o));
+    }
+    const float sk = mk > 0.f ? __fdiv_rn(mk, 127.f) : 1.f;
+    const float sv = mv > 0.f ? __fdiv_rn(mv, 127.f) : 1.f;
+    *reinterpret_cast<uint32_t *>(tile + k8_lane_off(t, lane)) = q8_pack4(k, sk);
+    store_v8(tile, t, lane, q8_pack4(v, sv));
+    if ((lane & 15) == 0) {
+        const int x = lane >> 4;
+        *reinterpret_cast<float *>(tile + 4096 + 64 * x + 4 * t) = sk;
+        *reinterpret_cast<float *>(tile + 4224 + 64 * x + 4 * t) = sv;
+    }
+}
+
+template <>
+__device__ void store_token<QWN_KV_CODEC_Q4_G32>(uint8_t *tile, int t, float4 k, float4 v, int lane) {
+    // K
+    {
+        float mn, mx;
+        minmax_first(k, lane, 8, mn, mx);
+        const float range = __fsub_rn(mx, mn);
+        const float inv = range > 1e-8f ? __fdiv_rn(1.0f, range) : 0.f;
+        const uint32_t c0 = tq_code(k.x, mn, inv, 15.f), c1 = tq_code(k.y, mn, inv, 15.f);
+        const uint32_t c2 = tq_code(k.z, mn, inv, 15.f), c3 = tq_code(k.w, mn, inv, 15.f);
+        const int n = 2 * (t >> 2) + (t & 1), h = (t >> 1) & 1;
+        const int g = lane >> 3, e = (lane >> 2) & 1, tg = lane & 3;
+        uint8_t *base = tile + h * 512 + (n * 4 + tg) * 16 + g * 4;
+        base[e] = (uint8_t)(c0 | (c2 << 4));
+        base[2 + e] = (uint8_t)(c1 | (c3 << 4));
+        if ((lane & 7) == 0)
+            *reinterpret_cast<uint32_t *>(tile + 2048 + 64 * g + 4 * t) =
+                (uint32_t)tq_f32_to_f16(range) | ((uint32_t)tq_f32_to_f16(mn) << 16);
+    }
+    // V
+    {
+        float mn, mx;
+        minmax_first(v, lane, 8, mn, mx);
+        const float range = __fsub_rn(mx, mn);
+        const float inv = range > 1e-8f ? __fdiv_rn(1.0f, range) : 0.f;
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int d = 4 * lane + i;
+            const uint32_t code = tq_code(vv[i], mn, inv, 15.f);
+            const int gidd = d & 7, j = d >> 3, lv = gidd * 4 + (t >> 2), b = t & 3;
+            const int w = j >> 1, e = j & 1;
+            const int pos = (b & 1) * 4 + e * 2 + (b >> 1);
+            const int chunk = (w >> 2) ^ ((lv >> 2) & 1);
+            const uint32_t byte = 1024 + lv * 32 + chunk * 16 + (w & 3) * 4 + (pos >> 1);
+            put_bits(tile, byte, (pos & 1) * 4, 0xFu, code);
+        }
+        if ((lane & 7) == 0) {
+            const int g = lane >> 3;
+            *reinterpret_cast<uint32_t *>(tile + 2304 + 64 * g + 4 * t) =
+                (uint32_t)tq_f32_to_f16(range) | ((uint32_t)tq_f32_to_f16(mn) << 16);
+        }
+    }
+}
+
+// 3.5-bit reference TurboQuant codes in the tile layout (see qwn_oracle.c)
+__device__ void tq35_put(uint8_t *half, int is_value, int t, int d, uint32_t code) {
+    if (!is_value) {
+        const int h = (t >> 1) & 1, n = 2 * (t >> 2) + (t & 1);
+        const int x = d >> 6, tg = (d >> 4) & 3, k = d & 15;
+        const int slot = h * 32 + n * 4 + tg;
+        const int e = k >> 1, np = (e & 1) * 4 + (e >> 1);
+        if (!(k & 1)) {
+            put_bits(half, slot * 8 + x * 4 + (np >> 1), (np & 1) * 4, 0xFu, code);
+        } else {
+            const uint32_t byte = 512 + slot * 4 + (np >> 1), sh = (np & 1) * 4;
+            if (x == 0) {
+                put_bits(half, byte, sh, 0x7u, code);
+            } else {
+                put_bits(half, byte, sh + 3, 0x1u, code & 1u);
+                const uint32_t hb = 768 + slot * 2;  // 16-bit field, bits 2*np
+                put_bits(half, hb + ((2 * np) >> 3), (2 * np) & 7, 0x3u, code >> 1);
+            }
+        }
+    } else {
+        const int x = d >> 6, r = d & 63, par = r & 1, q = r >> 1, gidd = q & 7, jl = q >> 3;
+        const int lv = gidd * 4 + (t >> 2), b = t & 3;
+        if (!par) {
+            const int col = x * 4 + jl, np = (b & 1) * 4 + (col & 1) * 2 + (b >> 1);
+            put_bits(half, lv * 16 + (col >> 1) * 4 + (np >> 1), (np & 1) * 4, 0xFu, code);
+        } else {
+            const int npos = (b & 1) * 4 + (jl & 1) * 2 + (b >> 1);
+            const uint32_t byte = 512 + lv * 8 + (jl >> 1) * 4 + (npos >> 1), sh = (npos & 1) * 4;
+            if (x == 0) {
+                put_bits(half, byte, sh, 0x7u, code);
+            } else {
+                put_bits(half, byte, sh + 3, 0x1u, code & 1u);
+                const int bitpos = 2 * ((jl >> 1) * 8 + npos);
+                put_bits(half, 768 + lv * 4 + (bitpos >> 3), bitpos & 7, 0x3u, code >> 1);
+            }
+        }
+    }
+}
+
+template <>
+__device__ void store_token<QWN_KV_CODEC_TQ35_G64>(uint8_t *tile, int t, float4 k, float4 v, int lane) {
+#pragma unroll
+    for (int which = 0; which < 2; which++) {
+        const float4 x4 = which ? v : k;
+        uint8_t *half = tile + which * 1024;
+        float mn, mx;
+        minmax_first(x4, lane, 16, mn, mx);  // groups of 64 = 16 lanes
+        const float range = __fsub_rn(mx, mn);
+        const float inv = range > 1e-8f ? __fdiv_rn(1.0f, range) : 0.f;
+        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int d = 4 * lane + i;
+            const uint32_t code = tq_code(xv[i], mn, inv, (i & 1) ? 7.f : 15.f);
+            tq35_put(half, which, t, d, code);
+        }
+        if ((lane & 15) == 0) {
+            const int x = lane >> 4;
+            *reinterpret_cast<uint32_t *>(half + 896 + 64 * x + 4 * t) =
+                (uint32_t)tq_f32_to_f16(range) | ((uint32_t)tq_f32_to_f16(mn) << 16);
+        }
+    }
+}
+
+struct StoreGeo {
+    uint8_t *pages;
+    uint64_t page_bytes;
+    uint32_t tile_bytes, tpp, page_tokens, kv_heads, mp, total_pages, max_seqs;
+    const int32_t *page_table;
+    const int32_t *seq_lens;
+    uint32_t *status;
+};
+
+__device__ __forceinline__ uint8_t *tile_for(const StoreGeo &g, int32_t seq, uint32_t layer,
+                                             uint32_t head, int32_t pos) {
+    const uint32_t lp = (uint32_t)pos / g.page_tokens;
+    if (lp >= g.mp) { latch(g.status, QWN_KV_STATUS_TABLE_OVERFLOW); return nullptr; }
+    const int32_t pg = g.page_table[(size_t)seq * g.mp + lp];
+    if (pg < 0 || (uint32_t)pg >= g.total_pages) { latch(g.status, QWN_KV_STATUS_BAD_PAGE); return nullptr; }
+    const uint32_t tin = ((uint32_t)pos % g.page_tokens) / 16u;
+    return g.pages + (size_t)pg * g.page_bytes +
+           ((size_t)(layer * g.kv_heads + head) * g.tpp + tin) * g.tile_bytes;
+}
+
+// append the newest token (position len-1) of each sequence in the batch
+template <int CODEC>
+__global__ void append_kernel(StoreGeo g, uint32_t layer, uint32_t n, const int32_t *seq_ids,
+                              const float *key, const float *value) {
+    const uint32_t wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (wg >= n * g.kv_heads) return;
+    const uint32_t i = wg / g.kv_heads, h = wg % g.kv_heads;
+    const int32_t seq = seq_ids ? seq_ids[i] : (int32_t)i;
+    if (seq < 0 || (uint32_t)seq >= g.max_seqs) { if (lane == 0) latch(g.status, QWN_KV_STATUS_BAD_SEQUENCE); return; }
+    const int32_t pos = g.seq_lens[seq] - 1;
+    if (pos < 0) { if (lane == 0) latch(g.status, QWN_KV_STATUS_BAD_LENGTH); return; }
+    uint8_t *tile = tile_for(g, seq, layer, h, pos);
+    if (!tile) return;
+    const size_t row = ((size_t)i * g.kv_heads + h) * kHeadDim;
+    const float4 k = reinterpret_cast<const float4 *>(key + row)[lane];
+    const float4 v = reinterpret_cast<const float4 *>(value + row)[lane];
+    store_token<CODEC>(tile, pos & 15, k, v, lane);
+}
+
+// store tokens [first, first+n) of one sequence (key/value [n][HK][128])
+template <int CODEC>
+__global__ void store_tokens_kernel(StoreGeo g, int32_t seq, uint32_t layer, uint32_t first,
+                                    uint32_t n, const float *key, const float *value) {
+    const uint32_t wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (wg >= n * g.kv_heads) return;
+    const uint32_t tk = wg / g.kv_heads, h = wg % g.kv_heads;
+    const int32_t pos = (int32_t)(first + tk);
+    if (pos >= g.seq_lens[seq]) { if (lane == 0) latch(g.status, QWN_KV_STATUS_BAD_LENGTH); return; }
+    uint8_t *tile = tile_for(g, seq, layer, h, pos);
+    if (!tile) return;
+    const size_t row = ((size_t)tk * g.kv_heads + h) * kHeadDim;
+    const float4 k = reinterpret_cast<const float4 *>(key + row)[lane];
+    const float4 v = reinterpret_cast<const float4 *>(value + row)[lane];
+    store_token<CODEC>(tile, pos & 15, k, v, lane);
+}
+
+// synthetic prefill of one sequence: every (layer, position, head)
+template <int CODEC>
+__global__ void prefill_kernel(StoreGeo g, int32_t seq, uint32_t layers, uint32_t len, uint64_t seed,
+                               const uint8_t *mask) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t total = (uint64_t)layers * len * g.kv_heads;
+    const uint64_t nw = (uint64_t)gridDim.x * (blockDim.x >> 5);
+    const uint32_t width = g.kv_heads * kHeadDim;
+    for (uint64_t wg = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wg < total; wg += nw) {
+        const uint32_t h = (uint32_t)(wg % g.kv_heads);
+        const uint32_t pos = (uint32_t)((wg / g.kv_heads) % len);
+        const uint32_t layer = (uint32_t)(wg / ((uint64_t)g.kv_heads * len));
+        uint8_t *tile = tile_for(g, seq, layer, h, (int32_t)pos);
+        if (!tile) continue;
+        const uint64_t kk = gen_key(seed, 2, (uint32_t)seq, layer), kvv = gen_key(seed, 3, (uint32_t)seq, layer);
+        const uint64_t base = (uint64_t)pos * width + h * kHeadDim + 4 * lane;
+        float kx[4], vx[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            kx[i] = gen_normal(kk, base + i);
+            vx[i] = gen_normal(kvv, base + i);
+            if (mask && mask[(size_t)layer * width + h * kHeadDim + 4 * lane + i]) kx[i] *= 8.0f;
+        }
+        store_token<CODEC>(tile, (int)(pos & 15), make_float4(kx[0], kx[1], kx[2], kx[3]),
+                           make_float4(vx[0], vx[1], vx[2], vx[3]), lane);
+    }
+}
+
+__global__ void generate_kernel(float *out, uint32_t rows, uint32_t width, uint32_t kind, uint64_t seed,
+                                uint32_t layer, const int32_t *seq_ids, const int32_t *pos,
+                                const uint8_t *mask) {
+    const uint64_t total = (uint64_t)rows * width;
+    for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t r = (uint32_t)(e / width), c = (uint32_t)(e % width);
+        const uint32_t seq = seq_ids ? (uint32_t)seq_ids[r] : r;
+        const uint64_t key = gen_key(seed, kind, seq, layer);
+        float x = gen_normal(key, (uint64_t)pos[r] * width + c);
+        if (mask && mask[c]) x *= 8.0f;
+        out[e] = x;
+    }
+}
+
+// qwn_block_table_append_token for every sequence of the batch, in order:
+// pages popped from the top of the LIFO free stack (c/qwn_paged_kv.c:95-138)
+__global__ void __launch_bounds__(1024) seq_append_kernel(uint32_t n, const int32_t *seq_ids,
+                                                          const int32_t *counts, int32_t *lens,
+                                                          int32_t *npages, int32_t *table, float *scores,
+                                                          const int32_t *free_stack, int32_t *free_top,
+                                                          uint32_t P, uint32_t mp, uint32_t max_seqs,
+                                                          uint32_t *status) {
+    using Scan = cub::BlockScan<int, 1024>;
+    __shared__ typename Scan::TempStorage tmp;
+    __shared__ int s_total, s_bad;
+    if (threadIdx.x == 0) { s_total = 0; s_bad = 0; }
+    __syncthreads();
+    for (uint32_t base = 0; base < n; base += 1024) {
+        const uint32_t i = base + threadIdx.x;
+        int need = 0;
+        if (i < n) {
+            const int32_t seq = seq_ids ? seq_ids[i] : (int32_t)i;
+            if (seq < 0 || (uint32_t)seq >= max_seqs) {
+                atomicOr(&s_bad, (int)QWN_KV_STATUS_BAD_SEQUENCE);
+            } else {
+                const int32_t cnt = counts ? counts[i] : 1;
+                const int32_t np_new = (lens[seq] + cnt + (int32_t)P - 1) / (int32_t)P;
+                if (cnt < 0 || np_new > (int32_t)mp) atomicOr(&s_bad, (int)QWN_KV_STATUS_TABLE_OVERFLOW);
+                need = max(0, np_new - npages[seq]);
+            }
+        }
+        int off0, agg;
+        Scan(tmp).ExclusiveSum(need, off0, agg);
+        __syncthreads();
+        if (threadIdx.x == 0) s_total += agg;
+        __syncthreads();
+    }
+    const int32_t top = *free_top;
+    if (s_bad || s_total > top) {
+        if (threadIdx.x == 0) latch(status, s_bad ? (uint32_t)s_bad : QWN_KV_STATUS_POOL_EXHAUSTED);
+        return;
+    }
+    int carry = 0;
+    for (uint32_t base = 0; base < n; base += 1024) {
+        const uint32_t i = base + threadIdx.x;
+        int need = 0, seq = 0, cnt = 0, np = 0;
+        if (i < n) {
+            seq = seq_ids ? seq_ids[i] : (int32_t)i;
+            cnt = counts ? counts[i] : 1;
+            np = npages[seq];
+            need = max(0, (lens[seq] + cnt + (int32_t)P - 1) / (int32_t)P - np);
+        }
+        int off, agg;
+        Scan(tmp).ExclusiveSum(need, off, agg);
+        if (i < n) {
+            for (int k = 0; k < need; k++) {
+                table[(size_t)seq * mp + np + k] = free_stack[top - 1 - (carry + off + k)];
+                scores[(size_t)seq * mp + np + k] = 1.0f;
+            }
+            npages[seq] = np + need;
+            lens[seq] += cnt;
+        }
+        carry += agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *free_top = top - carry;
+}
+
+__global__ void fill_i32(int32_t *p, int32_t v, size_t n) {
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x)
+        p[e] = v;
+}
+__global__ void iota_i32(int32_t *p, size_t n) {
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x)
+        p[e] = (int32_t)e;
+}
+
+StoreGeo store_geo(Pool *p) {
+    StoreGeo g;
+    g.pages = p->pages;
+    g.page_bytes = p->page_bytes;
+    g.tile_bytes = (uint32_t)p->tile_bytes;
+    g.tpp = p->tiles_per_page;
+    g.page_tokens = p->page_tokens;
+    g.kv_heads = p->kv_heads;
+    g.mp = p->max_pages_per_seq;
+    g.total_pages = p->total_pages;
+    g.max_seqs = p->max_seqs;
+    g.page_table = p->page_table;
+    g.seq_lens = p->seq_lens;
+    g.status = p->status;
+    return g;
+}
+
+template <template <int> class K, class... Args>
+cudaError_t dispatch_store(uint32_t codec, dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+    switch (codec) {
+        case QWN_KV_CODEC_Q8_HEAD_F16: K<QWN_KV_CODEC_Q8_HEAD_F16>::launch(grid, block, s, args...); break;
+        case QWN_KV_CODEC_Q8_B64_F32: K<QWN_KV_CODEC_Q8_B64_F32>::launch(grid, block, s, args...); break;
+        case QWN_KV_CODEC_TQ35_G64: K<QWN_KV_CODEC_TQ35_G64>::launch(grid, block, s, args...); break;
+        case QWN_KV_CODEC_Q4_G32: K<QWN_KV_CODEC_Q4_G32>::launch(grid, block, s, args...); break;
+        default: return cudaErrorNotSupported;
+    }
+    count_launch();
+    return cudaGetLastError();
+}
+template <int C> struct AppendL {
+    template <class... A> static void launch(dim3 g, dim3 b, cudaStream_t s, A... a) {
+        append_kernel<C><<<g, b, 0, s>>>(a...);
+    }
+};
+template <int C> struct StoreL {
+    template <class... A> static void launch(dim3 g, dim3 b, cudaStream_t s, A... a) {
+        store_tokens_kernel<C><<<g, b, 0, s>>>(a...);
+    }
+};
+template <int C> struct PrefillL {
+    template <class... A> static void launch(dim3 g, dim3 b, cudaStream_t s, A... a) {
+        prefill_kernel<C><<<g, b, 0, s>>>(a...);
+    }
+};
+
+}  // namespace
+
+cudaError_t launch_seq_append(Pool *p, uint32_t n, const int32_t *seq_ids, const int32_t *counts,
+                              cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    seq_append_kernel<<<1, 1024, 0, s>>>(n, seq_ids, counts, p->seq_lens, p->seq_pages, p->page_table,
+                                         p->page_scores, p->free_stack, p->free_top, p->page_tokens,
+                                         p->max_pages_per_seq, p->max_seqs, p->status);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_append(Pool *p, uint32_t layer, uint32_t n, const int32_t *seq_ids, const float *key,
+                          const float *value, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    const uint32_t warps = n * p->kv_heads;
+    return dispatch_store<AppendL>(p->codec, dim3((warps + 3) / 4), dim3(128), s, store_geo(p), layer, n,
+                                   seq_ids, key, value);
+}
+
+cudaError_t launch_store_tokens(Pool *p, int32_t seq, uint32_t layer, uint32_t first, uint32_t n,
+                                const float *key, const float *value, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    const uint32_t warps = n * p->kv_heads;
+    return dispatch_store<StoreL>(p->codec, dim3((warps + 3) / 4), dim3(128), s, store_geo(p), seq, layer,
+                                  first, n, key, value);
+}
+
+cudaError_t launch_generate(float *out, uint32_t rows, uint32_t width, uint32_t kind, uint64_t seed,
+                            uint32_t layer, const int32_t *seq_ids, const int32_t *pos, const uint8_t *mask,
+                            cudaStream_t s) {
+    const uint64_t total = (uint64_t)rows * width;
+    if (total == 0) return cudaSuccess;
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((total + 255) / 256, 148u * 16u);
+    generate_kernel<<<blocks, 256, 0, s>>>(out, rows, width, kind, seed, layer, seq_ids, pos, mask);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pool_init_state(Pool *p, cudaStream_t s) {
+    cudaError_t e;
+    if ((e = cudaMemsetAsync(p->page_table, 0xFF, sizeof(int32_t) * (size_t)p->max_seqs * p->max_pages_per_seq, s)))
+        return e;
+    if ((e = cudaMemsetAsync(p->seq_lens, 0, sizeof(int32_t) * p->max_seqs, s))) return e;
+    if ((e = cudaMemsetAsync(p->seq_pages, 0, sizeof(int32_t) * p->max_seqs, s))) return e;
+    if ((e = cudaMemsetAsync(p->page_scores, 0, sizeof(float) * (size_t)p->max_seqs * p->max_pages_per_seq, s)))
+        return e;
+    if ((e = cudaMemsetAsync(p->status, 0, sizeof(uint32_t), s))) return e;
+    if ((e = cudaMemsetAsync(p->counters, 0, sizeof(uint32_t) * p->max_segments, s))) return e;
+    // free stack: total-1-i, optionally permuted (Fisher-Yates on the host)
+    std::vector<int32_t> stack(p->total_pages);
+    for (uint32_t i = 0; i < p->total_pages; i++) stack[i] = (int32_t)(p->total_pages - 1 - i);
+    if (p->perm_seed) {
+        auto mix = [](uint64_t x) {
+            uint64_t z = x + 0x9E3779B97F4A7C15ull;
+            z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+            z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+            return z ^ (z >> 31);
+        };
+        const uint64_t key = mix(p->perm_seed ^ 0x5045524Dull);
+        for (int64_t i = (int64_t)p->total_pages - 1; i > 0; i--) {
+            const uint64_t j = mix(key + (uint64_t)i) % (uint64_t)(i + 1);
+            std::swap(stack[(size_t)i], stack[(size_t)j]);
+        }
+    }
+    if ((e = cudaMemcpyAsync(p->free_stack, stack.data(), sizeof(int32_t) * stack.size(),
+                             cudaMemcpyHostToDevice, s)))
+        return e;
+    const int32_t top = (int32_t)p->total_pages;
+    if ((e = cudaMemcpyAsync(p->free_top, &top, sizeof(int32_t), cudaMemcpyHostToDevice, s))) return e;
+    return cudaStreamSynchronize(s);  // the host vectors above go out of scope
+}
+
+}  // namespace qkv
+
+using namespace qkv;
+
+// ===========================================================================
+// exported entry points
+// ===========================================================================
+extern "C" {
+
+QWN_CUDA_ABI_API uint64_t qwn_kv_launch_count(void) { return g_launches.load(); }
+
+QWN_CUDA_ABI_API int qwn_kv_memcpy_d2h(void *host, const void *dev, uint64_t bytes) {
+    cudaError_t e = cudaMemcpy(host, dev, bytes, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_memcpy_d2h", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+QWN_CUDA_ABI_API int qwn_kv_memcpy_h2d(void *dev, const void *host, uint64_t bytes) {
+    cudaError_t e = cudaMemcpy(dev, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_memcpy_h2d", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+static void pool_release(Pool *p) {
+    cudaSetDevice(p->device);
+    cudaFree(p->pages); cudaFree(p->page_table); cudaFree(p->seq_lens); cudaFree(p->seq_pages);
+    cudaFree(p->free_stack); cudaFree(p->free_top); cudaFree(p->page_scores); cudaFree(p->status);
+    cudaFree(p->partials); cudaFree(p->counters); cudaFree(p->tile_mass); cudaFree(p->seg_ml);
+    cudaFree(p->evict_dead); cudaFree(p->evict_count); cudaFree(p->ident);
+    cudaFree(p->stage_q); cudaFree(p->stage_k); cudaFree(p->stage_v); cudaFree(p->stage_o);
+    for (uint32_t i = 0; i < p->layer_events; i++) {
+        cudaEventDestroy(p->layer_in_ev[i]);
+        cudaEventDestroy(p->layer_out_ev[i]);
+    }
+    delete[] p->layer_in_ev;
+    delete[] p->layer_out_ev;
+    if (p->stream) cudaStreamDestroy(p->stream);
+    if (p->copy_stream) cudaStreamDestroy(p->copy_stream);
+    delete p;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_pool_create(const QwnKvPoolOptions *o, QwnKvPoolHandle *out) {
+    if (!o || !out || !header_ok(o->header, sizeof(*o)) || !header_ok(out->header, sizeof(*out))) {
+        set_error("qwn_kv_pool_create: bad header");
+        return QWN_CUDA_STATUS_ABI_MISMATCH;
+    }
+    const size_t tb = tile_bytes_of(o->codec);
+    if (!tb || o->head_dim != (uint32_t)kHeadDim || o->layers == 0 || o->kv_heads == 0 ||
+        o->page_tokens == 0 || o->page_tokens % 16 || o->total_pages == 0 || o->max_seqs == 0 ||
+        o->max_pages_per_seq == 0) {
+        set_error("qwn_kv_pool_create: unsupported geometry (head_dim must be 128, page_tokens a multiple of 16)");
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    const uint32_t mq = o->max_query_heads ? o->max_query_heads : o->kv_heads * kMaxGroup;
+    if (mq % o->kv_heads || mq / o->kv_heads > (uint32_t)kMaxGroup) {
+        set_error("qwn_kv_pool_create: query heads must be a multiple of kv_heads, at most 8 per kv head");
+        return QWN_CUDA_STATUS_UNSUPPORTED;
+    }
+    if (cudaSetDevice(o->device_id) != cudaSuccess) {
+        set_cuda_error("cudaSetDevice", cudaGetLastError());
+        return QWN_CUDA_STATUS_UNAVAILABLE;
+    }
+    Pool *p = new (std::nothrow) Pool();
+    if (!p) return QWN_CUDA_STATUS_OUT_OF_MEMORY;
+    p->device = o->device_id;
+    p->codec = o->codec;
+    p->layers = o->layers;
+    p->kv_heads = o->kv_heads;
+    p->page_tokens = o->page_tokens;
+    p->tiles_per_page = o->page_tokens / 16;
+    p->total_pages = o->total_pages;
+    p->max_seqs = o->max_seqs;
+    p->max_pages_per_seq = o->max_pages_per_seq;
+    p->max_query_heads = mq;
+    p->perm_seed = o->permutation_seed;
+    p->tile_bytes = tb;
+    p->page_bytes = tb * p->tiles_per_page * (size_t)o->layers * o->kv_heads;
+    p->pool_bytes = p->page_bytes * (size_t)o->total_pages;
+
+    // persistent attention grid: resident CTAs x SMs
+    int sms = 0, per_sm = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
+    const void *kern = attention_kernel_ptr(p->codec);
+    const size_t smem = attention_smem_bytes(p->codec);
+    if (kern) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarpsPerCta * 32, smem);
+    }
+    if (per_sm < 1) per_sm = 1;
+    p->attn_ctas = (uint32_t)(sms > 0 ? sms : 148) * (uint32_t)per_sm;
+    p->attn_warps = p->attn_ctas * kWarpsPerCta;
+    p->max_segments = (uint64_t)o->max_seqs * o->kv_heads;
+    p->max_units = (uint64_t)o->max_seqs * o->max_pages_per_seq * p->tiles_per_page * o->kv_heads;
+    const size_t part_bytes = ((size_t)p->attn_warps + p->max_segments) * kPartialFloats * sizeof(float);
+    const size_t mass_bytes = (size_t)p->max_units * kMaxGroup * sizeof(float2);
+    const size_t segml_bytes = (size_t)p->max_segments * kMaxGroup * sizeof(float2);
+    const size_t table_elems = (size_t)o->max_seqs * o->max_pages_per_seq;
+    p->scratch_bytes = part_bytes + mass_bytes + segml_bytes + p->max_segments * sizeof(uint32_t) + table_elems;
+
+    size_t free_b = 0, total_b = 0;
+    cudaMemGetInfo(&free_b, &total_b);
+    const uint64_t need = p->pool_bytes + p->scratch_bytes + table_elems * 8 + (size_t)o->total_pages * 4;
+    if ((o->memory_budget_bytes && need > o->memory_budget_bytes) || need > free_b) {
+        delete p;
+        set_error("qwn_kv_pool_create: pool does not fit the memory budget / free device memory");
+        return QWN_CUDA_STATUS_OUT_OF_MEMORY;
+    }
+    bool ok = cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&p->copy_stream, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaMalloc(&p->pages, p->pool_bytes) == cudaSuccess &&
+              cudaMalloc(&p->page_table, sizeof(int32_t) * table_elems) == cudaSuccess &&
+              cudaMalloc(&p->seq_lens, sizeof(int32_t) * o->max_seqs) == cudaSuccess &&
+              cudaMalloc(&p->seq_pages, sizeof(int32_t) * o->max_seqs) == cudaSuccess &&
+              cudaMalloc(&p->free_stack, sizeof(int32_t) * o->total_pages) == cudaSuccess &&
+              cudaMalloc(&p->free_top, sizeof(int32_t)) == cudaSuccess &&
+              cudaMalloc(&p->page_scores, sizeof(float) * table_elems) == cudaSuccess &&
+              cudaMalloc(&p->status, sizeof(uint32_t)) == cudaSuccess &&
+              cudaMalloc(&p->partials, part_bytes) == cudaSuccess &&
+              cudaMalloc(&p->counters, sizeof(uint32_t) * p->max_segments) == cudaSuccess &&
+              cudaMalloc(&p->tile_mass, mass_bytes) == cudaSuccess &&
+              cudaMalloc(&p->seg_ml, segml_bytes) == cudaSuccess &&
+              cudaMalloc(&p->evict_dead, table_elems) == cudaSuccess &&
+              cudaMalloc(&p->evict_count, sizeof(int32_t) * o->max_seqs) == cudaSuccess &&
+              cudaMalloc(&p->ident, sizeof(int32_t) * o->max_seqs) == cudaSuccess;
+    if (!ok) {
+        set_cuda_error("qwn_kv_pool_create: allocation", cudaGetLastError());
+        pool_release(p);
+        return QWN_CUDA_STATUS_OUT_OF_MEMORY;
+    }
+    cudaMemsetAsync(p->pages, 0, p->pool_bytes, p->stream);
+    iota_i32<<<(o->max_seqs + 255) / 256, 256, 0, p->stream>>>(p->ident, o->max_seqs);
+    count_launch();
+    cudaError_t e = launch_pool_init_state(p, p->stream);
+    if (e != cudaSuccess) {
+        set_cuda_error("qwn_kv_pool_create: init", e);
+        pool_release(p);
+        return QWN_CUDA_STATUS_RUNTIME_ERROR;
+    }
+    std::memset(out, 0, sizeof(*out));
+    qwn_cuda_abi_header_init(&out->header, sizeof(*out));
+    out->opaque = p;
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_pool_destroy(QwnKvPoolHandle *h) {
+    Pool *p = pool_from(h);
+    if (!p) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(p->device);
+    cudaDeviceSynchronize();
+    pool_release(p);
+    h->opaque = nullptr;
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_pool_get_info(const QwnKvPoolHandle *h, QwnKvPoolInfo *info) {
+    Pool *p = pool_from(h);
+    if (!p || !info || !header_ok(info->header, sizeof(*info))) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    std::memset(info, 0, sizeof(*info));
+    qwn_cuda_abi_header_init(&info->header, sizeof(*info));
+    info->pages_dev = p->pages;
+    info->page_table_dev = p->page_table;
+    info->seq_lens_dev = p->seq_lens;
+    info->seq_pages_dev = p->seq_pages;
+    info->free_stack_dev = p->free_stack;
+    info->free_top_dev = p->free_top;
+    info->page_scores_dev = p->page_scores;
+    info->status_dev = p->status;
+    info->tile_bytes = p->tile_bytes;
+    info->page_bytes = p->page_bytes;
+    info->pool_bytes = p->pool_bytes;
+    info->scratch_bytes = p->scratch_bytes;
+    info->attention_ctas = p->attn_ctas;
+    info->attention_warps = p->attn_warps;
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_pool_reset(QwnKvPoolHandle *h) {
+    Pool *p = pool_from(h);
+    if (!p) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> lk(p->mu);
+    cudaSetDevice(p->device);
+    cudaError_t e = launch_pool_init_state(p, p->stream);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_pool_reset", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_pool_check(QwnKvPoolHandle *h, uint32_t *bits) {
+    Pool *p = pool_from(h);
+    if (!p || !bits) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(p->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_pool_check", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    uint32_t st = 0;
+    cudaMemcpy(&st, p->status, sizeof(st), cudaMemcpyDeviceToHost);
+    cudaMemset(p->status, 0, sizeof(uint32_t));
+    if (st & QWN_KV_STATUS_WAIT_TIMEOUT)  // an abandoned merge leaves counters behind
+        cudaMemset(p->counters, 0, sizeof(uint32_t) * p->max_segments);
+    *bits = st;
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_seq_append(QwnKvPoolHandle *h, uint32_t n, const int32_t *seq_ids,
+                                       const int32_t *counts, void *stream) {
+    Pool *p = pool_from(h);
+    if (!p || n > p->max_seqs) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(p->device);
+    cudaError_t e = launch_seq_append(p, n, seq_ids, counts, stream_of(p, stream));
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_seq_append", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+static int decode_impl(Pool *p, const QwnKvDecodeRequest *r, cudaStream_t s) {
+    if (r->layer >= p->layers || r->num_seqs > p->max_seqs || !r->query_dev || !r->output_dev ||
+        r->query_heads == 0 || r->query_heads % p->kv_heads || r->query_heads > p->max_query_heads ||
+        ((r->key_dev == nullptr) != (r->value_dev == nullptr))) {
+        set_error("qwn_kv_decode: invalid request");
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if (p->codec == QWN_KV_CODEC_TQ35_G64 && !attention_kernel_ptr(p->codec)) {
+        set_error("qwn_kv_decode: codec has no attention kernel in this build");
+        return QWN_CUDA_STATUS_UNSUPPORTED;
+    }
+    cudaError_t e = cudaSuccess;
+    if (r->key_dev) e = launch_append(p, r->layer, r->num_seqs, r->seq_ids_dev, r->key_dev, r->value_dev, s);
+    if (e == cudaSuccess) {
+        AttnLaunch a{};
+        a.layer = r->layer;
+        a.num_seqs = r->num_seqs;
+        a.query_heads = r->query_heads;
+        a.attend_limit = r->attend_limit;
+        a.seq_ids = r->seq_ids_dev;
+        a.query = r->query_dev;
+        a.output = r->output_dev;
+        a.scale = r->scale > 0.f ? r->scale : 1.0f / std::sqrt((float)kHeadDim);
+        a.page_mass = r->page_mass_dev;
+        e = launch_attention(p, a, s);
+    }
+    if (e == cudaSuccess && r->page_mass_dev) {
+        e = launch_page_mass(p, r->num_seqs, r->seq_ids_dev, r->query_heads, r->page_mass_dev, s);
+    }
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_decode", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_decode(QwnKvPoolHandle *h, const QwnKvDecodeRequest *r) {
+    Pool *p = pool_from(h);
+    if (!p || !r || !header_ok(r->header, sizeof(*r))) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(p->device);
+    return decode_impl(p, r, stream_of(p, r->stream));
+}
+
+QWN_CUDA_ABI_API int qwn_kv_append(QwnKvPoolHandle *h, uint32_t layer, uint32_t n, const int32_t *seq_ids,
+                                   const float *key, const float *value, void *stream) {
+    Pool *p = pool_from(h);
+    if (!p || layer >= p->layers || n > p->max_seqs || !key || !value) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(p->device);
+    cudaError_t e = launch_append(p, layer, n, seq_ids, key, value, stream_of(p, stream));
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_append", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_partial(QwnKvPoolHandle *h, const QwnKvPartialRequest *r) {
+    Pool *p = pool_from(h);
+    if (!p || !r || !header_ok(r->header, sizeof(*r)) || r->layer >= p->layers || !r->query_dev ||
+        !r->m_dev || !r->l_dev || !r->o_dev || r->query_heads % p->kv_heads ||
+        r->query_heads > p->max_query_heads || r->num_seqs > p->max_seqs) {
+        set_error("qwn_kv_partial: invalid request");
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    cudaSetDevice(p->device);
+    AttnLaunch a{};
+    a.layer = r->layer;
+    a.num_seqs = r->num_seqs;
+    a.query_heads = r->query_heads;
+    a.seq_ids = r->seq_ids_dev;
+    a.query = r->query_dev;
+    a.scale = r->scale > 0.f ? r->scale : 1.0f / std::sqrt((float)kHeadDim);
+    a.part_m = r->m_dev;
+    a.part_l = r->l_dev;
+    a.part_o = r->o_dev;
+    a.t_begin = r->t_begin;
+    a.t_end = r->t_end;
+    cudaStream_t s = stream_of(p, r->stream);
+    // rows whose range is empty are never visited by a warp: mark them empty
+    cudaError_t e = cudaMemsetAsync(r->l_dev, 0, sizeof(float) * r->num_seqs * r->query_heads, s);
+    if (e == cudaSuccess) {
+        e = launch_fill_f32(r->m_dev, -INFINITY, (size_t)r->num_seqs * r->query_heads, s);
+    }
+    if (e == cudaSuccess) e = launch_attention(p, a, s);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_partial", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_merge_partials(uint32_t parts, uint32_t rows, const float *m, const float *l,
+                                           const float *o, float *out, void *stream) {
+    if (!m || !l || !o || !out || parts == 0) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaError_t e = launch_merge(parts, rows, m, l, o, out, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_merge_partials", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_store_tokens(QwnKvPoolHandle *h, int32_t seq, uint32_t layer, uint32_t first,
+                                         uint32_t n, const float *key, const float *value, void *stream) {
+    Pool *p = pool_from(h);
+    if (!p || seq < 0 || (uint32_t)seq >= p->max_seqs || layer >= p->layers || !key || !value)
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(p->device);
+    cudaError_t e = launch_store_tokens(p, seq, layer, first, n, key, value, stream_of(p, stream));
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_store_tokens", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_generate_rows(float *out, uint32_t rows, uint32_t width, uint32_t kind,
+                                          uint64_t seed, uint32_t layer, const int32_t *seq_ids,
+                                          const int32_t *pos, const uint8_t *mask, void *stream) {
+    if (!out || !pos) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaError_t e = launch_generate(out, rows, width, kind, seed, layer, seq_ids, pos, mask,
+                                    static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_generate_rows", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_prefill_synthetic(QwnKvPoolHandle *h, uint32_t n, const int32_t *host_seq_ids,
+                                              const int32_t *host_lens, uint64_t seed,
+                                              const uint8_t *mask_host, void *stream) {
+    Pool *p = pool_from(h);
+    if (!p || !host_seq_ids || !host_lens || n > p->max_seqs) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(p->device);
+    cudaStream_t s = stream_of(p, stream);
+    int32_t *d_ids = nullptr, *d_cnt = nullptr;
+    uint8_t *d_mask = nullptr;
+    const size_t mask_bytes = (size_t)p->layers * p->kv_heads * kHeadDim;
+    cudaError_t e = cudaMalloc(&d_ids, sizeof(int32_t) * n);
+    if (e == cudaSuccess) e = cudaMalloc(&d_cnt, sizeof(int32_t) * n);
+    if (e == cudaSuccess && mask_host) e = cudaMalloc(&d_mask, mask_bytes);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_ids, host_seq_ids, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_cnt, host_lens, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && mask_host) e = cudaMemcpyAsync(d_mask, mask_host, mask_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = launch_seq_append(p, n, d_ids, d_cnt, s);
+    for (uint32_t i = 0; e == cudaSuccess && i < n; i++) {
+        if (host_lens[i] <= 0) continue;
+        const uint64_t warps = (uint64_t)p->layers * (uint64_t)host_lens[i] * p->kv_heads;
+        const uint32_t blocks = (uint32_t)std::min<uint64_t>((warps + 3) / 4, 148ull * 32ull);
+        e = dispatch_store<PrefillL>(p->codec, dim3(blocks), dim3(128), s, store_geo(p), host_seq_ids[i],
+                                     p->layers, (uint32_t)host_lens[i], seed, (const uint8_t *)d_mask);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(d_ids);
+    cudaFree(d_cnt);
+    cudaFree(d_mask);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_prefill_synthetic", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_evict(QwnKvPoolHandle *h, const QwnKvEvictRequest *r) {
+    Pool *p = pool_from(h);
+    if (!p || !r || !header_ok(r->header, sizeof(*r)) || !r->page_mass_dev || !r->flags_dev ||
+        r->num_seqs > p->max_seqs)
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(p->device);
+    cudaError_t e = launch_evict(p, r->num_seqs, r->seq_ids_dev, r->page_mass_dev, r->flags_dev,
+                                 r->token_budget, stream_of(p, r->stream));
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_evict", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_decode_step_host(QwnKvPoolHandle *h, const QwnKvHostStepRequest *r,
+                                             QwnCudaTelemetry *tel) {
+    Pool *p = pool_from(h);
+    if (!p || !r || !header_ok(r->header, sizeof(*r)) || !r->host_query || !r->host_key || !r->host_value ||
+        !r->host_output || r->num_layers == 0 || r->num_layers > p->layers || r->num_seqs == 0 ||
+        r->num_seqs > p->max_seqs || r->query_heads % p->kv_heads || r->query_heads > p->max_query_heads) {
+        set_error("qwn_kv_decode_step_host: invalid request");
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    std::lock_guard<std::mutex> lk(p->mu);
+    cudaSetDevice(p->device);
+    const size_t q_el = (size_t)r->num_seqs * r->query_heads * kHeadDim;
+    const size_t kv_el = (size_t)r->num_seqs * p->kv_heads * kHeadDim;
+    const size_t lq = q_el * r->num_layers, lkv = kv_el * r->num_layers;
+    cudaError_t e = cudaSuccess;
+    if (lq > p->stage_q_elems || lkv > p->stage_kv_elems) {
+        cudaFree(p->stage_q); cudaFree(p->stage_k); cudaFree(p->stage_v); cudaFree(p->stage_o);
+        p->stage_q = p->stage_k = p->stage_v = p->stage_o = nullptr;
+        p->stage_q_elems = p->stage_kv_elems = 0;
+        if ((e = cudaMalloc(&p->stage_q, lq * 4)) || (e = cudaMalloc(&p->stage_o, lq * 4)) ||
+            (e = cudaMalloc(&p->stage_k, lkv * 4)) || (e = cudaMalloc(&p->stage_v, lkv * 4))) {
+            set_cuda_error("qwn_kv_decode_step_host: staging", e);
+            return QWN_CUDA_STATUS_OUT_OF_MEMORY;
+        }
+        p->stage_q_elems = lq;
+        p->stage_kv_elems = lkv;
+    }
+    if (r->num_layers > p->layer_events) {
+        for (uint32_t i = 0; i < p->layer_events; i++) {
+            cudaEventDestroy(p->layer_in_ev[i]);
+            cudaEventDestroy(p->layer_out_ev[i]);
+        }
+        delete[] p->layer_in_ev;
+        delete[] p->layer_out_ev;
+        p->layer_in_ev = new cudaEvent_t[r->num_layers];
+        p->layer_out_ev = new cudaEvent_t[r->num_layers];
+        for (uint32_t i = 0; i < r->num_layers; i++) {
+            cudaEventCreateWithFlags(&p->layer_in_ev[i], cudaEventDisableTiming);
+            cudaEventCreateWithFlags(&p->layer_out_ev[i], cudaEventDisableTiming);
+        }
+        p->layer_events = r->num_layers;
+    }
+    cudaEvent_t t0, t1;
+    cudaEventCreate(&t0);
+    cudaEventCreate(&t1);
+    cudaEventRecord(t0, p->stream);
+    // per-layer inputs on the copy stream, compute waits per layer, outputs back per layer
+    for (uint32_t L = 0; L < r->num_layers && e == cudaSuccess; L++) {
+        e = cudaMemcpyAsync(p->stage_q + L * q_el, r->host_query + L * q_el, q_el * 4, cudaMemcpyHostToDevice,
+                            p->copy_stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(p->stage_k + L * kv_el, r->host_key + L * kv_el, kv_el * 4,
+                                cudaMemcpyHostToDevice, p->copy_stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(p->stage_v + L * kv_el, r->host_value + L * kv_el, kv_el * 4,
+                                cudaMemcpyHostToDevice, p->copy_stream);
+        if (e == cudaSuccess) e = cudaEventRecord(p->layer_in_ev[L], p->copy_stream);
+    }
+    if (e == cudaSuccess) e = launch_seq_append(p, r->num_seqs, nullptr, nullptr, p->stream);
+    for (uint32_t L = 0; L < r->num_layers && e == cudaSuccess; L++) {
+        e = cudaStreamWaitEvent(p->stream, p->layer_in_ev[L], 0);
+        QwnKvDecodeRequest d{};
+        qwn_cuda_abi_header_init(&d.header, sizeof(d));
+        d.layer = L;
+        d.num_seqs = r->num_seqs;
+        d.query_heads = r->query_heads;
+        d.scale = r->scale;
+        d.query_dev = p->stage_q + L * q_el;
+        d.key_dev = p->stage_k + L * kv_el;
+        d.value_dev = p->stage_v + L * kv_el;
+        d.output_dev = p->stage_o + L * q_el;
+        if (e == cudaSuccess && decode_impl(p, &d, p->stream) != QWN_CUDA_STATUS_OK) e = cudaErrorLaunchFailure;
+        if (e == cudaSuccess) e = cudaEventRecord(p->layer_out_ev[L], p->stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->copy_stream, p->layer_out_ev[L], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(r->host_output + L * q_el, p->stage_o + L * q_el, q_el * 4,
+                                cudaMemcpyDeviceToHost, p->copy_stream);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(p->copy_stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(p->stream);
+    cudaEventRecord(t1, p->stream);
+    cudaEventSynchronize(t1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, t0, t1);
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_decode_step_host", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    uint32_t st = 0;
+    cudaMemcpy(&st, p->status, sizeof(st), cudaMemcpyDeviceToHost);
+    if (tel && header_ok(tel->header, sizeof(*tel))) {
+        tel->kv_cache_kernel_count += 1 + 2ull * r->num_layers;
+        tel->kv_cache_upload_bytes += (uint64_t)(lq + 2 * lkv) * 4;
+        tel->kv_cache_kernel_ms += ms;
+        std::snprintf(tel->kv_cache_kernel_type, sizeof(tel->kv_cache_kernel_type), "paged-b200-split-kv");
+    }
+    if (st & QWN_KV_STATUS_POOL_EXHAUSTED) {
+        set_error("paged KV pool exhausted");
+        return QWN_CUDA_STATUS_OUT_OF_MEMORY;
+    }
+    if (st) {
+        set_error("device status latched an error (see qwn_kv_pool_check)");
+        return QWN_CUDA_STATUS_RUNTIME_ERROR;
+    }
+    return QWN_CUDA_STATUS_OK;
+}
+
+}  // extern "C"
