@@ -24,7 +24,8 @@
  *                         (c/qwanto_pagedeviction.c:54-93), lifted to pages
  *
  * All pointers named *_dev are device pointers; host_* are host pointers.
- * Calls that take a stream enqueue work and return without synchronising;
+ * Calls that take a stream enqueue work on it (NULL = the CUDA default
+ * stream) and return without synchronising;
  * device-side failures (pool exhausted, bad page id, a wait that timed out)
  * are latched in a status word read by qwn_kv_pool_check().
  * Status codes are QwnCudaStatus (qwn_cuda_abi.h).
@@ -129,7 +130,7 @@ typedef struct {
                                    attention mass summed over query heads */
     uint32_t attend_limit;      /* attend tokens [0, min(len, attend_limit)); 0 = len */
     uint32_t reserved;
-    void *stream;               /* cudaStream_t; NULL = the pool's stream */
+    void *stream;               /* cudaStream_t; NULL = the CUDA default stream */
 } QwnKvDecodeRequest;
 
 /* One layer of decode for a batch: when key_dev/value_dev are given, the

@@ -666,7 +666,14 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         if (cons.tile + 1 == cons.geo.ntiles || c + 1 == u1) {
             const uint32_t s_idx = cons.i * HK + cons.h;
             const uint64_t Us = cons.seg_base, ns = cons.geo.ntiles;
+            // warps whose (non-empty) range meets the segment: warp of unit u is
+            // ((u+1)W-1)/T.  With T >= W every warp between the first and the
+            // last is non-empty; with T < W each unit is a warp of its own.
             const uint64_t wa = ((Us + 1) * W - 1) / T, wb = ((Us + ns) * W - 1) / T;
+            const uint32_t nparts = T >= W ? (uint32_t)(wb - wa + 1) : (uint32_t)ns;
+            auto part_warp = [&](uint32_t pp) -> uint64_t {
+                return T >= W ? wa + pp : ((Us + pp + 1) * W - 1) / T;
+            };
             float lr = l;
             lr += __shfl_xor_sync(0xffffffffu, lr, 1);
             lr += __shfl_xor_sync(0xffffffffu, lr, 2);
@@ -681,7 +688,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
                 }
             }
             const size_t row0 = (size_t)cons.i * Hq + (size_t)cons.h * G;
-            if (wa == wb) {
+            if (nparts == 1) {
                 // this warp saw the whole segment: final output
                 if ((uint32_t)gid < G) {
                     const size_t row = row0 + gid;
@@ -723,19 +730,18 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
                 uint32_t old = 0;
                 if (lane == 0) old = atomicAdd(&A.counters[s_idx], 1u);
                 old = __shfl_sync(0xffffffffu, old, 0);
-                if (old == (uint32_t)(wb - wa)) {
+                if (old == nparts - 1) {
                     __threadfence();
-                    const uint32_t nparts = (uint32_t)(wb - wa + 1);
                     for (uint32_t g = 0; g < G; g++) {
                         float ms = -INFINITY;
                         for (uint32_t pp = 0; pp < nparts; pp++) {
-                            const float *sl = A.partials + (size_t)(wa + pp + s_idx) * kPartialFloats;
+                            const float *sl = A.partials + (size_t)(part_warp(pp) + s_idx) * kPartialFloats;
                             ms = fmaxf(ms, __ldcg(sl + kMaxGroup * kHeadDim + g));
                         }
                         float ls = 0.f;
                         float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
                         for (uint32_t pp = 0; pp < nparts; pp++) {
-                            const float *sl = A.partials + (size_t)(wa + pp + s_idx) * kPartialFloats;
+                            const float *sl = A.partials + (size_t)(part_warp(pp) + s_idx) * kPartialFloats;
                             const float wgt = ex2(__ldcg(sl + kMaxGroup * kHeadDim + g) - ms);
                             ls += __ldcg(sl + kMaxGroup * kHeadDim + kMaxGroup + g) * wgt;
                             const float4 v = __ldcg(reinterpret_cast<const float4 *>(sl + g * kHeadDim) + lane);

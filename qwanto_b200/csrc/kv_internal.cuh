@@ -84,9 +84,10 @@ inline Pool *pool_from(const QwnKvPoolHandle *h) {
     if (!h || !header_ok(h->header, sizeof(*h)) || !h->opaque) return nullptr;
     return static_cast<Pool *>(h->opaque);
 }
-inline cudaStream_t stream_of(Pool *p, void *s) {
-    return s ? static_cast<cudaStream_t>(s) : p->stream;
-}
+// NULL is the CUDA default stream of the calling thread (as for any CUDA
+// API), so callers on the default stream -- torch's current stream by
+// default -- are ordered with this library's launches.
+inline cudaStream_t stream_of(Pool *, void *s) { return static_cast<cudaStream_t>(s); }
 
 // launchers implemented in the .cu files (return cudaError_t of the launch)
 cudaError_t launch_seq_append(Pool *p, uint32_t n, const int32_t *seq_ids, const int32_t *counts,
