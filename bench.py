@@ -378,10 +378,18 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--ring", type=int, default=8, help="distinct input step buffers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override the config's layer count (profiling)")
+    ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3  # the timing rules want >= 3 warm-up steps
     wl = workload(args.config)
+    if args.layers:
+        wl["layers"] = args.layers
+        wl["name"] += f" [layers overridden to {args.layers}]"
+    if args.batch:
+        wl["batch"] = args.batch
+        wl["name"] += f" [batch overridden to {args.batch}]"
     if args.impl == "reference":
         # CPU only: rank 0 runs the reference, the other ranks exit at once
         return run_reference(args, wl, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
