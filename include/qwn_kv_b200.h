@@ -229,6 +229,39 @@ QWN_CUDA_ABI_API int qwn_kv_decode_step_host(QwnKvPoolHandle *pool,
                                              const QwnKvHostStepRequest *request,
                                              QwnCudaTelemetry *telemetry);
 
+/* Decode attention that allocates nothing.  This entry point has no
+ * counterpart in the reference; it exists for callers that cannot allocate
+ * device memory at the moment they need attention: a server that gave all
+ * free HBM to its own arena at start-up, a latency-critical loop that cannot
+ * afford cudaMalloc/cudaFree synchronising the device, or an FFI caller that
+ * holds only raw device pointers to a KV pool laid out as qwn_kv_pool_* lays
+ * it out (QwnKvPoolInfo gives them) and no pool handle.
+ * It runs the qwn_kv_decode attention (no append) with its scratch in a
+ * fixed device array inside the library (about 4.3 MB per device, held until
+ * the process exits).  Limits: num_seqs x kv_heads <= 256; query heads per kv
+ * head <= 8; head_dim 128; codecs Q8_B64_F32, Q8_HEAD_F16, Q4_G32.  All calls
+ * on a device share the array: calls whose work may overlap on the GPU race
+ * and must be ordered by the caller.  The first call on a device sets the
+ * array up (looks up its address); make it before any stream capture. */
+typedef struct {
+    QwnCudaAbiHeader header;
+    int32_t device_id;
+    uint32_t codec;
+    uint32_t layers, kv_heads, head_dim, page_tokens;  /* pool geometry */
+    uint32_t total_pages, max_seqs, max_pages_per_seq;
+    uint32_t layer, num_seqs, query_heads;
+    float scale;                    /* 0 = 1/sqrt(128) */
+    const void *pages_dev;
+    const int32_t *page_table_dev;  /* [max_seqs][max_pages_per_seq] */
+    const int32_t *seq_lens_dev;    /* [max_seqs] */
+    const int32_t *seq_ids_dev;     /* [num_seqs] or NULL = 0..num_seqs-1 */
+    const float *query_dev;         /* [num_seqs][query_heads][128] */
+    float *output_dev;              /* [num_seqs][query_heads][128] */
+    uint32_t *status_dev;           /* optional QWN_KV_STATUS_* bits */
+    void *stream;                   /* NULL = the CUDA default stream */
+} QwnKvStaticAttentionRequest;
+QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttentionRequest *request);
+
 /* copy a device range to/from host (tests and tools without a CUDA runtime) */
 QWN_CUDA_ABI_API int qwn_kv_memcpy_d2h(void *host, const void *dev, uint64_t bytes);
 QWN_CUDA_ABI_API int qwn_kv_memcpy_h2d(void *dev, const void *host, uint64_t bytes);

@@ -157,6 +157,16 @@ class HostStepRequest(C.Structure):
                 ("host_key", C.c_void_p), ("host_value", C.c_void_p), ("host_output", C.c_void_p)]
 
 
+class StaticAttentionRequest(C.Structure):
+    _fields_ = [("header", Header), ("device_id", C.c_int32), ("codec", C.c_uint32), ("layers", C.c_uint32),
+                ("kv_heads", C.c_uint32), ("head_dim", C.c_uint32), ("page_tokens", C.c_uint32),
+                ("total_pages", C.c_uint32), ("max_seqs", C.c_uint32), ("max_pages_per_seq", C.c_uint32),
+                ("layer", C.c_uint32), ("num_seqs", C.c_uint32), ("query_heads", C.c_uint32),
+                ("scale", C.c_float), ("pages_dev", C.c_void_p), ("page_table_dev", C.c_void_p),
+                ("seq_lens_dev", C.c_void_p), ("seq_ids_dev", C.c_void_p), ("query_dev", C.c_void_p),
+                ("output_dev", C.c_void_p), ("status_dev", C.c_void_p), ("stream", C.c_void_p)]
+
+
 _P = C.POINTER
 _SIGS = {
     "qwn_cuda_abi_query": (C.c_int, [_P(AbiInfo)]),
@@ -196,6 +206,7 @@ _SIGS = {
                                            C.c_void_p, C.c_void_p]),
     "qwn_kv_evict": (C.c_int, [_P(Handle), _P(EvictRequest)]),
     "qwn_kv_decode_step_host": (C.c_int, [_P(Handle), _P(HostStepRequest), _P(Telemetry)]),
+    "qwn_kv_attention_static": (C.c_int, [_P(StaticAttentionRequest)]),
     "qwn_kv_memcpy_d2h": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64]),
     "qwn_kv_memcpy_h2d": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64]),
     "qwn_kv_launch_count": (C.c_uint64, []),

@@ -882,3 +882,156 @@ cudaError_t launch_merge(uint32_t parts, uint32_t rows, const float *m, const fl
 }
 
 }  // namespace qkv
+
+// ===========================================================================
+// Decode attention that allocates nothing.
+//
+// Some callers cannot allocate device memory when they need attention: a
+// serving process that handed all free HBM to its own arena at start-up (a
+// cudaMalloc here would fail, or fragment the arena), a latency-critical loop
+// where cudaMalloc/cudaFree would synchronise the device and stall other
+// streams, and FFI callers that hold only raw device pointers to a KV pool and
+// no qwn_kv_pool handle (whose scratch was allocated with the pool).  This
+// entry point runs the same split-KV kernel with its scratch -- the partial
+// (m, l, o) slots and the merge counters -- in a file-scope device array.
+//
+// Limits: at most kStaticSegments (sequence x kv head) segments per call and
+// kStaticSlots partial slots (warps of the grid + segments); larger requests
+// are rejected.  The array is shared by every call on a device and keeps the
+// last call's contents: the counters are cleared on the stream at the start
+// of each call, so calls whose work overlaps on the GPU (different streams,
+// no ordering between them) race on the array and must not be issued.
+// The first call on a device looks up the array's device address and sets
+// the kernel's shared-memory attribute; make that first call before any
+// stream capture.  Every GPU that loads the library holds the array
+// (kStaticBytes) until the process exits.
+// ===========================================================================
+namespace qkv {
+namespace {
+constexpr int kStaticSlots = 1024;
+constexpr int kStaticSegments = 256;
+constexpr size_t kStaticFloats = (size_t)kStaticSlots * kPartialFloats + kStaticSegments;
+static __device__ __align__(256) float g_static_scratch[kStaticFloats];
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_mu;
+float *g_static_addr[kStaticMaxDevices] = {};
+uint32_t g_static_ctas[kStaticMaxDevices][5] = {};
+
+template <int CODEC>
+cudaError_t static_setup(int dev) {
+    using CD = Codec<CODEC>;
+    const size_t smem = (size_t)kWarpsPerCta * CD::kStages * (CD::kBytes + 8);
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int sms = 0, per_sm = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_kernel<CODEC>, kWarpsPerCta * 32, smem)) !=
+        cudaSuccess)
+        return e;
+    g_static_ctas[dev][CODEC] = (uint32_t)(sms * (per_sm > 0 ? per_sm : 1));
+    return cudaSuccess;
+}
+}  // namespace
+}  // namespace qkv
+
+extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttentionRequest *r) {
+    using namespace qkv;
+    if (!r || !header_ok(r->header, sizeof(*r))) return QWN_CUDA_STATUS_ABI_MISMATCH;
+    const size_t tb = tile_bytes_of(r->codec);
+    if (!tb || r->codec == QWN_KV_CODEC_TQ35_G64 || r->head_dim != (uint32_t)kHeadDim || r->kv_heads == 0 ||
+        r->page_tokens == 0 || r->page_tokens % 16 || r->layer >= r->layers || r->query_heads == 0 ||
+        r->query_heads % r->kv_heads || r->query_heads / r->kv_heads > (uint32_t)kMaxGroup || !r->pages_dev ||
+        !r->page_table_dev || !r->seq_lens_dev || !r->query_dev || !r->output_dev || r->total_pages == 0 ||
+        r->max_seqs == 0 || r->max_pages_per_seq == 0 || r->num_seqs > r->max_seqs) {
+        set_error("qwn_kv_attention_static: invalid request");
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    if ((uint64_t)r->num_seqs * r->kv_heads > (uint64_t)kStaticSegments) {
+        set_error("qwn_kv_attention_static: num_seqs x kv_heads exceeds the static scratch limit of 256 segments");
+        return QWN_CUDA_STATUS_UNSUPPORTED;
+    }
+    if (r->device_id < 0 || r->device_id >= kStaticMaxDevices) {
+        set_error("qwn_kv_attention_static: device id out of range");
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    cudaError_t e = cudaSetDevice(r->device_id);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_attention_static: cudaSetDevice", e); return QWN_CUDA_STATUS_UNAVAILABLE; }
+    const int dev = r->device_id;
+    {
+        std::lock_guard<std::mutex> lk(g_static_mu);
+        if (!g_static_addr[dev]) {
+            float *ptr = nullptr;
+            e = cudaGetSymbolAddress(reinterpret_cast<void **>(&ptr), g_static_scratch);
+            if (e != cudaSuccess || !ptr) {
+                set_cuda_error("qwn_kv_attention_static: cudaGetSymbolAddress", e);
+                return QWN_CUDA_STATUS_RUNTIME_ERROR;
+            }
+            if ((e = static_setup<QWN_KV_CODEC_Q8_B64_F32>(dev)) != cudaSuccess ||
+                (e = static_setup<QWN_KV_CODEC_Q8_HEAD_F16>(dev)) != cudaSuccess ||
+                (e = static_setup<QWN_KV_CODEC_Q4_G32>(dev)) != cudaSuccess) {
+                set_cuda_error("qwn_kv_attention_static: kernel set-up", e);
+                return QWN_CUDA_STATUS_RUNTIME_ERROR;
+            }
+            g_static_addr[dev] = ptr;
+        }
+    }
+    if (r->num_seqs == 0) return QWN_CUDA_STATUS_OK;
+    float *scratch = g_static_addr[dev];
+    uint32_t *counters = reinterpret_cast<uint32_t *>(scratch + (size_t)kStaticSlots * kPartialFloats);
+    cudaStream_t s = static_cast<cudaStream_t>(r->stream);
+    // the merge counters must start at zero; the slots are written before read
+    e = cudaMemsetAsync(counters, 0, sizeof(uint32_t) * kStaticSegments, s);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_attention_static: clear", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    const uint32_t segs = r->num_seqs * r->kv_heads;
+    uint32_t ctas = g_static_ctas[dev][r->codec];
+    const uint32_t max_ctas = (kStaticSlots - segs) / kWarpsPerCta;  // warps + segments <= slots
+    if (ctas > max_ctas) ctas = max_ctas;
+    AttnArgs A{};
+    A.pages = static_cast<const uint8_t *>(r->pages_dev);
+    A.tile_bytes = (uint32_t)tb;
+    A.tpp = r->page_tokens / 16;
+    A.page_tokens = r->page_tokens;
+    A.page_bytes = tb * A.tpp * (uint64_t)r->layers * r->kv_heads;
+    A.page_table = r->page_table_dev;
+    A.mp = r->max_pages_per_seq;
+    A.total_pages = r->total_pages;
+    A.max_seqs = r->max_seqs;
+    A.seq_lens = r->seq_lens_dev;
+    A.seq_ids = r->seq_ids_dev;
+    A.num_seqs = r->num_seqs;
+    A.kv_heads = r->kv_heads;
+    A.group = r->query_heads / r->kv_heads;
+    A.layer = r->layer;
+    A.query = r->query_dev;
+    A.output = r->output_dev;
+    A.scale_log2 = (r->scale > 0.f ? r->scale : 1.0f / sqrtf((float)kHeadDim)) * kLog2e;
+    A.partials = scratch;
+    A.counters = counters;
+    A.status = r->status_dev;
+    switch (r->codec) {
+        case QWN_KV_CODEC_Q8_HEAD_F16: {
+            using CD = Codec<QWN_KV_CODEC_Q8_HEAD_F16>;
+            attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16><<<ctas, kWarpsPerCta * 32,
+                kWarpsPerCta * CD::kStages * (CD::kBytes + 8), s>>>(A);
+            break;
+        }
+        case QWN_KV_CODEC_Q8_B64_F32: {
+            using CD = Codec<QWN_KV_CODEC_Q8_B64_F32>;
+            attn_kernel<QWN_KV_CODEC_Q8_B64_F32><<<ctas, kWarpsPerCta * 32,
+                kWarpsPerCta * CD::kStages * (CD::kBytes + 8), s>>>(A);
+            break;
+        }
+        default: {
+            using CD = Codec<QWN_KV_CODEC_Q4_G32>;
+            attn_kernel<QWN_KV_CODEC_Q4_G32><<<ctas, kWarpsPerCta * 32,
+                kWarpsPerCta * CD::kStages * (CD::kBytes + 8), s>>>(A);
+            break;
+        }
+    }
+    count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) {
+        set_cuda_error("qwn_kv_attention_static: launch", e);
+        return QWN_CUDA_STATUS_RUNTIME_ERROR;
+    }
+    return QWN_CUDA_STATUS_OK;
+}
