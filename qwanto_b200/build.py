@@ -19,7 +19,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "qwn_cuda.so")
 
 SOURCES = ["kv_pool.cu", "kv_attention.cu", "kv_evict.cu", "abi_v1.cu"]
-HEADERS = [os.path.join(CSRC, "kv_internal.cuh"), os.path.join(INCLUDE, "qwn_cuda_abi.h"),
+HEADERS = [os.path.join(CSRC, "kv_internal.cuh"), os.path.join(CSRC, "kv_store.cuh"), os.path.join(INCLUDE, "qwn_cuda_abi.h"),
            os.path.join(INCLUDE, "qwn_kv_b200.h")]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

@@ -18,7 +18,13 @@
 // GQA group of G<=8 query heads uses rows 0..G-1), scales and zero points are
 // applied in fp32 outside the MMA, so the result tracks the reference's fp32
 // arithmetic (c/qwanto_turboquant.c:648-705, :218-288) within ~1e-6.
+//
+// When the caller passes the newest token's K/V, the warp that owns the last
+// tile of a segment quantizes and stores that token into the page (the
+// append of c/qwanto_turboquant.c:632-646) just before it issues the bulk
+// copy of that tile, so append and attention are one launch.
 #include "kv_internal.cuh"
+#include "kv_store.cuh"
 
 #include <float.h>
 
@@ -26,7 +32,8 @@ namespace qkv {
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kNuInit = 7.888609052210118e-31f;  // 2^-100
+constexpr float kNuFloor = 7.888609052210118e-31f;  // 2^-100
+constexpr float kNuHeadroom = 16384.0f;            // rescale only when a scale exceeds nu * 2^14
 
 struct AttnArgs {
     const uint8_t *pages;
@@ -46,6 +53,7 @@ struct AttnArgs {
     float2 *tile_mass;
     float2 *seg_ml;
     float *part_m, *part_l, *part_o;  // non-null: export unnormalised (m, l, o)
+    const float *new_k, *new_v;       // non-null: fused append of the newest token
     uint32_t *status;
 };
 
@@ -54,26 +62,22 @@ __device__ __forceinline__ float pow2ceil(float x) {
     if (b & 0x7FFFFFu) b = (b & 0x7F800000u) + 0x00800000u;
     return __uint_as_float(b);
 }
-__device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w & 0xFFFF))); }
-__device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w >> 16))); }
+__device__ __forceinline__ float2 h2x2f(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+}
 
-__device__ __forceinline__ void split_hilo(float x, __half &hi, __half &lo) {
-    hi = __float2half_rn(x);
-    lo = __float2half_rn(x - __half2float(hi));
-}
-__device__ __forceinline__ uint32_t pack2(__half a, __half b) {
-    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
-}
 // A-operand rows gid (hi) and gid+8 (lo) for four values at k-positions
-// (2tig, 2tig+1) and (2tig+8, 2tig+9)
+// (2tig, 2tig+1) and (2tig+8, 2tig+9); packed conversions
 __device__ __forceinline__ void make_a(const float (&v)[4], uint32_t (&a)[4]) {
-    __half h[4], l[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) split_hilo(v[i], h[i], l[i]);
-    a[0] = pack2(h[0], h[1]);
-    a[1] = pack2(l[0], l[1]);
-    a[2] = pack2(h[2], h[3]);
-    a[3] = pack2(l[2], l[3]);
+    const __half2 h01 = __floats2half2_rn(v[0], v[1]);
+    const __half2 h23 = __floats2half2_rn(v[2], v[3]);
+    const float2 b01 = __half22float2(h01), b23 = __half22float2(h23);
+    const __half2 l01 = __floats2half2_rn(v[0] - b01.x, v[1] - b01.y);
+    const __half2 l23 = __floats2half2_rn(v[2] - b23.x, v[3] - b23.y);
+    a[0] = *reinterpret_cast<const uint32_t *>(&h01);
+    a[1] = *reinterpret_cast<const uint32_t *>(&l01);
+    a[2] = *reinterpret_cast<const uint32_t *>(&h23);
+    a[3] = *reinterpret_cast<const uint32_t *>(&l23);
 }
 
 // ---------------------------------------------------------------------------
@@ -87,9 +91,9 @@ __device__ __forceinline__ void online_softmax(const float (&s)[4], float (&p)[4
     float tmax = fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3]));
     tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
     tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-    float m_new = fmaxf(m, tmax);
+    const float m_new = fmaxf(m, tmax);
     if (__any_sync(0xffffffffu, m_new > m)) {
-        float alpha = ex2(m - m_new);
+        const float alpha = ex2(m - m_new);
         l *= alpha;
         acc.rescale_all(alpha);
         m = m_new;
@@ -99,16 +103,25 @@ __device__ __forceinline__ void online_softmax(const float (&s)[4], float (&p)[4
     l += (p[0] + p[1]) + (p[2] + p[3]);
 }
 
-// value normaliser: keep nu >= every value scale seen so that p*scale/nu <= 1
+// Value normaliser: nu is a power of two set from the first tile of the
+// segment; p*scale/nu is then an f16 of moderate size.  It is raised (with
+// an exact power-of-two rescale of the accumulators) only when a later scale
+// exceeds nu*2^14, which keeps p*scale/nu < 2^15 inside the f16 range.
 template <class Acc>
-__device__ __forceinline__ void update_nu(float vmax, int x, Acc &acc) {
-    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-    if (vmax > acc.nu[x]) {
-        float nn = pow2ceil(vmax);
-        acc.rescale_part(x, acc.nu[x] / nn);
-        acc.nu[x] = nn;
-        acc.inv_nu[x] = 1.0f / nn;
+__device__ __forceinline__ void update_nu(const float (&vs)[4], int x, Acc &acc) {
+    const float lmax = fmaxf(fmaxf(vs[0], vs[1]), fmaxf(vs[2], vs[3]));
+    const bool first = acc.nu[x] == 0.f;
+    if (__any_sync(0xffffffffu, first || lmax > acc.nu[x] * kNuHeadroom)) {
+        float vmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, 1));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+        const float nn = fmaxf(pow2ceil(vmax), kNuFloor);
+        if (first) {
+            acc.nu[x] = nn;
+        } else if (nn > acc.nu[x]) {
+            acc.rescale_part(x, acc.nu[x] / nn);
+            acc.nu[x] = nn;
+        }
+        acc.inv_nu[x] = 1.0f / acc.nu[x];
     }
 }
 
@@ -127,7 +140,7 @@ template <> struct Codec<QWN_KV_CODEC_Q8_HEAD_F16> {
         __device__ void reset() {
 #pragma unroll
             for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-            nu[0] = kNuInit; inv_nu[0] = 1.0f / kNuInit;
+            nu[0] = 0.f; inv_nu[0] = 0.f;
         }
         __device__ void rescale_all(float f) {
 #pragma unroll
@@ -142,7 +155,7 @@ template <> struct Codec<QWN_KV_CODEC_Q8_HEAD_F16> {
         for (int s = 0; s < 8; s++) {
             float v[4] = {0.f, 0.f, 0.f, 0.f};
             if (q) {
-                float4 x = *reinterpret_cast<const float4 *>(q + 64 * (s >> 2) + 16 * tig + 4 * (s & 3));
+                const float4 x = *reinterpret_cast<const float4 *>(q + 64 * (s >> 2) + 16 * tig + 4 * (s & 3));
                 v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
             }
             make_a(v, f.a[s]);
@@ -151,43 +164,39 @@ template <> struct Codec<QWN_KV_CODEC_Q8_HEAD_F16> {
     __device__ static float out_value(const Acc &acc, int j, int c, float) {
         return (acc.o[j][c] + acc.o[j][c + 2]) * acc.nu[0];
     }
-    __device__ static void compute(const uint8_t *tile, const Frag &f, Acc &acc, float &m, float &l,
-                                   int t_lo, int t_hi, float scale_log2, float &tile_u) {
-        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-        float s[4];
-        const uint2 ksr = *reinterpret_cast<const uint2 *>(tile + 4096 + 8 * tig);
-        const float ks[4] = {half_lo(ksr.x), half_hi(ksr.x), half_lo(ksr.y), half_hi(ksr.y)};
+    // K: per half h (token columns), two accumulator chains (even / odd
+    // k-steps) so consecutive MMAs are independent
+    __device__ static void qk(const uint8_t *tile, const Frag &f, float (&raw)[4]) {
+        const int lane = threadIdx.x & 31, sw = (lane >> 2) & 1;
+        const uint2 ksr = *reinterpret_cast<const uint2 *>(tile + 4096 + 8 * (lane & 3));
+        const float2 k01 = h2x2f(ksr.x), k23 = h2x2f(ksr.y);
 #pragma unroll
         for (int h = 0; h < 2; h++) {
-            float acc_k[4] = {0.f, 0.f, 0.f, 0.f};
             const uint4 *kp = reinterpret_cast<const uint4 *>(tile + h * 1024 + lane * 32);
-            const uint4 w0 = kp[gid & 1], w1 = kp[(gid & 1) ^ 1];
-            const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const uint4 x0 = kp[sw], x1 = kp[sw ^ 1];
+            const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int st = 0; st < 8; st++) {
+            for (int st = 0; st < 8; st += 2) {
                 uint32_t b0, b1;
-                u8x4_to_h2x2(wd[st], b0, b1);
-                mma16816(acc_k, f.a[st], b0, b1);
+                u8x4_to_h2x2(w[st], b0, b1);
+                mma16816(ce, f.a[st], b0, b1);
+                u8x4_to_h2x2(w[st + 1], b0, b1);
+                mma16816(co, f.a[st + 1], b0, b1);
             }
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int i = 2 * h + j, t = 4 * tig + i;
-                const float raw = acc_k[j] + acc_k[j + 2];
-                s[i] = (t >= t_lo && t < t_hi) ? raw * ks[i] * scale_log2 : -INFINITY;
-            }
+            const float sa = h ? k23.x : k01.x, sb = h ? k23.y : k01.y;
+            raw[2 * h] = ((ce[0] + co[0]) + (ce[2] + co[2])) * sa;
+            raw[2 * h + 1] = ((ce[1] + co[1]) + (ce[3] + co[3])) * sb;
         }
-        float p[4];
-        online_softmax(s, p, m, l, acc);
+    }
+    __device__ static void pv(const uint8_t *tile, Acc &acc, const float (&p)[4], const bool (&ok)[4]) {
+        const int lane = threadIdx.x & 31, tig = lane & 3;
         const uint2 vsr = *reinterpret_cast<const uint2 *>(tile + 4128 + 8 * tig);
-        float vs[4] = {half_lo(vsr.x), half_hi(vsr.x), half_lo(vsr.y), half_hi(vsr.y)};
-        float vmax = 0.f;
+        const float2 v01 = h2x2f(vsr.x), v23 = h2x2f(vsr.y);
+        float vs[4] = {v01.x, v01.y, v23.x, v23.y};
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int t = 4 * tig + i;
-            if (!(t >= t_lo && t < t_hi)) vs[i] = 0.f;
-            vmax = fmaxf(vmax, vs[i]);
-        }
-        update_nu(vmax, 0, acc);
+        for (int i = 0; i < 4; i++) vs[i] = ok[i] ? vs[i] : 0.f;
+        update_nu(vs, 0, acc);
         float pt[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) pt[i] = p[i] * vs[i] * acc.inv_nu[0];
@@ -206,7 +215,6 @@ template <> struct Codec<QWN_KV_CODEC_Q8_HEAD_F16> {
                 mma16816(acc.o[4 * q + r], a, b0, b1);
             }
         }
-        tile_u = (p[0] + p[1]) + (p[2] + p[3]);
     }
 };
 
@@ -220,7 +228,7 @@ template <> struct Codec<QWN_KV_CODEC_Q8_B64_F32> {
         __device__ void reset() {
 #pragma unroll
             for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-            nu[0] = nu[1] = kNuInit; inv_nu[0] = inv_nu[1] = 1.0f / kNuInit;
+            nu[0] = nu[1] = 0.f; inv_nu[0] = inv_nu[1] = 0.f;
         }
         __device__ void rescale_all(float f) {
 #pragma unroll
@@ -241,49 +249,41 @@ template <> struct Codec<QWN_KV_CODEC_Q8_B64_F32> {
     __device__ static float out_value(const Acc &acc, int j, int c, float) {
         return (acc.o[j][c] + acc.o[j][c + 2]) * acc.nu[j >> 3];
     }
-    __device__ static void compute(const uint8_t *tile, const Frag &f, Acc &acc, float &m, float &l,
-                                   int t_lo, int t_hi, float scale_log2, float &tile_u) {
-        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-        float s[4];
-        const float4 k0 = *reinterpret_cast<const float4 *>(tile + 4096 + 16 * tig);
-        const float4 k1 = *reinterpret_cast<const float4 *>(tile + 4096 + 64 + 16 * tig);
-        const float ks0[4] = {k0.x, k0.y, k0.z, k0.w}, ks1[4] = {k1.x, k1.y, k1.z, k1.w};
+    // k-steps 0-3 cover dims 0..63 (scale 0), 4-7 dims 64..127 (scale 1)
+    __device__ static void qk(const uint8_t *tile, const Frag &f, float (&raw)[4]) {
+        const int lane = threadIdx.x & 31, sw = (lane >> 2) & 1, tig = lane & 3;
+        const float4 ka = *reinterpret_cast<const float4 *>(tile + 4096 + 16 * tig);
+        const float4 kb = *reinterpret_cast<const float4 *>(tile + 4096 + 64 + 16 * tig);
 #pragma unroll
         for (int h = 0; h < 2; h++) {
-            float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
             const uint4 *kp = reinterpret_cast<const uint4 *>(tile + h * 1024 + lane * 32);
-            const uint4 w0 = kp[gid & 1], w1 = kp[(gid & 1) ^ 1];
-            const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const uint4 x0 = kp[sw], x1 = kp[sw ^ 1];
+            const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int st = 0; st < 4; st++) {
                 uint32_t b0, b1;
-                u8x4_to_h2x2(wd[st], b0, b1);
-                mma16816(a0, f.a[st], b0, b1);
-                u8x4_to_h2x2(wd[st + 4], b0, b1);
-                mma16816(a1, f.a[st + 4], b0, b1);
+                u8x4_to_h2x2(w[st], b0, b1);
+                mma16816(ca, f.a[st], b0, b1);
+                u8x4_to_h2x2(w[st + 4], b0, b1);
+                mma16816(cb, f.a[st + 4], b0, b1);
             }
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int i = 2 * h + j, t = 4 * tig + i;
-                const float raw = (a0[j] + a0[j + 2]) * ks0[i] + (a1[j] + a1[j + 2]) * ks1[i];
-                s[i] = (t >= t_lo && t < t_hi) ? raw * scale_log2 : -INFINITY;
-            }
+            const float sa0 = h ? ka.z : ka.x, sa1 = h ? ka.w : ka.y;
+            const float sb0 = h ? kb.z : kb.x, sb1 = h ? kb.w : kb.y;
+            raw[2 * h] = (ca[0] + ca[2]) * sa0 + (cb[0] + cb[2]) * sb0;
+            raw[2 * h + 1] = (ca[1] + ca[3]) * sa1 + (cb[1] + cb[3]) * sb1;
         }
-        float p[4];
-        online_softmax(s, p, m, l, acc);
+    }
+    __device__ static void pv(const uint8_t *tile, Acc &acc, const float (&p)[4], const bool (&ok)[4]) {
+        const int lane = threadIdx.x & 31, tig = lane & 3;
         uint32_t a[2][4];
 #pragma unroll
         for (int x = 0; x < 2; x++) {
             const float4 v4 = *reinterpret_cast<const float4 *>(tile + 4224 + 64 * x + 16 * tig);
             float vs[4] = {v4.x, v4.y, v4.z, v4.w};
-            float vmax = 0.f;
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int t = 4 * tig + i;
-                if (!(t >= t_lo && t < t_hi)) vs[i] = 0.f;
-                vmax = fmaxf(vmax, vs[i]);
-            }
-            update_nu(vmax, x, acc);
+            for (int i = 0; i < 4; i++) vs[i] = ok[i] ? vs[i] : 0.f;
+            update_nu(vs, x, acc);
             float pt[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) pt[i] = p[i] * vs[i] * acc.inv_nu[x];
@@ -302,7 +302,6 @@ template <> struct Codec<QWN_KV_CODEC_Q8_B64_F32> {
                 mma16816(acc.o[4 * q + r], a[q >> 1], b0, b1);
             }
         }
-        tile_u = (p[0] + p[1]) + (p[2] + p[3]);
     }
 };
 
@@ -318,7 +317,7 @@ template <> struct Codec<QWN_KV_CODEC_Q4_G32> {
 #pragma unroll
             for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 #pragma unroll
-            for (int g = 0; g < 4; g++) { z[g] = 0.f; nu[g] = kNuInit; inv_nu[g] = 1.0f / kNuInit; }
+            for (int g = 0; g < 4; g++) { z[g] = 0.f; nu[g] = 0.f; inv_nu[g] = 0.f; }
         }
         __device__ void rescale_all(float f) {
 #pragma unroll
@@ -344,7 +343,7 @@ template <> struct Codec<QWN_KV_CODEC_Q4_G32> {
             for (int e = 0; e < 2; e++) {
                 float v[4] = {0.f, 0.f, 0.f, 0.f};
                 if (q) {
-                    float4 x = *reinterpret_cast<const float4 *>(q + 32 * g + 16 * e + 4 * tig);
+                    const float4 x = *reinterpret_cast<const float4 *>(q + 32 * g + 16 * e + 4 * tig);
                     v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
                 }
                 part += (v[0] + v[1]) + (v[2] + v[3]);
@@ -359,63 +358,47 @@ template <> struct Codec<QWN_KV_CODEC_Q4_G32> {
     __device__ static float out_value(const Acc &acc, int j, int c, float zsum) {
         return (acc.o[j][c] + acc.o[j][c + 2]) * acc.nu[j >> 2] + zsum;
     }
-    __device__ static void compute(const uint8_t *tile, const Frag &f, Acc &acc, float &m, float &l,
-                                   int t_lo, int t_hi, float scale_log2, float &tile_u) {
+    __device__ static void qk(const uint8_t *tile, const Frag &f, float (&raw)[4]) {
         const int lane = threadIdx.x & 31, tig = lane & 3;
-        float s[4];
-        float kr[4][4], km[4][4];  // [group][token i]
+        const uint4 kw0 = *reinterpret_cast<const uint4 *>(tile + lane * 16);
+        const uint4 kw1 = *reinterpret_cast<const uint4 *>(tile + 512 + lane * 16);
+        const uint32_t w0[4] = {kw0.x, kw0.y, kw0.z, kw0.w}, w1[4] = {kw1.x, kw1.y, kw1.z, kw1.w};
+        raw[0] = raw[1] = raw[2] = raw[3] = 0.f;
 #pragma unroll
         for (int g = 0; g < 4; g++) {
+            float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t r[4], u[4];
+            nib8_to_h2x4(w0[g], r);
+            nib8_to_h2x4(w1[g], u);
+            mma16816(c0, f.a[2 * g], r[0], r[1]);
+            mma16816(c1, f.a[2 * g], u[0], u[1]);
+            mma16816(c0, f.a[2 * g + 1], r[2], r[3]);
+            mma16816(c1, f.a[2 * g + 1], u[2], u[3]);
             const uint4 kp = *reinterpret_cast<const uint4 *>(tile + 2048 + 64 * g + 16 * tig);
-            const uint32_t w[4] = {kp.x, kp.y, kp.z, kp.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                kr[g][i] = half_lo(w[i]) * (1.0f / 15.0f);
-                km[g][i] = half_hi(w[i]);
-            }
+            const float2 p0 = h2x2f(kp.x), p1 = h2x2f(kp.y), p2 = h2x2f(kp.z), p3 = h2x2f(kp.w);
+            const float zq = f.qsum[g];
+            raw[0] += p0.x * (1.0f / 15.0f) * (c0[0] + c0[2]) + p0.y * zq;
+            raw[1] += p1.x * (1.0f / 15.0f) * (c0[1] + c0[3]) + p1.y * zq;
+            raw[2] += p2.x * (1.0f / 15.0f) * (c1[0] + c1[2]) + p2.y * zq;
+            raw[3] += p3.x * (1.0f / 15.0f) * (c1[1] + c1[3]) + p3.y * zq;
         }
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint4 kw = *reinterpret_cast<const uint4 *>(tile + h * 512 + lane * 16);
-            const uint32_t wd[4] = {kw.x, kw.y, kw.z, kw.w};
-            float raw[2] = {0.f, 0.f};
-#pragma unroll
-            for (int g = 0; g < 4; g++) {
-                float acc_k[4] = {0.f, 0.f, 0.f, 0.f};
-                uint32_t r[4];
-                nib8_to_h2x4(wd[g], r);
-                mma16816(acc_k, f.a[2 * g], r[0], r[1]);
-                mma16816(acc_k, f.a[2 * g + 1], r[2], r[3]);
-#pragma unroll
-                for (int j = 0; j < 2; j++) {
-                    const int i = 2 * h + j;
-                    raw[j] += kr[g][i] * (acc_k[j] + acc_k[j + 2]) + km[g][i] * f.qsum[g];
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int i = 2 * h + j, t = 4 * tig + i;
-                s[i] = (t >= t_lo && t < t_hi) ? raw[j] * scale_log2 : -INFINITY;
-            }
-        }
-        float p[4];
-        online_softmax(s, p, m, l, acc);
+    }
+    __device__ static void pv(const uint8_t *tile, Acc &acc, const float (&p)[4], const bool (&ok)[4]) {
+        const int lane = threadIdx.x & 31, tig = lane & 3;
         uint32_t a[4][4];
 #pragma unroll
         for (int g = 0; g < 4; g++) {
             const uint4 vp = *reinterpret_cast<const uint4 *>(tile + 2304 + 64 * g + 16 * tig);
-            const uint32_t w[4] = {vp.x, vp.y, vp.z, vp.w};
-            float vs[4], vmax = 0.f;
+            const float2 p0 = h2x2f(vp.x), p1 = h2x2f(vp.y), p2 = h2x2f(vp.z), p3 = h2x2f(vp.w);
+            float vs[4] = {p0.x * (1.0f / 15.0f), p1.x * (1.0f / 15.0f), p2.x * (1.0f / 15.0f),
+                           p3.x * (1.0f / 15.0f)};
+            const float mn[4] = {p0.y, p1.y, p2.y, p3.y};
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const int t = 4 * tig + i;
-                const bool ok = t >= t_lo && t < t_hi;
-                vs[i] = ok ? half_lo(w[i]) * (1.0f / 15.0f) : 0.f;
-                const float mn = ok ? half_hi(w[i]) : 0.f;
-                acc.z[g] += p[i] * mn;
-                vmax = fmaxf(vmax, vs[i]);
+                vs[i] = ok[i] ? vs[i] : 0.f;
+                acc.z[g] += ok[i] ? p[i] * mn[i] : 0.f;
             }
-            update_nu(vmax, g, acc);
+            update_nu(vs, g, acc);
             float pt[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) pt[i] = p[i] * vs[i] * acc.inv_nu[g];
@@ -436,9 +419,37 @@ template <> struct Codec<QWN_KV_CODEC_Q4_G32> {
                 mma16816(acc.o[2 * wi + 1], a[wi >> 1], b[2], b[3]);
             }
         }
-        tile_u = (p[0] + p[1]) + (p[2] + p[3]);
     }
 };
+
+// one tile: scores, online softmax, P x V.  Returns the tile's probability
+// mass of this lane's tokens (for eviction scores).
+template <int CODEC>
+__device__ __forceinline__ float tile_step(const uint8_t *tile, const typename Codec<CODEC>::Frag &f,
+                                           typename Codec<CODEC>::Acc &acc, float &m, float &l, int t_lo,
+                                           int t_hi, float scale_log2) {
+    using CD = Codec<CODEC>;
+    const int tig = threadIdx.x & 3;
+    float raw[4];
+    CD::qk(tile, f, raw);
+    float s[4];
+    bool ok[4];
+    if (t_lo == 0 && t_hi == 16) {  // warp-uniform: full tile
+#pragma unroll
+        for (int i = 0; i < 4; i++) { s[i] = raw[i] * scale_log2; ok[i] = true; }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int t = 4 * tig + i;
+            ok[i] = t >= t_lo && t < t_hi;
+            s[i] = ok[i] ? raw[i] * scale_log2 : -INFINITY;
+        }
+    }
+    float p[4];
+    online_softmax(s, p, m, l, acc);
+    CD::pv(tile, acc, p, ok);
+    return (p[0] + p[1]) + (p[2] + p[3]);
+}
 
 // ---------------------------------------------------------------------------
 // batch geometry
@@ -460,7 +471,7 @@ __device__ __forceinline__ Geo geo_of(const AttnArgs &A, uint32_t i) {
     int32_t hi = A.seq_lens[g.seq];
     if (A.attend_limit && hi > (int32_t)A.attend_limit) hi = (int32_t)A.attend_limit;
     if (A.t_end && hi > (int32_t)A.t_end) hi = (int32_t)A.t_end;
-    int32_t lo = (int32_t)A.t_begin;
+    const int32_t lo = (int32_t)A.t_begin;
     if (hi > (int32_t)(A.mp * A.page_tokens)) {
         latch(A.status, QWN_KV_STATUS_BAD_LENGTH);
         hi = (int32_t)(A.mp * A.page_tokens);
@@ -519,153 +530,67 @@ __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t v) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        uint32_t n = __shfl_up_sync(0xffffffffu, v, o);
+        const uint32_t n = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += n;
     }
     return v;
 }
 
-// ---------------------------------------------------------------------------
-// the kernel
-// ---------------------------------------------------------------------------
-template <int CODEC>
-__global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnArgs A) {
-    using CD = Codec<CODEC>;
-    constexpr int S = CD::kStages, B = CD::kBytes;
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-    uint8_t *wsm = smem + (size_t)warp * S * B;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)kWarpsPerCta * S * B) + warp * S;
-    if (lane == 0) {
-#pragma unroll
-        for (int st = 0; st < S; st++) mbar_init(&bars[st], 1);
-        fence_barrier_init();
+// per-warp shared-memory window: sources of the next 32 units and, for the
+// fused append, the segment whose newest token lives in that unit (-1: none)
+struct WarpWindow {
+    const uint8_t *src[32];
+    int32_t append_seg[32];
+};
+
+// Fill the window with units [base, base+32) of this warp, lane L taking unit
+// base+L, walking forward `skip` units from `from`.
+__device__ __forceinline__ void fill_window(const AttnArgs &A, const Walk &from, uint32_t skip, uint64_t base,
+                                            uint64_t u1, WarpWindow *win) {
+    const int lane = threadIdx.x & 31;
+    const uint8_t *src = nullptr;
+    int32_t app = -1;
+    if (base + lane < u1) {
+        Walk t = from;
+        walk_advance(A, t, skip + lane);
+        src = unit_addr(A, t);
+        if (A.new_k && t.tile + 1 == t.geo.ntiles) app = (int32_t)(t.i * A.kv_heads + t.h);
     }
+    win->src[lane] = src;
+    win->append_seg[lane] = app;
     __syncwarp();
+}
 
+// quantize and store the newest token of segment `seg` into `tile`
+template <int CODEC>
+__device__ __noinline__ void fused_append(const float *new_k, const float *new_v, const int32_t *seq_ids,
+                                          const int32_t *seq_lens, uint32_t kv_heads, int32_t seg,
+                                          const uint8_t *tile) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t i = (uint32_t)seg / kv_heads, h = (uint32_t)seg % kv_heads;
+    const int32_t seq = seq_ids ? seq_ids[i] : (int32_t)i;
+    const int32_t pos = seq_lens[seq] - 1;
+    const size_t row = ((size_t)i * kv_heads + h) * kHeadDim;
+    const float4 k = reinterpret_cast<const float4 *>(new_k + row)[lane];
+    const float4 v = reinterpret_cast<const float4 *>(new_v + row)[lane];
+    store_token<CODEC>(const_cast<uint8_t *>(tile), pos & 15, k, v, lane);
+    // the bulk copy that follows reads this tile through the async proxy
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncwarp();
+}
+
+// End of a warp's share of a segment: write the output, or a partial and
+// merge when this warp is the last to finish the segment.  Kept out of line
+// so the streaming loop keeps its registers.
+template <int CODEC>
+__device__ __forceinline__ void finish_segment(const AttnArgs &A, const typename Codec<CODEC>::Acc &acc, float m, float l,
+                                            uint32_t seg_i, uint32_t seg_h, uint64_t Us, uint64_t ns, uint64_t T,
+                                            uint64_t W, uint64_t wid) {
+    using CD = Codec<CODEC>;
+    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
     const uint32_t HK = A.kv_heads, G = A.group, Hq = HK * G;
-    const uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
-    const uint64_t wid = (uint64_t)blockIdx.x * kWarpsPerCta + warp;
-
-    // total units of the batch
-    uint64_t T = 0;
-    for (uint32_t base = 0; base < A.num_seqs; base += 32) {
-        const uint32_t i = base + lane;
-        uint32_t u = i < A.num_seqs ? geo_of(A, i).ntiles * HK : 0;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
-        T += u;
-    }
-    if (T == 0) return;
-    const uint64_t u0 = wid * T / W, u1 = (wid + 1) * T / W;
-    if (u0 >= u1) return;
-
-    // locate u0
-    Walk cons;
-    {
-        uint64_t acc = 0;
-        for (uint32_t base = 0; base < A.num_seqs; base += 32) {
-            const uint32_t i = base + lane;
-            const uint32_t u = i < A.num_seqs ? geo_of(A, i).ntiles * HK : 0;
-            const uint32_t incl = warp_incl_scan(u);
-            const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
-            if (u0 < acc + tot) {
-                const uint32_t ball = __ballot_sync(0xffffffffu, acc + incl > u0);
-                const int L = __ffs(ball) - 1;
-                const uint32_t excl = __shfl_sync(0xffffffffu, incl - u, L);
-                cons.i = base + L;
-                cons.geo = geo_of(A, cons.i);
-                const uint64_t rem = u0 - (acc + excl);
-                cons.h = (uint32_t)(rem / cons.geo.ntiles);
-                cons.tile = (uint32_t)(rem % cons.geo.ntiles);
-                cons.seg_base = acc + excl + (uint64_t)cons.h * cons.geo.ntiles;
-                break;
-            }
-            acc += tot;
-        }
-    }
-
-    // address window: lane L holds the source of unit win_base + L
-    Walk win = cons;
-    uint64_t win_base = u0;
-    const uint8_t *my_src = nullptr;
-    {
-        Walk t = win;
-        walk_advance(A, t, lane);
-        if (win_base + lane < u1) my_src = unit_addr(A, t);
-    }
-#pragma unroll
-    for (int st = 0; st < S; st++) {
-        const uint64_t j = u0 + st;
-        const uint8_t *src = (const uint8_t *)__shfl_sync(0xffffffffu, (unsigned long long)my_src, st);
-        if (j < u1 && lane == 0) {
-            mbar_expect_tx(&bars[st], B);
-            bulk_g2s(wsm + st * B, src, B, &bars[st]);
-        }
-    }
-
-    typename CD::Frag frag;
-    typename CD::Acc acc;
-    float m = -INFINITY, l = 0.f;
-    const float2 *no_mass = nullptr;
-    (void)no_mass;
-
-    for (uint64_t c = u0; c < u1; ++c) {
-        const uint32_t st = (uint32_t)((c - u0) % S);
-        const uint32_t par = (uint32_t)(((c - u0) / S) & 1);
-        if (cons.tile == 0 || c == u0) {
-            const float *q = nullptr;
-            if ((uint32_t)gid < G)
-                q = A.query + ((size_t)cons.i * Hq + (size_t)cons.h * G + gid) * kHeadDim;
-            CD::load_q(frag, q, tig);
-            acc.reset();
-            m = -INFINITY;
-            l = 0.f;
-        }
-        if (!mbar_wait_bounded(&bars[st], par)) {
-            if (lane == 0) latch(A.status, QWN_KV_STATUS_WAIT_TIMEOUT);
-            // wait (bounded) for the copies still in flight into this warp's stages
-            for (uint64_t d = c + 1; d < u1 && d < c + S; ++d) {
-                const uint32_t s2 = (uint32_t)((d - u0) % S), p2 = (uint32_t)(((d - u0) / S) & 1);
-                mbar_wait_bounded(&bars[s2], p2);
-            }
-            return;
-        }
-        const int tile_tok0 = (int)(cons.geo.tile0 + cons.tile) * 16;
-        const int t_lo = max(cons.geo.tok_lo - tile_tok0, 0);
-        const int t_hi = min(cons.geo.tok_hi - tile_tok0, 16);
-        float tile_u;
-        CD::compute(wsm + st * B, frag, acc, m, l, t_lo, t_hi, A.scale_log2, tile_u);
-        if (A.tile_mass) {
-            tile_u += __shfl_xor_sync(0xffffffffu, tile_u, 1);
-            tile_u += __shfl_xor_sync(0xffffffffu, tile_u, 2);
-            if (tig == 0 && (uint32_t)gid < G) A.tile_mass[c * kMaxGroup + gid] = make_float2(tile_u, m);
-        }
-        __syncwarp();
-
-        // refill this stage with unit c + S
-        const uint64_t j = c + S;
-        if (j < u1) {
-            if (j >= win_base + 32) {
-                walk_advance(A, win, 32);
-                win_base += 32;
-                Walk t = win;
-                walk_advance(A, t, lane);
-                my_src = (win_base + lane < u1) ? unit_addr(A, t) : nullptr;
-            }
-            const uint8_t *src =
-                (const uint8_t *)__shfl_sync(0xffffffffu, (unsigned long long)my_src, (int)(j - win_base));
-            if (lane == 0) {
-                fence_proxy_async_shared();
-                mbar_expect_tx(&bars[st], B);
-                bulk_g2s(wsm + st * B, src, B, &bars[st]);
-            }
-        }
-
-        // end of this warp's share of the segment?
-        if (cons.tile + 1 == cons.geo.ntiles || c + 1 == u1) {
+    struct { uint32_t i, h; } cons = {seg_i, seg_h};
             const uint32_t s_idx = cons.i * HK + cons.h;
-            const uint64_t Us = cons.seg_base, ns = cons.geo.ntiles;
             // warps whose (non-empty) range meets the segment: warp of unit u is
             // ((u+1)W-1)/T.  With T >= W every warp between the first and the
             // last is non-empty; with T < W each unit is a warp of its own.
@@ -718,8 +643,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
                     for (int jn = 0; jn < 16; jn++)
 #pragma unroll
                         for (int cc = 0; cc < 2; cc++)
-                            slot[gid * kHeadDim + CD::dim_of(jn, tig, cc)] =
-                                CD::out_value(acc, jn, cc, zs[jn >> 2]);
+                            slot[gid * kHeadDim + CD::dim_of(jn, tig, cc)] = CD::out_value(acc, jn, cc, zs[jn >> 2]);
                     if (tig == 0) {
                         slot[kMaxGroup * kHeadDim + gid] = m;
                         slot[kMaxGroup * kHeadDim + kMaxGroup + gid] = lr;
@@ -762,8 +686,141 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
                 }
             }
         }
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int CODEC>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnArgs A) {
+    using CD = Codec<CODEC>;
+    constexpr int S = CD::kStages, B = CD::kBytes;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    uint8_t *wsm = smem + (size_t)warp * S * B;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)kWarpsPerCta * S * B) + warp * S;
+    WarpWindow *win = reinterpret_cast<WarpWindow *>(smem + (size_t)kWarpsPerCta * S * (B + 8)) + warp;
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < S; st++) mbar_init(&bars[st], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+
+    const uint32_t HK = A.kv_heads, G = A.group, Hq = HK * G;
+    const uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
+    const uint64_t wid = (uint64_t)blockIdx.x * kWarpsPerCta + warp;
+
+    // total units of the batch
+    uint64_t T = 0;
+    for (uint32_t base = 0; base < A.num_seqs; base += 32) {
+        const uint32_t i = base + lane;
+        uint32_t u = i < A.num_seqs ? geo_of(A, i).ntiles * HK : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
+        T += u;
+    }
+    if (T == 0) return;
+    const uint64_t u0 = wid * T / W, u1 = (wid + 1) * T / W;
+    if (u0 >= u1) return;
+    const uint32_t n = (uint32_t)(u1 - u0);
+
+    // locate u0
+    Walk cons;
+    {
+        uint64_t acc = 0;
+        for (uint32_t base = 0; base < A.num_seqs; base += 32) {
+            const uint32_t i = base + lane;
+            const uint32_t u = i < A.num_seqs ? geo_of(A, i).ntiles * HK : 0;
+            const uint32_t incl = warp_incl_scan(u);
+            const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
+            if (u0 < acc + tot) {
+                const uint32_t ball = __ballot_sync(0xffffffffu, acc + incl > u0);
+                const int L = __ffs(ball) - 1;
+                const uint32_t excl = __shfl_sync(0xffffffffu, incl - u, L);
+                cons.i = base + L;
+                cons.geo = geo_of(A, cons.i);
+                const uint64_t rem = u0 - (acc + excl);
+                cons.h = (uint32_t)(rem / cons.geo.ntiles);
+                cons.tile = (uint32_t)(rem % cons.geo.ntiles);
+                cons.seg_base = acc + excl + (uint64_t)cons.h * cons.geo.ntiles;
+                break;
+            }
+            acc += tot;
+        }
+    }
+
+    // window of unit sources: units [wbase, wbase+32) of this warp's range
+    uint32_t wbase = 0;
+    fill_window(A, cons, 0, u0, u1, win);
+    const uint32_t npro = n < (uint32_t)S ? n : (uint32_t)S;
+    for (uint32_t j = 0; j < npro; j++) {
+        const int32_t seg = win->append_seg[j];
+        if (seg >= 0) fused_append<CODEC>(A.new_k, A.new_v, A.seq_ids, A.seq_lens, A.kv_heads, seg, win->src[j]);
+        if (lane == 0) {
+            mbar_expect_tx(&bars[j], B);
+            bulk_g2s(wsm + j * B, win->src[j], B, &bars[j]);
+        }
+    }
+
+    typename CD::Frag frag;
+    typename CD::Acc acc;
+    float m = -INFINITY, l = 0.f;
+    uint32_t st = 0, par = 0;
+
+    for (uint32_t k = 0; k < n; ++k) {
+        if (cons.tile == 0 || k == 0) {
+            const float *q = nullptr;
+            if ((uint32_t)gid < G) q = A.query + ((size_t)cons.i * Hq + (size_t)cons.h * G + gid) * kHeadDim;
+            CD::load_q(frag, q, tig);
+            acc.reset();
+            m = -INFINITY;
+            l = 0.f;
+        }
+        if (!mbar_wait_bounded(&bars[st], par)) {
+            if (lane == 0) latch(A.status, QWN_KV_STATUS_WAIT_TIMEOUT);
+            // wait (bounded) for the copies still in flight into this warp's stages
+            uint32_t s2 = st, p2 = par;
+            for (uint32_t d = k + 1; d < n && d < k + (uint32_t)S; ++d) {
+                if (++s2 == (uint32_t)S) { s2 = 0; p2 ^= 1u; }
+                mbar_wait_bounded(&bars[s2], p2);
+            }
+            return;
+        }
+        const int tile_tok0 = (int)(cons.geo.tile0 + cons.tile) * 16;
+        const int t_lo = max(cons.geo.tok_lo - tile_tok0, 0);
+        const int t_hi = min(cons.geo.tok_hi - tile_tok0, 16);
+        float tile_u = tile_step<CODEC>(wsm + st * B, frag, acc, m, l, t_lo, t_hi, A.scale_log2);
+        if (A.tile_mass) {
+            tile_u += __shfl_xor_sync(0xffffffffu, tile_u, 1);
+            tile_u += __shfl_xor_sync(0xffffffffu, tile_u, 2);
+            if (tig == 0 && (uint32_t)gid < G)
+                A.tile_mass[(u0 + k) * kMaxGroup + gid] = make_float2(tile_u, m);
+        }
+        __syncwarp();
+
+        // refill this stage with unit k + S
+        const uint32_t j = k + (uint32_t)S;
+        if (j < n) {
+            if (j - wbase == 32u) {
+                wbase = j;
+                fill_window(A, cons, (uint32_t)S, u0 + wbase, u1, win);
+            }
+            const int32_t seg = win->append_seg[j - wbase];
+            const uint8_t *src = win->src[j - wbase];
+            if (seg >= 0) fused_append<CODEC>(A.new_k, A.new_v, A.seq_ids, A.seq_lens, A.kv_heads, seg, src);
+            if (lane == 0) {
+                fence_proxy_async_shared();
+                mbar_expect_tx(&bars[st], B);
+                bulk_g2s(wsm + st * B, src, B, &bars[st]);
+            }
+        }
+        if (++st == (uint32_t)S) { st = 0; par ^= 1u; }
+
+        // end of this warp's share of the segment?
+        if (cons.tile + 1 == cons.geo.ntiles || k + 1 == n)
+            finish_segment<CODEC>(A, acc, m, l, cons.i, cons.h, cons.seg_base, cons.geo.ntiles, T, W, wid);
         // next unit
-        if (c + 1 < u1) {
+        if (k + 1 < n) {
             if (++cons.tile == cons.geo.ntiles) walk_next_segment(A, cons);
         }
     }
@@ -788,10 +845,14 @@ __global__ void merge_kernel(uint32_t parts, uint32_t rows, const float *m, cons
 }
 
 template <int CODEC>
+constexpr size_t codec_smem() {
+    return (size_t)kWarpsPerCta * Codec<CODEC>::kStages * (Codec<CODEC>::kBytes + 8) +
+           (size_t)kWarpsPerCta * sizeof(WarpWindow);
+}
+
+template <int CODEC>
 cudaError_t launch_codec(Pool *p, const AttnArgs &A, cudaStream_t s) {
-    using CD = Codec<CODEC>;
-    const size_t smem = (size_t)kWarpsPerCta * CD::kStages * CD::kBytes +
-                        (size_t)kWarpsPerCta * CD::kStages * sizeof(uint64_t);
+    const size_t smem = codec_smem<CODEC>();
     static bool configured[64] = {false};
     if (!configured[p->device & 63]) {
         cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC>,
@@ -808,18 +869,9 @@ cudaError_t launch_codec(Pool *p, const AttnArgs &A, cudaStream_t s) {
 
 size_t attention_smem_bytes(uint32_t codec) {
     switch (codec) {
-        case QWN_KV_CODEC_Q8_HEAD_F16: {
-            using CD = Codec<QWN_KV_CODEC_Q8_HEAD_F16>;
-            return (size_t)kWarpsPerCta * CD::kStages * (CD::kBytes + 8);
-        }
-        case QWN_KV_CODEC_Q8_B64_F32: {
-            using CD = Codec<QWN_KV_CODEC_Q8_B64_F32>;
-            return (size_t)kWarpsPerCta * CD::kStages * (CD::kBytes + 8);
-        }
-        case QWN_KV_CODEC_Q4_G32: {
-            using CD = Codec<QWN_KV_CODEC_Q4_G32>;
-            return (size_t)kWarpsPerCta * CD::kStages * (CD::kBytes + 8);
-        }
+        case QWN_KV_CODEC_Q8_HEAD_F16: return codec_smem<QWN_KV_CODEC_Q8_HEAD_F16>();
+        case QWN_KV_CODEC_Q8_B64_F32: return codec_smem<QWN_KV_CODEC_Q8_B64_F32>();
+        case QWN_KV_CODEC_Q4_G32: return codec_smem<QWN_KV_CODEC_Q4_G32>();
         default: return 0;
     }
 }
@@ -864,6 +916,8 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
     A.part_m = a.part_m;
     A.part_l = a.part_l;
     A.part_o = a.part_o;
+    A.new_k = a.new_k;
+    A.new_v = a.new_v;
     A.status = p->status;
     switch (p->codec) {
         case QWN_KV_CODEC_Q8_HEAD_F16: return launch_codec<QWN_KV_CODEC_Q8_HEAD_F16>(p, A, s);
@@ -919,8 +973,7 @@ uint32_t g_static_ctas[kStaticMaxDevices][5] = {};
 
 template <int CODEC>
 cudaError_t static_setup(int dev) {
-    using CD = Codec<CODEC>;
-    const size_t smem = (size_t)kWarpsPerCta * CD::kStages * (CD::kBytes + 8);
+    const size_t smem = codec_smem<CODEC>();
     cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     int sms = 0, per_sm = 0;
@@ -1010,21 +1063,15 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
     A.status = r->status_dev;
     switch (r->codec) {
         case QWN_KV_CODEC_Q8_HEAD_F16: {
-            using CD = Codec<QWN_KV_CODEC_Q8_HEAD_F16>;
-            attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16><<<ctas, kWarpsPerCta * 32,
-                kWarpsPerCta * CD::kStages * (CD::kBytes + 8), s>>>(A);
+            attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16><<<ctas, kWarpsPerCta * 32, codec_smem<QWN_KV_CODEC_Q8_HEAD_F16>(), s>>>(A);
             break;
         }
         case QWN_KV_CODEC_Q8_B64_F32: {
-            using CD = Codec<QWN_KV_CODEC_Q8_B64_F32>;
-            attn_kernel<QWN_KV_CODEC_Q8_B64_F32><<<ctas, kWarpsPerCta * 32,
-                kWarpsPerCta * CD::kStages * (CD::kBytes + 8), s>>>(A);
+            attn_kernel<QWN_KV_CODEC_Q8_B64_F32><<<ctas, kWarpsPerCta * 32, codec_smem<QWN_KV_CODEC_Q8_B64_F32>(), s>>>(A);
             break;
         }
         default: {
-            using CD = Codec<QWN_KV_CODEC_Q4_G32>;
-            attn_kernel<QWN_KV_CODEC_Q4_G32><<<ctas, kWarpsPerCta * 32,
-                kWarpsPerCta * CD::kStages * (CD::kBytes + 8), s>>>(A);
+            attn_kernel<QWN_KV_CODEC_Q4_G32><<<ctas, kWarpsPerCta * 32, codec_smem<QWN_KV_CODEC_Q4_G32>(), s>>>(A);
             break;
         }
     }

@@ -18,7 +18,7 @@ constexpr int kHeadDim = 128;
 constexpr int kTileTokens = 16;
 constexpr int kMaxGroup = 8;          // query heads per kv head handled by one warp
 constexpr int kWarpsPerCta = 4;       // attention CTA = 4 independent warps
-constexpr uint32_t kWaitLimit = 1u << 24;  // bounded mbarrier polls before giving up
+constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polls before giving up
 
 // ----------------------------------------------------------------------------
 // host-side error state and launch accounting
@@ -112,6 +112,8 @@ struct AttnLaunch {
     // partial mode (split-KV across devices)
     float *part_m, *part_l, *part_o;
     uint32_t t_begin, t_end;
+    // fused quantize-on-append of the newest token ([num_seqs][kv_heads][128])
+    const float *new_k, *new_v;
 };
 cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s);
 cudaError_t launch_merge(uint32_t parts, uint32_t rows, const float *m, const float *l,
