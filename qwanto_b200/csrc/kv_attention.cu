@@ -579,113 +579,166 @@ __device__ __noinline__ void fused_append(const float *new_k, const float *new_v
     __syncwarp();
 }
 
-// End of a warp's share of a segment: write the output, or a partial and
-// merge when this warp is the last to finish the segment.  Kept out of line
-// so the streaming loop keeps its registers.
-template <int CODEC>
-__device__ __forceinline__ void finish_segment(const AttnArgs &A, const typename Codec<CODEC>::Acc &acc, float m, float l,
-                                            uint32_t seg_i, uint32_t seg_h, uint64_t Us, uint64_t ns, uint64_t T,
-                                            uint64_t W, uint64_t wid) {
-    using CD = Codec<CODEC>;
-    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-    const uint32_t HK = A.kv_heads, G = A.group, Hq = HK * G;
-    struct { uint32_t i, h; } cons = {seg_i, seg_h};
-            const uint32_t s_idx = cons.i * HK + cons.h;
-            // warps whose (non-empty) range meets the segment: warp of unit u is
-            // ((u+1)W-1)/T.  With T >= W every warp between the first and the
-            // last is non-empty; with T < W each unit is a warp of its own.
-            const uint64_t wa = ((Us + 1) * W - 1) / T, wb = ((Us + ns) * W - 1) / T;
-            const uint32_t nparts = T >= W ? (uint32_t)(wb - wa + 1) : (uint32_t)ns;
-            auto part_warp = [&](uint32_t pp) -> uint64_t {
-                return T >= W ? wa + pp : ((Us + pp + 1) * W - 1) / T;
-            };
-            float lr = l;
-            lr += __shfl_xor_sync(0xffffffffu, lr, 1);
-            lr += __shfl_xor_sync(0xffffffffu, lr, 2);
-            float zs[4] = {0.f, 0.f, 0.f, 0.f};
-            if constexpr (CODEC == QWN_KV_CODEC_Q4_G32) {
+// Merge the nparts partial slots of segment s_idx into its output rows
+// (row0 = s_idx * G).  The slots were written by other warps, so every read
+// is an L2 round trip: (m, l) of part pp are read by lane pp % 32 and the o
+// rows of a chunk of 32 parts by all lanes, unrolled so that the loads are in
+// flight together rather than one latency per part.
+__device__ __forceinline__ void merge_segment(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
+                                              uint64_t T, uint64_t W) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t G = A.group;
+    const uint64_t wa = ((Us + 1) * W - 1) / T;
+    auto slot_of = [&](uint32_t pp) -> const float * {
+        const uint64_t w = T >= W ? wa + pp : ((Us + pp + 1) * W - 1) / T;
+        return A.partials + (size_t)(w + s_idx) * kPartialFloats;
+    };
+    auto load_ml = [&](uint32_t pp, float (&m)[kMaxGroup], float (&l)[kMaxGroup]) {
+        const float4 *p = reinterpret_cast<const float4 *>(slot_of(pp) + kMaxGroup * kHeadDim);
+        const float4 m0 = __ldcg(p), m1 = __ldcg(p + 1), l0 = __ldcg(p + 2), l1 = __ldcg(p + 3);
+        m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w; m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
+        l[0] = l0.x; l[1] = l0.y; l[2] = l0.z; l[3] = l0.w; l[4] = l1.x; l[5] = l1.y; l[6] = l1.z; l[7] = l1.w;
+    };
+    float ms[kMaxGroup];
 #pragma unroll
-                for (int g = 0; g < 4; g++) {
-                    float z = acc.z[g];
-                    z += __shfl_xor_sync(0xffffffffu, z, 1);
-                    z += __shfl_xor_sync(0xffffffffu, z, 2);
-                    zs[g] = z;
-                }
-            }
-            const size_t row0 = (size_t)cons.i * Hq + (size_t)cons.h * G;
-            if (nparts == 1) {
-                // this warp saw the whole segment: final output
-                if ((uint32_t)gid < G) {
-                    const size_t row = row0 + gid;
-                    if (A.part_o) {
-                        float *o = A.part_o + row * kHeadDim;
+    for (int g = 0; g < kMaxGroup; g++) ms[g] = -INFINITY;
+    for (uint32_t c = 0; c < nparts; c += 32) {
+        if (c + lane < nparts) {
+            float m[kMaxGroup], l[kMaxGroup];
+            load_ml(c + lane, m, l);
 #pragma unroll
-                        for (int jn = 0; jn < 16; jn++)
+            for (int g = 0; g < kMaxGroup; g++) ms[g] = fmaxf(ms[g], m[g]);
+        }
+    }
 #pragma unroll
-                            for (int cc = 0; cc < 2; cc++)
-                                o[CD::dim_of(jn, tig, cc)] = CD::out_value(acc, jn, cc, zs[jn >> 2]);
-                        if (tig == 0) { A.part_m[row] = m; A.part_l[row] = lr; }
-                    } else {
-                        const float inv = lr > 0.f ? 1.0f / lr : 0.f;
-                        float *o = A.output + row * kHeadDim;
+    for (int g = 0; g < kMaxGroup; g++)
 #pragma unroll
-                        for (int jn = 0; jn < 16; jn++)
+        for (int o = 16; o > 0; o >>= 1) ms[g] = fmaxf(ms[g], __shfl_xor_sync(0xffffffffu, ms[g], o));
+    float ls[kMaxGroup];
+    float4 acc[kMaxGroup];
 #pragma unroll
-                            for (int cc = 0; cc < 2; cc++)
-                                o[CD::dim_of(jn, tig, cc)] = CD::out_value(acc, jn, cc, zs[jn >> 2]) * inv;
-                    }
-                    if (A.seg_ml && tig == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + gid] = make_float2(m, lr);
-                }
-            } else {
-                float *slot = A.partials + (size_t)(wid + s_idx) * kPartialFloats;
-                if ((uint32_t)gid < G) {
+    for (int g = 0; g < kMaxGroup; g++) { ls[g] = 0.f; acc[g] = make_float4(0.f, 0.f, 0.f, 0.f); }
+    for (uint32_t c = 0; c < nparts; c += 32) {
+        float w[kMaxGroup];
 #pragma unroll
-                    for (int jn = 0; jn < 16; jn++)
+        for (int g = 0; g < kMaxGroup; g++) w[g] = 0.f;
+        if (c + lane < nparts) {
+            float m[kMaxGroup], l[kMaxGroup];
+            load_ml(c + lane, m, l);
 #pragma unroll
-                        for (int cc = 0; cc < 2; cc++)
-                            slot[gid * kHeadDim + CD::dim_of(jn, tig, cc)] = CD::out_value(acc, jn, cc, zs[jn >> 2]);
-                    if (tig == 0) {
-                        slot[kMaxGroup * kHeadDim + gid] = m;
-                        slot[kMaxGroup * kHeadDim + kMaxGroup + gid] = lr;
-                    }
-                }
-                __threadfence();
-                __syncwarp();
-                uint32_t old = 0;
-                if (lane == 0) old = atomicAdd(&A.counters[s_idx], 1u);
-                old = __shfl_sync(0xffffffffu, old, 0);
-                if (old == nparts - 1) {
-                    __threadfence();
-                    for (uint32_t g = 0; g < G; g++) {
-                        float ms = -INFINITY;
-                        for (uint32_t pp = 0; pp < nparts; pp++) {
-                            const float *sl = A.partials + (size_t)(part_warp(pp) + s_idx) * kPartialFloats;
-                            ms = fmaxf(ms, __ldcg(sl + kMaxGroup * kHeadDim + g));
-                        }
-                        float ls = 0.f;
-                        float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                        for (uint32_t pp = 0; pp < nparts; pp++) {
-                            const float *sl = A.partials + (size_t)(part_warp(pp) + s_idx) * kPartialFloats;
-                            const float wgt = ex2(__ldcg(sl + kMaxGroup * kHeadDim + g) - ms);
-                            ls += __ldcg(sl + kMaxGroup * kHeadDim + kMaxGroup + g) * wgt;
-                            const float4 v = __ldcg(reinterpret_cast<const float4 *>(sl + g * kHeadDim) + lane);
-                            o4.x += v.x * wgt; o4.y += v.y * wgt; o4.z += v.z * wgt; o4.w += v.w * wgt;
-                        }
-                        const size_t row = row0 + g;
-                        if (A.part_o) {
-                            reinterpret_cast<float4 *>(A.part_o + row * kHeadDim)[lane] = o4;
-                            if (lane == 0) { A.part_m[row] = ms; A.part_l[row] = ls; }
-                        } else {
-                            const float inv = ls > 0.f ? 1.0f / ls : 0.f;
-                            reinterpret_cast<float4 *>(A.output + row * kHeadDim)[lane] =
-                                make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
-                        }
-                        if (A.seg_ml && lane == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + g] = make_float2(ms, ls);
-                    }
-                    if (lane == 0) A.counters[s_idx] = 0u;
+            for (int g = 0; g < kMaxGroup; g++) {
+                if ((uint32_t)g < G) {  // slots hold only the group's rows
+                    w[g] = ex2(m[g] - ms[g]);
+                    ls[g] += l[g] * w[g];
                 }
             }
         }
+        const uint32_t nq = nparts - c < 32u ? nparts - c : 32u;
+#pragma unroll 4
+        for (uint32_t qq = 0; qq < nq; qq++) {
+            const float *sl = slot_of(c + qq);
+#pragma unroll
+            for (int g = 0; g < kMaxGroup; g++) {
+                const float wg = __shfl_sync(0xffffffffu, w[g], qq);
+                if ((uint32_t)g < G) {
+                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(sl + g * kHeadDim) + lane);
+                    acc[g].x += v.x * wg; acc[g].y += v.y * wg; acc[g].z += v.z * wg; acc[g].w += v.w * wg;
+                }
+            }
+        }
+    }
+    const size_t row0 = (size_t)s_idx * G;
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; g++) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ls[g] += __shfl_xor_sync(0xffffffffu, ls[g], o);
+        if ((uint32_t)g >= G) continue;
+        const size_t row = row0 + g;
+        if (A.part_o) {
+            reinterpret_cast<float4 *>(A.part_o + row * kHeadDim)[lane] = acc[g];
+            if (lane == 0) { A.part_m[row] = ms[g]; A.part_l[row] = ls[g]; }
+        } else {
+            const float inv = ls[g] > 0.f ? 1.0f / ls[g] : 0.f;
+            reinterpret_cast<float4 *>(A.output + row * kHeadDim)[lane] =
+                make_float4(acc[g].x * inv, acc[g].y * inv, acc[g].z * inv, acc[g].w * inv);
+        }
+        if (A.seg_ml && lane == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + g] = make_float2(ms[g], ls[g]);
+    }
+    if (lane == 0) A.counters[s_idx] = 0u;  // ready for the next launch
+}
+
+// End of a warp's share of segment s_idx (batch entry i, kv head h, first
+// unit Us, ns units).  A warp that saw the whole segment writes the output;
+// otherwise it writes its partial (m, l, o) to slot wid + s_idx and counts
+// itself on the segment's counter.  Returns the number of parts when this
+// warp arrived last and must merge them, else 0.  The merge itself runs after
+// the warp's streaming loop, where the loop's registers are free.
+template <int CODEC>
+__device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const typename Codec<CODEC>::Acc &acc,
+                                                   float m, float l, uint32_t s_idx, uint64_t Us, uint64_t ns,
+                                                   uint64_t T, uint64_t W, uint64_t wid) {
+    using CD = Codec<CODEC>;
+    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const uint32_t G = A.group;
+    // warps whose (non-empty) range meets the segment: warp of unit u is
+    // ((u+1)W-1)/T.  With T >= W every warp between the first and the last
+    // is non-empty; with T < W each unit is a warp of its own.
+    const uint64_t wa = ((Us + 1) * W - 1) / T, wb = ((Us + ns) * W - 1) / T;
+    const uint32_t nparts = T >= W ? (uint32_t)(wb - wa + 1) : (uint32_t)ns;
+    float lr = l;
+    lr += __shfl_xor_sync(0xffffffffu, lr, 1);
+    lr += __shfl_xor_sync(0xffffffffu, lr, 2);
+    float zs[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (CODEC == QWN_KV_CODEC_Q4_G32) {
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            float z = acc.z[g];
+            z += __shfl_xor_sync(0xffffffffu, z, 1);
+            z += __shfl_xor_sync(0xffffffffu, z, 2);
+            zs[g] = z;
+        }
+    }
+    const size_t row = (size_t)s_idx * G + gid;
+    if (nparts == 1) {
+        if ((uint32_t)gid < G) {
+            if (A.part_o) {
+                float *o = A.part_o + row * kHeadDim;
+#pragma unroll
+                for (int jn = 0; jn < 16; jn++)
+                    *reinterpret_cast<float2 *>(o + CD::dim_of(jn, tig, 0)) =
+                        make_float2(CD::out_value(acc, jn, 0, zs[jn >> 2]), CD::out_value(acc, jn, 1, zs[jn >> 2]));
+                if (tig == 0) { A.part_m[row] = m; A.part_l[row] = lr; }
+            } else {
+                const float inv = lr > 0.f ? 1.0f / lr : 0.f;
+                float *o = A.output + row * kHeadDim;
+#pragma unroll
+                for (int jn = 0; jn < 16; jn++)
+                    *reinterpret_cast<float2 *>(o + CD::dim_of(jn, tig, 0)) =
+                        make_float2(CD::out_value(acc, jn, 0, zs[jn >> 2]) * inv,
+                                    CD::out_value(acc, jn, 1, zs[jn >> 2]) * inv);
+            }
+            if (A.seg_ml && tig == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + gid] = make_float2(m, lr);
+        }
+        return 0;
+    }
+    float *slot = A.partials + (size_t)(wid + s_idx) * kPartialFloats;
+    if ((uint32_t)gid < G) {
+#pragma unroll
+        for (int jn = 0; jn < 16; jn++)
+            *reinterpret_cast<float2 *>(slot + gid * kHeadDim + CD::dim_of(jn, tig, 0)) =
+                make_float2(CD::out_value(acc, jn, 0, zs[jn >> 2]), CD::out_value(acc, jn, 1, zs[jn >> 2]));
+        if (tig == 0) {
+            slot[kMaxGroup * kHeadDim + gid] = m;
+            slot[kMaxGroup * kHeadDim + kMaxGroup + gid] = lr;
+        }
+    }
+    __threadfence();
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(&A.counters[s_idx], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    return old == nparts - 1 ? nparts : 0u;
+}
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -766,6 +819,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
     typename CD::Acc acc;
     float m = -INFINITY, l = 0.f;
     uint32_t st = 0, par = 0;
+    // merges this warp owes (it arrived last at a shared segment), run after the loop
+    uint32_t pend_n = 0, pend_s0 = 0, pend_n0 = 0, pend_s1 = 0, pend_n1 = 0;
+    uint64_t pend_u0 = 0, pend_u1 = 0;
 
     for (uint32_t k = 0; k < n; ++k) {
         if (cons.tile == 0 || k == 0) {
@@ -817,12 +873,23 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         if (++st == (uint32_t)S) { st = 0; par ^= 1u; }
 
         // end of this warp's share of the segment?
-        if (cons.tile + 1 == cons.geo.ntiles || k + 1 == n)
-            finish_segment<CODEC>(A, acc, m, l, cons.i, cons.h, cons.seg_base, cons.geo.ntiles, T, W, wid);
+        if (cons.tile + 1 == cons.geo.ntiles || k + 1 == n) {
+            const uint32_t s_idx = cons.i * HK + cons.h;
+            const uint32_t np = finish_segment<CODEC>(A, acc, m, l, s_idx, cons.seg_base, cons.geo.ntiles, T, W, wid);
+            if (np) {
+                const int e = pend_n++;  // at most two: the segment the range starts in and the one it ends in
+                if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.seg_base; }
+                else { pend_s1 = s_idx; pend_n1 = np; pend_u1 = cons.seg_base; }
+            }
+        }
         // next unit
         if (k + 1 < n) {
             if (++cons.tile == cons.geo.ntiles) walk_next_segment(A, cons);
         }
+    }
+    for (uint32_t e = 0; e < pend_n; e++) {
+        __threadfence();
+        merge_segment(A, e ? pend_s1 : pend_s0, e ? pend_n1 : pend_n0, e ? pend_u1 : pend_u0, T, W);
     }
 }
 
