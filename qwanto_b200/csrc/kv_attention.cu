@@ -581,11 +581,14 @@ __device__ __noinline__ void fused_append(const float *new_k, const float *new_v
 
 // Merge the nparts partial slots of segment s_idx into its output rows
 // (row0 = s_idx * G).  The slots were written by other warps, so every read
-// is an L2 round trip: (m, l) of part pp are read by lane pp % 32 and the o
-// rows of a chunk of 32 parts by all lanes, unrolled so that the loads are in
-// flight together rather than one latency per part.
-__device__ __forceinline__ void merge_segment(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
-                                              uint64_t T, uint64_t W) {
+// is an L2 round trip; they are batched so that a handful of round trips
+// cover a segment: lane pp % 32 reads (m, l) of part pp while all lanes
+// already load the o rows of the first kBatch parts, and the remaining parts
+// follow kBatch at a time.  GG >= G is the compile-time row count.
+template <int GG>
+__device__ __forceinline__ void merge_rows(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
+                                           uint64_t T, uint64_t W) {
+    constexpr int kBatch = 16 / GG;  // float4 loads in flight per lane
     const int lane = threadIdx.x & 31;
     const uint32_t G = A.group;
     const uint64_t wa = ((Us + 1) * W - 1) / T;
@@ -593,78 +596,86 @@ __device__ __forceinline__ void merge_segment(const AttnArgs &A, uint32_t s_idx,
         const uint64_t w = T >= W ? wa + pp : ((Us + pp + 1) * W - 1) / T;
         return A.partials + (size_t)(w + s_idx) * kPartialFloats;
     };
-    auto load_ml = [&](uint32_t pp, float (&m)[kMaxGroup], float (&l)[kMaxGroup]) {
-        const float4 *p = reinterpret_cast<const float4 *>(slot_of(pp) + kMaxGroup * kHeadDim);
-        const float4 m0 = __ldcg(p), m1 = __ldcg(p + 1), l0 = __ldcg(p + 2), l1 = __ldcg(p + 3);
-        m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w; m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
-        l[0] = l0.x; l[1] = l0.y; l[2] = l0.z; l[3] = l0.w; l[4] = l1.x; l[5] = l1.y; l[6] = l1.z; l[7] = l1.w;
-    };
-    float ms[kMaxGroup];
+    float M[GG], ls[GG];
+    float4 acc[GG];
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; g++) ms[g] = -INFINITY;
+    for (int g = 0; g < GG; g++) { M[g] = -INFINITY; ls[g] = 0.f; acc[g] = make_float4(0.f, 0.f, 0.f, 0.f); }
     for (uint32_t c = 0; c < nparts; c += 32) {
-        if (c + lane < nparts) {
-            float m[kMaxGroup], l[kMaxGroup];
-            load_ml(c + lane, m, l);
-#pragma unroll
-            for (int g = 0; g < kMaxGroup; g++) ms[g] = fmaxf(ms[g], m[g]);
-        }
-    }
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; g++)
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ms[g] = fmaxf(ms[g], __shfl_xor_sync(0xffffffffu, ms[g], o));
-    float ls[kMaxGroup];
-    float4 acc[kMaxGroup];
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; g++) { ls[g] = 0.f; acc[g] = make_float4(0.f, 0.f, 0.f, 0.f); }
-    for (uint32_t c = 0; c < nparts; c += 32) {
-        float w[kMaxGroup];
-#pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) w[g] = 0.f;
-        if (c + lane < nparts) {
-            float m[kMaxGroup], l[kMaxGroup];
-            load_ml(c + lane, m, l);
-#pragma unroll
-            for (int g = 0; g < kMaxGroup; g++) {
-                if ((uint32_t)g < G) {  // slots hold only the group's rows
-                    w[g] = ex2(m[g] - ms[g]);
-                    ls[g] += l[g] * w[g];
-                }
-            }
-        }
         const uint32_t nq = nparts - c < 32u ? nparts - c : 32u;
-#pragma unroll 4
-        for (uint32_t qq = 0; qq < nq; qq++) {
-            const float *sl = slot_of(c + qq);
+        float m[GG], l[GG];
 #pragma unroll
-            for (int g = 0; g < kMaxGroup; g++) {
-                const float wg = __shfl_sync(0xffffffffu, w[g], qq);
-                if ((uint32_t)g < G) {
-                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(sl + g * kHeadDim) + lane);
-                    acc[g].x += v.x * wg; acc[g].y += v.y * wg; acc[g].z += v.z * wg; acc[g].w += v.w * wg;
+        for (int g = 0; g < GG; g++) { m[g] = -INFINITY; l[g] = 0.f; }
+        if ((uint32_t)lane < nq) {
+            const float *ml = slot_of(c + lane) + kMaxGroup * kHeadDim;
+#pragma unroll
+            for (int g = 0; g < GG; g++)
+                if ((uint32_t)g < G) { m[g] = __ldcg(ml + g); l[g] = __ldcg(ml + kMaxGroup + g); }
+        }
+        float4 v[kBatch][GG];
+        auto load_batch = [&](uint32_t q0) {
+#pragma unroll
+            for (int b = 0; b < kBatch; b++) {
+                const float *sl = slot_of(c + q0 + b);
+#pragma unroll
+                for (int g = 0; g < GG; g++)
+                    v[b][g] = (q0 + b < nq && (uint32_t)g < G)
+                                  ? __ldcg(reinterpret_cast<const float4 *>(sl + g * kHeadDim) + lane)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        };
+        load_batch(0);
+        float w[GG];
+#pragma unroll
+        for (int g = 0; g < GG; g++) {
+            float cm = m[g];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+            const float nm = fmaxf(M[g], cm);
+            const float alpha = M[g] == -INFINITY ? 0.f : ex2(M[g] - nm);
+            M[g] = nm;
+            ls[g] *= alpha;
+            acc[g].x *= alpha; acc[g].y *= alpha; acc[g].z *= alpha; acc[g].w *= alpha;
+            w[g] = (uint32_t)lane < nq && (uint32_t)g < G ? ex2(m[g] - nm) : 0.f;
+            ls[g] += l[g] * w[g];
+        }
+        for (uint32_t q0 = 0; q0 < nq; q0 += kBatch) {
+            if (q0) load_batch(q0);
+#pragma unroll
+            for (int b = 0; b < kBatch; b++) {
+#pragma unroll
+                for (int g = 0; g < GG; g++) {
+                    const float wg = __shfl_sync(0xffffffffu, w[g], (q0 + b) & 31);
+                    acc[g].x += v[b][g].x * wg; acc[g].y += v[b][g].y * wg;
+                    acc[g].z += v[b][g].z * wg; acc[g].w += v[b][g].w * wg;
                 }
             }
         }
     }
     const size_t row0 = (size_t)s_idx * G;
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; g++) {
+    for (int g = 0; g < GG; g++) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ls[g] += __shfl_xor_sync(0xffffffffu, ls[g], o);
         if ((uint32_t)g >= G) continue;
         const size_t row = row0 + g;
         if (A.part_o) {
             reinterpret_cast<float4 *>(A.part_o + row * kHeadDim)[lane] = acc[g];
-            if (lane == 0) { A.part_m[row] = ms[g]; A.part_l[row] = ls[g]; }
+            if (lane == 0) { A.part_m[row] = M[g]; A.part_l[row] = ls[g]; }
         } else {
             const float inv = ls[g] > 0.f ? 1.0f / ls[g] : 0.f;
             reinterpret_cast<float4 *>(A.output + row * kHeadDim)[lane] =
                 make_float4(acc[g].x * inv, acc[g].y * inv, acc[g].z * inv, acc[g].w * inv);
         }
-        if (A.seg_ml && lane == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + g] = make_float2(ms[g], ls[g]);
+        if (A.seg_ml && lane == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + g] = make_float2(M[g], ls[g]);
     }
     if (lane == 0) A.counters[s_idx] = 0u;  // ready for the next launch
+}
+
+__device__ __forceinline__ void merge_segment(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
+                                              uint64_t T, uint64_t W) {
+    if (A.group <= 2) merge_rows<2>(A, s_idx, nparts, Us, T, W);
+    else if (A.group <= 4) merge_rows<4>(A, s_idx, nparts, Us, T, W);
+    else merge_rows<8>(A, s_idx, nparts, Us, T, W);
 }
 
 // End of a warp's share of segment s_idx (batch entry i, kv head h, first
@@ -732,11 +743,13 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
             slot[kMaxGroup * kHeadDim + kMaxGroup + gid] = lr;
         }
     }
-    __threadfence();
+    // the warp barrier orders the lanes' slot stores before lane 0's release;
+    // the acquire side orders the last arriver's reads of the other slots
     __syncwarp();
     uint32_t old = 0;
-    if (lane == 0) old = atomicAdd(&A.counters[s_idx], 1u);
+    if (lane == 0) old = atom_add_acq_rel_gpu(&A.counters[s_idx], 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
+    __syncwarp();
     return old == nparts - 1 ? nparts : 0u;
 }
 
@@ -888,7 +901,6 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         }
     }
     for (uint32_t e = 0; e < pend_n; e++) {
-        __threadfence();
         merge_segment(A, e ? pend_s1 : pend_s0, e ? pend_n1 : pend_n0, e ? pend_u1 : pend_u0, T, W);
     }
 }

@@ -210,6 +210,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 // 1-D bulk copy global -> shared, completion counted on an mbarrier (no multicast)
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
                                          uint64_t *bar) {
