@@ -291,11 +291,18 @@ void qor_q4g32_quantize(const float *src, int n, uint8_t *codes, uint16_t *range
  * A tile holds 16 tokens of one (page, layer, kv head).  Byte positions are
  * chosen so that each lane of a warp loads its mma.sync fragments with a few
  * 128-bit shared-memory loads and no bank conflicts:
- *  - int8 K, token t, dim d: half h=(t>>1)&1, column n=2*(t>>2)+(t&1),
- *    lane n*4+((d>>4)&3), 16-byte half (d>>6) xor (n&1), byte d&15;
- *    stored biased (code + 128).
- *  - int8 V, token t, dim d: lane (d&7)*4+(t>>2), 16-byte chunk
- *    ((d>>5)) xor ((lane>>1)&3), word (d>>3)&3, byte t&3; biased.
+ *  - int8 K (bytes 0..2047), token t, dim d: row t of 128 bytes (the A
+ *    operand rows of the integer QK^T product), 16-byte chunk (d>>4) stored
+ *    at position (d>>4) xor ((t&1)<<2), byte d&15; stored biased (code+128).
+ *  - int8 V (bytes 2048..4095), token t, dim d: m-block mb=d>>4, row
+ *    r=d&15, lane ((r&7)<<2)|((t&7)>>1); the lane's 64 bytes hold 8 bytes
+ *    per m-block, 16-byte chunk (mb>>1) stored at position
+ *    (mb>>1) xor ((lane>>1)&3), byte 8*(mb&1) + 4*(t>>3) + 2*(r>>3) + (t&1):
+ *    the A operand (dims x tokens) of the PV product; biased.
+ *  - int8 scales: tokens t and t+8 adjacent.  Q8_HEAD: fp16 K scale at
+ *    4096 + 4*(t&7) + 2*(t>>3), V scale at 4128 + same.  Q8_B64: fp32 K
+ *    scale of channel block x at 4096 + 16*(t&7) + 8*x + 4*(t>>3), V at
+ *    4224 + same.
  *  - 4-bit K: lane n*4+tig, word g=d>>5 in the lane's 16 bytes, nibble
  *    position (i&1)*4+e*2+(i>>1) with e=(d>>4)&1, tig=(d>>2)&3, i=d&3.
  *  - 4-bit V: lane (d&7)*4+(t>>2), word w=d>>4 (16-byte chunk (w>>2) xor
@@ -313,16 +320,19 @@ size_t qor_tile_bytes(int codec) {
 }
 
 static size_t k8_off(int t, int d) {
-    int h = (t >> 1) & 1, n = 2 * (t >> 2) + (t & 1), tig = (d >> 4) & 3, x = d >> 6;
-    int lane = n * 4 + tig;
-    return (size_t)h * 1024 + (size_t)lane * 32 + (size_t)((x ^ (n & 1)) << 4) + (size_t)(d & 15);
+    return (size_t)t * 128 + (size_t)(((d >> 4) ^ ((t & 1) << 2)) << 4) + (size_t)(d & 15);
 }
 
 static size_t v8_off(int t, int d) {
-    int gid = d & 7, j = d >> 3, tig = t >> 2, b = t & 3, lane = gid * 4 + tig, q = j >> 2;
-    return 2048 + (size_t)lane * 64 + (size_t)((q ^ ((lane >> 1) & 3)) << 4) +
-           (size_t)((j & 3) << 2) + (size_t)b;
+    int mb = d >> 4, r = d & 15, lane = ((r & 7) << 2) | ((t & 7) >> 1);
+    int chunk = (mb >> 1) ^ ((lane >> 1) & 3);
+    int e = 4 * (t >> 3) + 2 * (r >> 3) + (t & 1);
+    return 2048 + (size_t)lane * 64 + (size_t)chunk * 16 + (size_t)(8 * (mb & 1) + e);
 }
+
+/* int8 scale positions (see the layout notes above) */
+static size_t s16_off(int t) { return (size_t)(4 * (t & 7) + 2 * (t >> 3)); }
+static size_t s32_off(int t, int x) { return (size_t)(16 * (t & 7) + 8 * x + 4 * (t >> 3)); }
 
 /* nibble address: byte offset and high(1)/low(0) nibble */
 static void k4_pos(int t, int d, size_t *byte, int *hi) {
@@ -486,15 +496,15 @@ void qor_tile_store(int codec, uint8_t *tile, int t, const float *k, const float
             qor_q8_b64_quantize(k, HD, ck, sk);
             qor_q8_b64_quantize(v, HD, cv, sv);
             for (int x = 0; x < 2; x++) {
-                put_f32(tile + 4096 + x * 64 + t * 4, sk[x]);
-                put_f32(tile + 4224 + x * 64 + t * 4, sv[x]);
+                put_f32(tile + 4096 + s32_off(t, x), sk[x]);
+                put_f32(tile + 4224 + s32_off(t, x), sv[x]);
             }
         } else {
             uint16_t sk, sv;
             qor_q8_head_quantize(k, HD, ck, &sk);
             qor_q8_head_quantize(v, HD, cv, &sv);
-            put_u16(tile + 4096 + t * 2, sk);
-            put_u16(tile + 4128 + t * 2, sv);
+            put_u16(tile + 4096 + s16_off(t), sk);
+            put_u16(tile + 4128 + s16_off(t), sv);
         }
         for (int d = 0; d < HD; d++) {
             tile[k8_off(t, d)] = (uint8_t)((int)ck[d] + 128);
@@ -545,9 +555,9 @@ void qor_tile_load(int codec, const uint8_t *tile, int t, int is_value, int16_t 
             codes[d] = (int16_t)((int)tile[is_value ? v8_off(t, d) : k8_off(t, d)] - 128);
         if (codec == QOR_CODEC_Q8_B64_F32) {
             for (int x = 0; x < 2; x++)
-                params[x] = get_f32(tile + (is_value ? 4224 : 4096) + x * 64 + t * 4);
+                params[x] = get_f32(tile + (is_value ? 4224 : 4096) + s32_off(t, x));
         } else {
-            params[0] = qor_f16_to_f32(get_u16(tile + (is_value ? 4128 : 4096) + t * 2));
+            params[0] = qor_f16_to_f32(get_u16(tile + (is_value ? 4128 : 4096) + s16_off(t)));
         }
     } else if (codec == QOR_CODEC_Q4_G32) {
         for (int d = 0; d < HD; d++) {

@@ -130,181 +130,6 @@ __device__ __forceinline__ void update_nu(const float (&vs)[4], int x, Acc &acc)
 // ---------------------------------------------------------------------------
 template <int CODEC> struct Codec;
 
-// int8 codes, per-token-head fp16 scale (4160-byte tile)
-template <> struct Codec<QWN_KV_CODEC_Q8_HEAD_F16> {
-    static constexpr int kBytes = 4160, kStages = 4, kNu = 1;
-    struct Frag { uint32_t a[8][4]; };
-    struct Acc {
-        float o[16][4];
-        float nu[kNu], inv_nu[kNu];
-        __device__ void reset() {
-#pragma unroll
-            for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-            nu[0] = 0.f; inv_nu[0] = 0.f;
-        }
-        __device__ void rescale_all(float f) {
-#pragma unroll
-            for (int j = 0; j < 16; j++) { o[j][0] *= f; o[j][1] *= f; o[j][2] *= f; o[j][3] *= f; }
-        }
-        __device__ void rescale_part(int, float f) { rescale_all(f); }
-    };
-    __device__ static int dim_of(int j, int tig, int c) { return 8 * j + 2 * tig + c; }
-    // k-step s covers dims 64(s>>2) + 16tig + 4(s&3) + {0,1 | 2,3}
-    __device__ static void load_q(Frag &f, const float *q, int tig) {
-#pragma unroll
-        for (int s = 0; s < 8; s++) {
-            float v[4] = {0.f, 0.f, 0.f, 0.f};
-            if (q) {
-                const float4 x = *reinterpret_cast<const float4 *>(q + 64 * (s >> 2) + 16 * tig + 4 * (s & 3));
-                v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-            }
-            make_a(v, f.a[s]);
-        }
-    }
-    __device__ static float out_value(const Acc &acc, int j, int c, float) {
-        return (acc.o[j][c] + acc.o[j][c + 2]) * acc.nu[0];
-    }
-    // K: per half h (token columns), two accumulator chains (even / odd
-    // k-steps) so consecutive MMAs are independent
-    __device__ static void qk(const uint8_t *tile, const Frag &f, float (&raw)[4]) {
-        const int lane = threadIdx.x & 31, sw = (lane >> 2) & 1;
-        const uint2 ksr = *reinterpret_cast<const uint2 *>(tile + 4096 + 8 * (lane & 3));
-        const float2 k01 = h2x2f(ksr.x), k23 = h2x2f(ksr.y);
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint4 *kp = reinterpret_cast<const uint4 *>(tile + h * 1024 + lane * 32);
-            const uint4 x0 = kp[sw], x1 = kp[sw ^ 1];
-            const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int st = 0; st < 8; st += 2) {
-                uint32_t b0, b1;
-                u8x4_to_h2x2(w[st], b0, b1);
-                mma16816(ce, f.a[st], b0, b1);
-                u8x4_to_h2x2(w[st + 1], b0, b1);
-                mma16816(co, f.a[st + 1], b0, b1);
-            }
-            const float sa = h ? k23.x : k01.x, sb = h ? k23.y : k01.y;
-            raw[2 * h] = ((ce[0] + co[0]) + (ce[2] + co[2])) * sa;
-            raw[2 * h + 1] = ((ce[1] + co[1]) + (ce[3] + co[3])) * sb;
-        }
-    }
-    __device__ static void pv(const uint8_t *tile, Acc &acc, const float (&p)[4], const bool (&ok)[4]) {
-        const int lane = threadIdx.x & 31, tig = lane & 3;
-        const uint2 vsr = *reinterpret_cast<const uint2 *>(tile + 4128 + 8 * tig);
-        const float2 v01 = h2x2f(vsr.x), v23 = h2x2f(vsr.y);
-        float vs[4] = {v01.x, v01.y, v23.x, v23.y};
-#pragma unroll
-        for (int i = 0; i < 4; i++) vs[i] = ok[i] ? vs[i] : 0.f;
-        update_nu(vs, 0, acc);
-        float pt[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) pt[i] = p[i] * vs[i] * acc.inv_nu[0];
-        uint32_t a[4];
-        make_a(pt, a);
-        const uint8_t *vt = tile + 2048 + lane * 64;
-        const int sw = (lane >> 1) & 3;
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(vt + ((q ^ sw) << 4));
-            const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                uint32_t b0, b1;
-                u8x4_to_h2x2(wv[r], b0, b1);
-                mma16816(acc.o[4 * q + r], a, b0, b1);
-            }
-        }
-    }
-};
-
-// int8 codes, fp32 scale per 64 channels: the reference Q8 (4352-byte tile)
-template <> struct Codec<QWN_KV_CODEC_Q8_B64_F32> {
-    static constexpr int kBytes = 4352, kStages = 4, kNu = 2;
-    using Frag = Codec<QWN_KV_CODEC_Q8_HEAD_F16>::Frag;
-    struct Acc {
-        float o[16][4];
-        float nu[kNu], inv_nu[kNu];
-        __device__ void reset() {
-#pragma unroll
-            for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-            nu[0] = nu[1] = 0.f; inv_nu[0] = inv_nu[1] = 0.f;
-        }
-        __device__ void rescale_all(float f) {
-#pragma unroll
-            for (int j = 0; j < 16; j++) { o[j][0] *= f; o[j][1] *= f; o[j][2] *= f; o[j][3] *= f; }
-        }
-        __device__ void rescale_part(int x, float f) {
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const int jj = 8 * x + j;
-                o[jj][0] *= f; o[jj][1] *= f; o[jj][2] *= f; o[jj][3] *= f;
-            }
-        }
-    };
-    __device__ static int dim_of(int j, int tig, int c) { return 8 * j + 2 * tig + c; }
-    __device__ static void load_q(Frag &f, const float *q, int tig) {
-        Codec<QWN_KV_CODEC_Q8_HEAD_F16>::load_q(f, q, tig);
-    }
-    __device__ static float out_value(const Acc &acc, int j, int c, float) {
-        return (acc.o[j][c] + acc.o[j][c + 2]) * acc.nu[j >> 3];
-    }
-    // k-steps 0-3 cover dims 0..63 (scale 0), 4-7 dims 64..127 (scale 1)
-    __device__ static void qk(const uint8_t *tile, const Frag &f, float (&raw)[4]) {
-        const int lane = threadIdx.x & 31, sw = (lane >> 2) & 1, tig = lane & 3;
-        const float4 ka = *reinterpret_cast<const float4 *>(tile + 4096 + 16 * tig);
-        const float4 kb = *reinterpret_cast<const float4 *>(tile + 4096 + 64 + 16 * tig);
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint4 *kp = reinterpret_cast<const uint4 *>(tile + h * 1024 + lane * 32);
-            const uint4 x0 = kp[sw], x1 = kp[sw ^ 1];
-            const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int st = 0; st < 4; st++) {
-                uint32_t b0, b1;
-                u8x4_to_h2x2(w[st], b0, b1);
-                mma16816(ca, f.a[st], b0, b1);
-                u8x4_to_h2x2(w[st + 4], b0, b1);
-                mma16816(cb, f.a[st + 4], b0, b1);
-            }
-            const float sa0 = h ? ka.z : ka.x, sa1 = h ? ka.w : ka.y;
-            const float sb0 = h ? kb.z : kb.x, sb1 = h ? kb.w : kb.y;
-            raw[2 * h] = (ca[0] + ca[2]) * sa0 + (cb[0] + cb[2]) * sb0;
-            raw[2 * h + 1] = (ca[1] + ca[3]) * sa1 + (cb[1] + cb[3]) * sb1;
-        }
-    }
-    __device__ static void pv(const uint8_t *tile, Acc &acc, const float (&p)[4], const bool (&ok)[4]) {
-        const int lane = threadIdx.x & 31, tig = lane & 3;
-        uint32_t a[2][4];
-#pragma unroll
-        for (int x = 0; x < 2; x++) {
-            const float4 v4 = *reinterpret_cast<const float4 *>(tile + 4224 + 64 * x + 16 * tig);
-            float vs[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++) vs[i] = ok[i] ? vs[i] : 0.f;
-            update_nu(vs, x, acc);
-            float pt[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) pt[i] = p[i] * vs[i] * acc.inv_nu[x];
-            make_a(pt, a[x]);
-        }
-        const uint8_t *vt = tile + 2048 + lane * 64;
-        const int sw = (lane >> 1) & 3;
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(vt + ((q ^ sw) << 4));
-            const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                uint32_t b0, b1;
-                u8x4_to_h2x2(wv[r], b0, b1);
-                mma16816(acc.o[4 * q + r], a[q >> 1], b0, b1);
-            }
-        }
-    }
-};
-
 // 4-bit codes, groups of 32 with fp16 range + fp16 min (2560-byte tile)
 template <> struct Codec<QWN_KV_CODEC_Q4_G32> {
     static constexpr int kBytes = 2560, kStages = 6, kNu = 4;
@@ -450,6 +275,410 @@ __device__ __forceinline__ float tile_step(const uint8_t *tile, const typename C
     CD::pv(tile, acc, p, ok);
     return (p[0] + p[1]) + (p[2] + p[3]);
 }
+
+// ---------------------------------------------------------------------------
+// int8 codecs (Q8_HEAD_F16, Q8_B64_F32): products with the tile as the A
+// operand.  The query heads of the GQA group fill the N columns, so one
+// m16n8 product covers 16 tokens x 4 heads:
+//  * QK^T on the integer tensor cores (m16n8k32 u8 x s8 -> s32): the K codes
+//    (stored biased, 1..255) are used as they are; each query row is split
+//    into four int8 slices q = s0*c0 + s1*c1 + s2*c2 + s3*c3 (s_{j+1} =
+//    s_j/254, residual below 2^-31 of max|q|), columns (head, slice).  The
+//    sums are exact integers; 128*sum(c_j) removes the code bias, and the
+//    slices recombine in fp32 with the token's K scale.
+//  * P x V on the f16 tensor cores with V^T as the A operand (dims x
+//    tokens) and P^T (tokens x (head, hi/lo)) as B: the probabilities of a
+//    lane's two tokens become f16 hi+lo pairs, and movmatrix transposes them
+//    into the B fragment.  V codes become exact f16 by byte permutes; the
+//    V scale is folded into P with the power-of-two normaliser nu.
+// HG head groups of 4 (G <= 4: HG = 1; G <= 8: HG = 2).
+// Lane (gid, tig): scores of tokens gid and gid+8 for head 4*hg + tig.
+// ---------------------------------------------------------------------------
+template <int CODEC, int HG>
+struct Int8T {
+    static constexpr bool kB64 = CODEC == QWN_KV_CODEC_Q8_B64_F32;
+    static constexpr int kX = kB64 ? 2 : 1;  // scale groups along head_dim
+    static constexpr int kBytes = kB64 ? 4352 : 4160, kStages = 4;
+    struct Frag {
+        uint32_t b[HG][2][4][2];   // IMMA B: [head group][n-block][k-block][reg]
+        uint32_t magic[HG][kX][4]; // per (scale group, slice) of this lane's head
+        float sc[HG][4];           // slice scale x log2(e) x softmax scale
+    };
+    struct State {
+        float o[HG][8][4];  // (dims x (head, hi/lo)) accumulators per m-block
+        float m[HG], l[HG];
+        float nu[kX], inv_nu[kX];
+    };
+
+    // dims of the lane's 32 query values: 16*tig + i (i < 16), 64 + 16*tig + i-16
+    __device__ static void begin(Frag &f, State &st, const AttnArgs &A, uint32_t s_idx) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        const uint32_t G = A.group;
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            const uint32_t hq = 4 * hg + (gid >> 1);
+            float v[32];
+            if (hq < G) {
+                const float *q = A.query + ((size_t)s_idx * G + hq) * kHeadDim;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    const float4 x = *reinterpret_cast<const float4 *>(q + (c >> 2) * 64 + 16 * tig + 4 * (c & 3));
+                    v[4 * c] = x.x; v[4 * c + 1] = x.y; v[4 * c + 2] = x.z; v[4 * c + 3] = x.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) v[i] = 0.f;
+            }
+            float mx = 0.f;
+            int bad = 0;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                if (isfinite(v[i])) mx = fmaxf(mx, fabsf(v[i]));
+                else bad = 1;
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
+            bad |= __shfl_xor_sync(0xffffffffu, bad, 2);
+            float s = mx > 0.f ? mx / 127.0f : 1.0f;
+            const float s0 = s;
+            int colsum[2][kX];  // this lane's column (slice 2nb + (gid&1)), per scale group
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float inv = 1.0f / s;
+                uint32_t packed[8];
+                int sum[kX];
+#pragma unroll
+                for (int x = 0; x < kX; x++) sum[x] = 0;
+#pragma unroll
+                for (int w = 0; w < 8; w++) {
+                    uint32_t word = 0;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int i = 4 * w + e;
+                        const float c = fminf(fmaxf(rintf(v[i] * inv), -127.f), 127.f);
+                        v[i] = fmaf(-c, s, v[i]);
+                        const int ci = (int)c;
+                        sum[kB64 ? (i >> 4) : 0] += ci;
+                        word |= ((uint32_t)ci & 0xFFu) << (8 * e);
+                    }
+                    packed[w] = word;
+                }
+                if ((j & 1) == (gid & 1)) {
+#pragma unroll
+                    for (int kb = 0; kb < 4; kb++) {
+                        const int base = 4 * (kb >> 1) + 2 * (kb & 1);  // word index of dims base..base+7
+                        f.b[hg][j >> 1][kb][0] = packed[base];
+                        f.b[hg][j >> 1][kb][1] = packed[base + 1];
+                    }
+#pragma unroll
+                    for (int x = 0; x < kX; x++) colsum[j >> 1][x] = sum[x];
+                }
+                s = s / 254.0f;
+            }
+            // column sums over the head's 128 dims (the four tig lanes)
+#pragma unroll
+            for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+                for (int x = 0; x < kX; x++) {
+                    colsum[nb][x] += __shfl_xor_sync(0xffffffffu, colsum[nb][x], 1);
+                    colsum[nb][x] += __shfl_xor_sync(0xffffffffu, colsum[nb][x], 2);
+                }
+            // C side: columns 2tig (slice 2nb) and 2tig+1 (slice 2nb+1) of head
+            // 4hg+tig come from the lanes with gid = 2tig + e
+#pragma unroll
+            for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+                for (int e = 0; e < 2; e++)
+#pragma unroll
+                    for (int x = 0; x < kX; x++) {
+                        const int cs = __shfl_sync(0xffffffffu, colsum[nb][x], 8 * tig + 4 * e);
+                        f.magic[hg][x][2 * nb + e] = 0x4B400000u - (uint32_t)(128 * cs);
+                    }
+            const float hs0 = __shfl_sync(0xffffffffu, s0, 8 * tig);
+            const int hbad = __shfl_sync(0xffffffffu, bad, 8 * tig);
+            float sj = hs0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                f.sc[hg][j] = hbad ? __int_as_float(0x7fffffff) : sj * A.scale_log2;
+                sj = sj / 254.0f;
+            }
+        }
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            st.m[hg] = -INFINITY;
+            st.l[hg] = 0.f;
+#pragma unroll
+            for (int mb = 0; mb < 8; mb++) st.o[hg][mb][0] = st.o[hg][mb][1] = st.o[hg][mb][2] = st.o[hg][mb][3] = 0.f;
+        }
+#pragma unroll
+        for (int x = 0; x < kX; x++) { st.nu[x] = 0.f; st.inv_nu[x] = 0.f; }
+    }
+
+    __device__ static void step(const uint8_t *tile, const Frag &f, State &st, int t_lo, int t_hi,
+                                float (&psum)[HG]) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        // ---- K fragments: token rows gid and gid+8
+        const int sw = (gid & 1) << 2;
+        const uint8_t *r0 = tile + 128 * gid, *r1 = tile + 128 * (gid + 8);
+        const uint4 k00 = *reinterpret_cast<const uint4 *>(r0 + ((tig ^ sw) << 4));
+        const uint4 k01 = *reinterpret_cast<const uint4 *>(r0 + (((4 + tig) ^ sw) << 4));
+        const uint4 k10 = *reinterpret_cast<const uint4 *>(r1 + ((tig ^ sw) << 4));
+        const uint4 k11 = *reinterpret_cast<const uint4 *>(r1 + (((4 + tig) ^ sw) << 4));
+        const uint32_t ka[4][4] = {{k00.x, k10.x, k00.y, k10.y},
+                                   {k00.z, k10.z, k00.w, k10.w},
+                                   {k01.x, k11.x, k01.y, k11.y},
+                                   {k01.z, k11.z, k01.w, k11.w}};
+        // ---- scales of tokens gid, gid+8
+        float ks[kX][2], vs[kX][2];
+        if constexpr (kB64) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(tile + 4096 + 16 * gid);
+            const float4 v4 = *reinterpret_cast<const float4 *>(tile + 4224 + 16 * gid);
+            ks[0][0] = k4.x; ks[0][1] = k4.y; ks[kX - 1][0] = k4.z; ks[kX - 1][1] = k4.w;
+            vs[0][0] = v4.x; vs[0][1] = v4.y; vs[kX - 1][0] = v4.z; vs[kX - 1][1] = v4.w;
+        } else {
+            const float2 k2 = h2x2f(*reinterpret_cast<const uint32_t *>(tile + 4096 + 4 * gid));
+            const float2 v2 = h2x2f(*reinterpret_cast<const uint32_t *>(tile + 4128 + 4 * gid));
+            ks[0][0] = k2.x; ks[0][1] = k2.y;
+            vs[0][0] = v2.x; vs[0][1] = v2.y;
+        }
+        const bool full = t_lo == 0 && t_hi == 16;  // warp-uniform
+        const bool ok0 = full || (gid >= t_lo && gid < t_hi);
+        const bool ok1 = full || (gid + 8 >= t_lo && gid + 8 < t_hi);
+        // ---- scores
+        float s[HG][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            int acc[2][2][4];  // [n-block][k-block pair][c]
+#pragma unroll
+            for (int kb = 0; kb < 4; kb++)
+#pragma unroll
+                for (int nb = 0; nb < 2; nb++) {
+                    if (kb & 1)
+                        imma16832(acc[nb][kb >> 1], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3], f.b[hg][nb][kb][0],
+                                  f.b[hg][nb][kb][1]);
+                    else
+                        imma16832_z(acc[nb][kb >> 1], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3],
+                                    f.b[hg][nb][kb][0], f.b[hg][nb][kb][1]);
+                }
+#pragma unroll
+            for (int tk = 0; tk < 2; tk++) {
+                float raw[kX];
+#pragma unroll
+                for (int x = 0; x < kX; x++) raw[x] = 0.f;
+#pragma unroll
+                for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int c = 2 * tk + e, j = 2 * nb + e;
+                        if constexpr (kB64) {
+                            raw[0] = fmaf(small_int_to_float(acc[nb][0][c], f.magic[hg][0][j]), f.sc[hg][j], raw[0]);
+                            raw[kX - 1] =
+                                fmaf(small_int_to_float(acc[nb][1][c], f.magic[hg][kX - 1][j]), f.sc[hg][j], raw[kX - 1]);
+                        } else {
+                            raw[0] = fmaf(small_int_to_float(acc[nb][0][c] + acc[nb][1][c], f.magic[hg][0][j]),
+                                          f.sc[hg][j], raw[0]);
+                        }
+                    }
+                float sc = raw[0] * ks[0][tk];
+                if constexpr (kB64) sc = fmaf(raw[kX - 1], ks[kX - 1][tk], sc);
+                s[hg][tk] = (tk ? ok1 : ok0) ? sc : -INFINITY;
+            }
+        }
+        // ---- online softmax per head (reduction over the 8 token lanes gid)
+        float p[HG][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float tmax = fmaxf(s[hg][0], s[hg][1]);
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+            const float m_new = fmaxf(st.m[hg], tmax);
+            if (__any_sync(0xffffffffu, m_new > st.m[hg])) {
+                const float alpha = ex2(st.m[hg] - m_new);
+                st.l[hg] *= alpha;
+#pragma unroll
+                for (int mb = 0; mb < 8; mb++) {
+                    st.o[hg][mb][0] *= alpha; st.o[hg][mb][1] *= alpha;
+                    st.o[hg][mb][2] *= alpha; st.o[hg][mb][3] *= alpha;
+                }
+                st.m[hg] = m_new;
+            }
+            p[hg][0] = ex2(s[hg][0] - st.m[hg]);
+            p[hg][1] = ex2(s[hg][1] - st.m[hg]);
+            st.l[hg] += p[hg][0] + p[hg][1];
+            psum[hg] = p[hg][0] + p[hg][1];
+        }
+        // ---- V scales -> normaliser nu (shared by all heads)
+#pragma unroll
+        for (int x = 0; x < kX; x++) {
+            vs[x][0] = ok0 ? vs[x][0] : 0.f;
+            vs[x][1] = ok1 ? vs[x][1] : 0.f;
+            const float lmax = fmaxf(vs[x][0], vs[x][1]);
+            const bool first = st.nu[x] == 0.f;
+            if (__any_sync(0xffffffffu, first || lmax > st.nu[x] * kNuHeadroom)) {
+                float vmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, 4));
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 8));
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 16));
+                const float nn = fmaxf(pow2ceil(vmax), kNuFloor);
+                if (first) {
+                    st.nu[x] = nn;
+                } else if (nn > st.nu[x]) {
+                    const float r = st.nu[x] / nn;
+#pragma unroll
+                    for (int hg = 0; hg < HG; hg++)
+#pragma unroll
+                        for (int mb = 0; mb < 8; mb++) {
+                            if (kB64 && (mb >> 2) != x) continue;
+                            st.o[hg][mb][0] *= r; st.o[hg][mb][1] *= r;
+                            st.o[hg][mb][2] *= r; st.o[hg][mb][3] *= r;
+                        }
+                    st.nu[x] = nn;
+                }
+                st.inv_nu[x] = 1.0f / st.nu[x];
+            }
+        }
+        // ---- P' = p * vs / nu as f16 hi+lo, transposed into the PV B operand
+        uint32_t bp[HG][kX][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++)
+#pragma unroll
+            for (int x = 0; x < kX; x++) {
+                const float pt0 = p[hg][0] * vs[x][0] * st.inv_nu[x];
+                const float pt1 = p[hg][1] * vs[x][1] * st.inv_nu[x];
+                const __half2 hi = __floats2half2_rn(pt0, pt1);
+                const float2 hf = __half22float2(hi);
+                const __half2 lo = __floats2half2_rn(pt0 - hf.x, pt1 - hf.y);
+                const uint32_t hu = *reinterpret_cast<const uint32_t *>(&hi);
+                const uint32_t lu = *reinterpret_cast<const uint32_t *>(&lo);
+                bp[hg][x][0] = movmatrix_trans(prmt(hu, lu, 0x5410u));  // (hi, lo) of token gid
+                bp[hg][x][1] = movmatrix_trans(prmt(hu, lu, 0x7632u));  // (hi, lo) of token gid+8
+            }
+        // ---- P x V
+        const uint8_t *vt = tile + 2048 + lane * 64;
+        const int vsw = (lane >> 1) & 3;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint4 c = *reinterpret_cast<const uint4 *>(vt + ((q ^ vsw) << 4));
+#pragma unroll
+            for (int hm = 0; hm < 2; hm++) {
+                const int mb = 2 * q + hm;
+                uint32_t a[4];
+                u8x4_to_h2x2(hm ? c.z : c.x, a[0], a[1]);
+                u8x4_to_h2x2(hm ? c.w : c.y, a[2], a[3]);
+                const int x = kB64 ? (mb >> 2) : 0;
+#pragma unroll
+                for (int hg = 0; hg < HG; hg++) mma16816(st.o[hg][mb], a, bp[hg][x][0], bp[hg][x][1]);
+            }
+        }
+    }
+
+    // tile probability mass and running max per head (eviction scores)
+    __device__ static void mass(const AttnArgs &A, uint64_t unit, const State &st, float (&psum)[HG]) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float u = psum[hg];
+            u += __shfl_xor_sync(0xffffffffu, u, 4);
+            u += __shfl_xor_sync(0xffffffffu, u, 8);
+            u += __shfl_xor_sync(0xffffffffu, u, 16);
+            const uint32_t h = 4 * hg + tig;
+            if (gid == 0 && h < A.group) A.tile_mass[unit * kMaxGroup + h] = make_float2(u, st.m[hg]);
+        }
+    }
+
+    // rows of the G query heads at o_base (stride 128), optionally normalised;
+    // m_out / l_out / seg_ml per head when non-null
+    __device__ static void store_rows(const AttnArgs &A, const State &st, float *o_base, float *m_out, float *l_out,
+                                      bool normalize, float2 *seg_ml) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float lt = st.l[hg];
+            lt += __shfl_xor_sync(0xffffffffu, lt, 4);
+            lt += __shfl_xor_sync(0xffffffffu, lt, 8);
+            lt += __shfl_xor_sync(0xffffffffu, lt, 16);
+            const uint32_t h = 4 * hg + tig;
+            if (h >= A.group) continue;
+            const float inv = normalize ? (lt > 0.f ? 1.0f / lt : 0.f) : 1.0f;
+            float *row = o_base + (size_t)h * kHeadDim;
+#pragma unroll
+            for (int mb = 0; mb < 8; mb++) {
+                const float f = st.nu[kB64 ? (mb >> 2) : 0] * inv;
+                row[16 * mb + gid] = (st.o[hg][mb][0] + st.o[hg][mb][1]) * f;
+                row[16 * mb + gid + 8] = (st.o[hg][mb][2] + st.o[hg][mb][3]) * f;
+            }
+            if (gid == 0) {
+                if (m_out) { m_out[h] = st.m[hg]; l_out[h] = lt; }
+                if (seg_ml) seg_ml[h] = make_float2(st.m[hg], lt);
+            }
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------
+// per-codec operations used by the kernel: begin (load the query rows of a
+// segment, reset the state), step (one tile), mass (eviction scores of the
+// tile), store_rows (the segment's G output rows, or a partial)
+// ---------------------------------------------------------------------------
+template <int CODEC, int HG>
+struct Ops : Int8T<CODEC, HG> {};
+
+// 4-bit codes: query heads in the M rows (hi rows 0..G-1, lo rows 8..8+G-1)
+template <int HG>
+struct Ops<QWN_KV_CODEC_Q4_G32, HG> {
+    using CD = Codec<QWN_KV_CODEC_Q4_G32>;
+    static constexpr int kBytes = CD::kBytes, kStages = CD::kStages;
+    struct Frag { typename CD::Frag f; float scale_log2; };
+    struct State { typename CD::Acc acc; float m, l; };
+    __device__ static void begin(Frag &f, State &st, const AttnArgs &A, uint32_t s_idx) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        const float *q = (uint32_t)gid < A.group ? A.query + ((size_t)s_idx * A.group + gid) * kHeadDim : nullptr;
+        CD::load_q(f.f, q, tig);
+        f.scale_log2 = A.scale_log2;
+        st.acc.reset();
+        st.m = -INFINITY;
+        st.l = 0.f;
+    }
+    __device__ static void step(const uint8_t *tile, const Frag &f, State &st, int t_lo, int t_hi,
+                                float (&psum)[HG]) {
+        psum[0] = tile_step<QWN_KV_CODEC_Q4_G32>(tile, f.f, st.acc, st.m, st.l, t_lo, t_hi, f.scale_log2);
+    }
+    __device__ static void mass(const AttnArgs &A, uint64_t unit, const State &st, float (&psum)[HG]) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        float u = psum[0];
+        u += __shfl_xor_sync(0xffffffffu, u, 1);
+        u += __shfl_xor_sync(0xffffffffu, u, 2);
+        if (tig == 0 && (uint32_t)gid < A.group) A.tile_mass[unit * kMaxGroup + gid] = make_float2(u, st.m);
+    }
+    __device__ static void store_rows(const AttnArgs &A, const State &st, float *o_base, float *m_out, float *l_out,
+                                      bool normalize, float2 *seg_ml) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        float lr = st.l;
+        lr += __shfl_xor_sync(0xffffffffu, lr, 1);
+        lr += __shfl_xor_sync(0xffffffffu, lr, 2);
+        float zs[4];
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            float z = st.acc.z[g];
+            z += __shfl_xor_sync(0xffffffffu, z, 1);
+            z += __shfl_xor_sync(0xffffffffu, z, 2);
+            zs[g] = z;
+        }
+        if ((uint32_t)gid >= A.group) return;
+        const float inv = normalize ? (lr > 0.f ? 1.0f / lr : 0.f) : 1.0f;
+        float *o = o_base + (size_t)gid * kHeadDim;
+#pragma unroll
+        for (int jn = 0; jn < 16; jn++)
+            *reinterpret_cast<float2 *>(o + CD::dim_of(jn, tig, 0)) =
+                make_float2(CD::out_value(st.acc, jn, 0, zs[jn >> 2]) * inv,
+                            CD::out_value(st.acc, jn, 1, zs[jn >> 2]) * inv);
+        if (tig == 0) {
+            if (m_out) { m_out[gid] = st.m; l_out[gid] = lr; }
+            if (seg_ml) seg_ml[gid] = make_float2(st.m, lr);
+        }
+    }
+};
 
 // ---------------------------------------------------------------------------
 // batch geometry
@@ -678,71 +907,33 @@ __device__ __forceinline__ void merge_segment(const AttnArgs &A, uint32_t s_idx,
     else merge_rows<8>(A, s_idx, nparts, Us, T, W);
 }
 
-// End of a warp's share of segment s_idx (batch entry i, kv head h, first
-// unit Us, ns units).  A warp that saw the whole segment writes the output;
-// otherwise it writes its partial (m, l, o) to slot wid + s_idx and counts
-// itself on the segment's counter.  Returns the number of parts when this
-// warp arrived last and must merge them, else 0.  The merge itself runs after
-// the warp's streaming loop, where the loop's registers are free.
-template <int CODEC>
-__device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const typename Codec<CODEC>::Acc &acc,
-                                                   float m, float l, uint32_t s_idx, uint64_t Us, uint64_t ns,
-                                                   uint64_t T, uint64_t W, uint64_t wid) {
-    using CD = Codec<CODEC>;
-    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-    const uint32_t G = A.group;
+// End of a warp's share of segment s_idx (first unit Us, ns units).  A warp
+// that saw the whole segment writes the output; otherwise it writes its
+// partial (m, l, o) to slot wid + s_idx and counts itself on the segment's
+// counter.  Returns the number of parts when this warp arrived last and must
+// merge them, else 0.  The merge itself runs after the warp's streaming loop,
+// where the loop's registers are free.
+template <class OPS>
+__device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const typename OPS::State &st, uint32_t s_idx,
+                                                   uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid) {
+    const int lane = threadIdx.x & 31;
     // warps whose (non-empty) range meets the segment: warp of unit u is
     // ((u+1)W-1)/T.  With T >= W every warp between the first and the last
     // is non-empty; with T < W each unit is a warp of its own.
     const uint64_t wa = ((Us + 1) * W - 1) / T, wb = ((Us + ns) * W - 1) / T;
     const uint32_t nparts = T >= W ? (uint32_t)(wb - wa + 1) : (uint32_t)ns;
-    float lr = l;
-    lr += __shfl_xor_sync(0xffffffffu, lr, 1);
-    lr += __shfl_xor_sync(0xffffffffu, lr, 2);
-    float zs[4] = {0.f, 0.f, 0.f, 0.f};
-    if constexpr (CODEC == QWN_KV_CODEC_Q4_G32) {
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            float z = acc.z[g];
-            z += __shfl_xor_sync(0xffffffffu, z, 1);
-            z += __shfl_xor_sync(0xffffffffu, z, 2);
-            zs[g] = z;
-        }
-    }
-    const size_t row = (size_t)s_idx * G + gid;
+    const size_t row0 = (size_t)s_idx * A.group;
     if (nparts == 1) {
-        if ((uint32_t)gid < G) {
-            if (A.part_o) {
-                float *o = A.part_o + row * kHeadDim;
-#pragma unroll
-                for (int jn = 0; jn < 16; jn++)
-                    *reinterpret_cast<float2 *>(o + CD::dim_of(jn, tig, 0)) =
-                        make_float2(CD::out_value(acc, jn, 0, zs[jn >> 2]), CD::out_value(acc, jn, 1, zs[jn >> 2]));
-                if (tig == 0) { A.part_m[row] = m; A.part_l[row] = lr; }
-            } else {
-                const float inv = lr > 0.f ? 1.0f / lr : 0.f;
-                float *o = A.output + row * kHeadDim;
-#pragma unroll
-                for (int jn = 0; jn < 16; jn++)
-                    *reinterpret_cast<float2 *>(o + CD::dim_of(jn, tig, 0)) =
-                        make_float2(CD::out_value(acc, jn, 0, zs[jn >> 2]) * inv,
-                                    CD::out_value(acc, jn, 1, zs[jn >> 2]) * inv);
-            }
-            if (A.seg_ml && tig == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + gid] = make_float2(m, lr);
-        }
+        float2 *sm = A.seg_ml ? A.seg_ml + (size_t)s_idx * kMaxGroup : nullptr;
+        if (A.part_o)
+            OPS::store_rows(A, st, A.part_o + row0 * kHeadDim, A.part_m + row0, A.part_l + row0, false, sm);
+        else
+            OPS::store_rows(A, st, A.output + row0 * kHeadDim, nullptr, nullptr, true, sm);
         return 0;
     }
     float *slot = A.partials + (size_t)(wid + s_idx) * kPartialFloats;
-    if ((uint32_t)gid < G) {
-#pragma unroll
-        for (int jn = 0; jn < 16; jn++)
-            *reinterpret_cast<float2 *>(slot + gid * kHeadDim + CD::dim_of(jn, tig, 0)) =
-                make_float2(CD::out_value(acc, jn, 0, zs[jn >> 2]), CD::out_value(acc, jn, 1, zs[jn >> 2]));
-        if (tig == 0) {
-            slot[kMaxGroup * kHeadDim + gid] = m;
-            slot[kMaxGroup * kHeadDim + kMaxGroup + gid] = lr;
-        }
-    }
+    OPS::store_rows(A, st, slot, slot + kMaxGroup * kHeadDim, slot + kMaxGroup * kHeadDim + kMaxGroup, false,
+                    nullptr);
     // the warp barrier orders the lanes' slot stores before lane 0's release;
     // the acquire side orders the last arriver's reads of the other slots
     __syncwarp();
@@ -756,23 +947,23 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int CODEC>
+template <int CODEC, int HG>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnArgs A) {
-    using CD = Codec<CODEC>;
-    constexpr int S = CD::kStages, B = CD::kBytes;
+    using OPS = Ops<CODEC, HG>;
+    constexpr int S = OPS::kStages, B = OPS::kBytes;
     extern __shared__ __align__(128) uint8_t smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t *wsm = smem + (size_t)warp * S * B;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)kWarpsPerCta * S * B) + warp * S;
     WarpWindow *win = reinterpret_cast<WarpWindow *>(smem + (size_t)kWarpsPerCta * S * (B + 8)) + warp;
     if (lane == 0) {
 #pragma unroll
-        for (int st = 0; st < S; st++) mbar_init(&bars[st], 1);
+        for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
         fence_barrier_init();
     }
     __syncwarp();
 
-    const uint32_t HK = A.kv_heads, G = A.group, Hq = HK * G;
+    const uint32_t HK = A.kv_heads;
     const uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
     const uint64_t wid = (uint64_t)blockIdx.x * kWarpsPerCta + warp;
 
@@ -828,23 +1019,15 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         }
     }
 
-    typename CD::Frag frag;
-    typename CD::Acc acc;
-    float m = -INFINITY, l = 0.f;
+    typename OPS::Frag frag;
+    typename OPS::State state;
     uint32_t st = 0, par = 0;
     // merges this warp owes (it arrived last at a shared segment), run after the loop
     uint32_t pend_n = 0, pend_s0 = 0, pend_n0 = 0, pend_s1 = 0, pend_n1 = 0;
     uint64_t pend_u0 = 0, pend_u1 = 0;
 
     for (uint32_t k = 0; k < n; ++k) {
-        if (cons.tile == 0 || k == 0) {
-            const float *q = nullptr;
-            if ((uint32_t)gid < G) q = A.query + ((size_t)cons.i * Hq + (size_t)cons.h * G + gid) * kHeadDim;
-            CD::load_q(frag, q, tig);
-            acc.reset();
-            m = -INFINITY;
-            l = 0.f;
-        }
+        if (cons.tile == 0 || k == 0) OPS::begin(frag, state, A, cons.i * HK + cons.h);
         if (!mbar_wait_bounded(&bars[st], par)) {
             if (lane == 0) latch(A.status, QWN_KV_STATUS_WAIT_TIMEOUT);
             // wait (bounded) for the copies still in flight into this warp's stages
@@ -858,13 +1041,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         const int tile_tok0 = (int)(cons.geo.tile0 + cons.tile) * 16;
         const int t_lo = max(cons.geo.tok_lo - tile_tok0, 0);
         const int t_hi = min(cons.geo.tok_hi - tile_tok0, 16);
-        float tile_u = tile_step<CODEC>(wsm + st * B, frag, acc, m, l, t_lo, t_hi, A.scale_log2);
-        if (A.tile_mass) {
-            tile_u += __shfl_xor_sync(0xffffffffu, tile_u, 1);
-            tile_u += __shfl_xor_sync(0xffffffffu, tile_u, 2);
-            if (tig == 0 && (uint32_t)gid < G)
-                A.tile_mass[(u0 + k) * kMaxGroup + gid] = make_float2(tile_u, m);
-        }
+        float psum[HG];
+        OPS::step(wsm + st * B, frag, state, t_lo, t_hi, psum);
+        if (A.tile_mass) OPS::mass(A, u0 + k, state, psum);
         __syncwarp();
 
         // refill this stage with unit k + S
@@ -877,8 +1056,10 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
             const int32_t seg = win->append_seg[j - wbase];
             const uint8_t *src = win->src[j - wbase];
             if (seg >= 0) fused_append<CODEC>(A.new_k, A.new_v, A.seq_ids, A.seq_lens, A.kv_heads, seg, src);
+            // every shared-memory read of this stage fed a register that was
+            // consumed before the __syncwarp above, so the copy cannot
+            // overtake them
             if (lane == 0) {
-                fence_proxy_async_shared();
                 mbar_expect_tx(&bars[st], B);
                 bulk_g2s(wsm + st * B, src, B, &bars[st]);
             }
@@ -888,7 +1069,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         // end of this warp's share of the segment?
         if (cons.tile + 1 == cons.geo.ntiles || k + 1 == n) {
             const uint32_t s_idx = cons.i * HK + cons.h;
-            const uint32_t np = finish_segment<CODEC>(A, acc, m, l, s_idx, cons.seg_base, cons.geo.ntiles, T, W, wid);
+            const uint32_t np = finish_segment<OPS>(A, state, s_idx, cons.seg_base, cons.geo.ntiles, T, W, wid);
             if (np) {
                 const int e = pend_n++;  // at most two: the segment the range starts in and the one it ends in
                 if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.seg_base; }
@@ -925,23 +1106,44 @@ __global__ void merge_kernel(uint32_t parts, uint32_t rows, const float *m, cons
 
 template <int CODEC>
 constexpr size_t codec_smem() {
-    return (size_t)kWarpsPerCta * Codec<CODEC>::kStages * (Codec<CODEC>::kBytes + 8) +
-           (size_t)kWarpsPerCta * sizeof(WarpWindow);
+    using O = Ops<CODEC, 1>;
+    return (size_t)kWarpsPerCta * O::kStages * (O::kBytes + 8) + (size_t)kWarpsPerCta * sizeof(WarpWindow);
+}
+
+// kernel variants: head groups of four query heads (int8 codecs), one for Q4
+template <int CODEC>
+cudaError_t configure_codec() {
+    const int smem = (int)codec_smem<CODEC>();
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if constexpr (CODEC != QWN_KV_CODEC_Q4_G32)
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attn_kernel<CODEC, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    return e;
+}
+template <int CODEC>
+cudaError_t launch_variant(uint32_t ctas, const AttnArgs &A, cudaStream_t s) {
+    const size_t smem = codec_smem<CODEC>();
+    if constexpr (CODEC != QWN_KV_CODEC_Q4_G32) {
+        if (A.group > 4) {
+            attn_kernel<CODEC, 2><<<ctas, kWarpsPerCta * 32, smem, s>>>(A);
+            return cudaGetLastError();
+        }
+    }
+    attn_kernel<CODEC, 1><<<ctas, kWarpsPerCta * 32, smem, s>>>(A);
+    return cudaGetLastError();
 }
 
 template <int CODEC>
 cudaError_t launch_codec(Pool *p, const AttnArgs &A, cudaStream_t s) {
-    const size_t smem = codec_smem<CODEC>();
     static bool configured[64] = {false};
     if (!configured[p->device & 63]) {
-        cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        const cudaError_t e = configure_codec<CODEC>();
         if (e != cudaSuccess) return e;
         configured[p->device & 63] = true;
     }
-    attn_kernel<CODEC><<<p->attn_ctas, kWarpsPerCta * 32, smem, s>>>(A);
+    const cudaError_t e = launch_variant<CODEC>(p->attn_ctas, A, s);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 }  // namespace
@@ -957,9 +1159,9 @@ size_t attention_smem_bytes(uint32_t codec) {
 
 const void *attention_kernel_ptr(uint32_t codec) {
     switch (codec) {
-        case QWN_KV_CODEC_Q8_HEAD_F16: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16>;
-        case QWN_KV_CODEC_Q8_B64_F32: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32>;
-        case QWN_KV_CODEC_Q4_G32: return (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32>;
+        case QWN_KV_CODEC_Q8_HEAD_F16: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16, 1>;
+        case QWN_KV_CODEC_Q8_B64_F32: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32, 1>;
+        case QWN_KV_CODEC_Q4_G32: return (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 1>;
         default: return nullptr;
     }
 }
@@ -1053,11 +1255,11 @@ uint32_t g_static_ctas[kStaticMaxDevices][5] = {};
 template <int CODEC>
 cudaError_t static_setup(int dev) {
     const size_t smem = codec_smem<CODEC>();
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = configure_codec<CODEC>();
     if (e != cudaSuccess) return e;
     int sms = 0, per_sm = 0;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_kernel<CODEC>, kWarpsPerCta * 32, smem)) !=
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_kernel<CODEC, 1>, kWarpsPerCta * 32, smem)) !=
         cudaSuccess)
         return e;
     g_static_ctas[dev][CODEC] = (uint32_t)(sms * (per_sm > 0 ? per_sm : 1));
@@ -1141,21 +1343,12 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
     A.counters = counters;
     A.status = r->status_dev;
     switch (r->codec) {
-        case QWN_KV_CODEC_Q8_HEAD_F16: {
-            attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16><<<ctas, kWarpsPerCta * 32, codec_smem<QWN_KV_CODEC_Q8_HEAD_F16>(), s>>>(A);
-            break;
-        }
-        case QWN_KV_CODEC_Q8_B64_F32: {
-            attn_kernel<QWN_KV_CODEC_Q8_B64_F32><<<ctas, kWarpsPerCta * 32, codec_smem<QWN_KV_CODEC_Q8_B64_F32>(), s>>>(A);
-            break;
-        }
-        default: {
-            attn_kernel<QWN_KV_CODEC_Q4_G32><<<ctas, kWarpsPerCta * 32, codec_smem<QWN_KV_CODEC_Q4_G32>(), s>>>(A);
-            break;
-        }
+        case QWN_KV_CODEC_Q8_HEAD_F16: e = launch_variant<QWN_KV_CODEC_Q8_HEAD_F16>(ctas, A, s); break;
+        case QWN_KV_CODEC_Q8_B64_F32: e = launch_variant<QWN_KV_CODEC_Q8_B64_F32>(ctas, A, s); break;
+        default: e = launch_variant<QWN_KV_CODEC_Q4_G32>(ctas, A, s); break;
     }
     count_launch();
-    if ((e = cudaGetLastError()) != cudaSuccess) {
+    if (e != cudaSuccess) {
         set_cuda_error("qwn_kv_attention_static: launch", e);
         return QWN_CUDA_STATUS_RUNTIME_ERROR;
     }

@@ -259,6 +259,35 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 // biased int8 (code+128) bytes 0,1 / 2,3 of w -> exact f16 pairs
+// integer tensor-core product: D(16x8 s32) += A(16x32 u8, row) x B(32x8 s8, col)
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// D = A x B with a zero accumulator input
+__device__ __forceinline__ void imma16832_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+// transpose of an 8x8 matrix of 16-bit values held one row pair per lane
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+// exact int32 -> fp32 for |x| < 2^22: the integer is added to the mantissa of
+// 1.5*2^23 (whose bit pattern is 0x4B400000) and that float is subtracted
+__device__ __forceinline__ float small_int_to_float(int x, uint32_t magic) {
+    return __uint_as_float((uint32_t)x + magic) - 12582912.0f;
+}
 __device__ __forceinline__ void u8x4_to_h2x2(uint32_t w, uint32_t &b01, uint32_t &b23) {
     const uint32_t k1152 = 0x64806480u;  // 1152.0 in both halves
     b01 = hsub2(prmt(w, 0x64646464u, 0x4140u), k1152);
@@ -284,15 +313,20 @@ __device__ __forceinline__ void nib8_low3_to_h2x4(uint32_t w, uint32_t (&r)[4]) 
 }
 
 // ---- paged tile layout (head_dim 128, 16 tokens per tile) ------------------
+// int8 K: token rows of 128 bytes, 16-byte chunk (d>>4) at (d>>4) ^ ((t&1)<<2)
 __device__ __forceinline__ uint32_t k8_off(int t, int d) {
-    int h = (t >> 1) & 1, n = 2 * (t >> 2) + (t & 1), tig = (d >> 4) & 3, x = d >> 6;
-    int lane = n * 4 + tig;
-    return (uint32_t)(h * 1024 + lane * 32 + ((x ^ (n & 1)) << 4) + (d & 15));
+    return (uint32_t)(t * 128 + (((d >> 4) ^ ((t & 1) << 2)) << 4) + (d & 15));
 }
+// int8 V: the PV A operand (dims x tokens); lane ((r&7)<<2)|((t&7)>>1) of
+// m-block d>>4, 8 bytes per m-block in the lane's 64 (16-byte chunks swizzled)
 __device__ __forceinline__ uint32_t v8_off(int t, int d) {
-    int gid = d & 7, j = d >> 3, tig = t >> 2, b = t & 3, lane = gid * 4 + tig, q = j >> 2;
-    return (uint32_t)(2048 + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4) + ((j & 3) << 2) + b);
+    const int mb = d >> 4, r = d & 15, lane = ((r & 7) << 2) | ((t & 7) >> 1);
+    const int chunk = (mb >> 1) ^ ((lane >> 1) & 3);
+    return (uint32_t)(2048 + lane * 64 + chunk * 16 + 8 * (mb & 1) + 4 * (t >> 3) + 2 * (r >> 3) + (t & 1));
 }
+// int8 scales: tokens t and t+8 adjacent
+__device__ __forceinline__ uint32_t s16_off(int t) { return (uint32_t)(4 * (t & 7) + 2 * (t >> 3)); }
+__device__ __forceinline__ uint32_t s32_off(int t, int x) { return (uint32_t)(16 * (t & 7) + 8 * x + 4 * (t >> 3)); }
 
 }  // namespace qkv
 #endif

@@ -49,11 +49,8 @@ __device__ __forceinline__ uint16_t head_scale16(float m) {
     if ((h & 0x7FFFu) >= 0x7C00u) h = 0x7BFFu;
     return h;
 }
-__device__ __forceinline__ uint32_t k8_lane_off(int t, int lane) {
-    const int n = 2 * (t >> 2) + (t & 1), h = (t >> 1) & 1;
-    return (uint32_t)(h * 1024 + (n * 4 + ((lane >> 2) & 3)) * 32 + (((lane >> 4) ^ (n & 1)) << 4) +
-                      4 * (lane & 3));
-}
+// the lane's four dims 4*lane..4*lane+3 are consecutive bytes of the K row
+__device__ __forceinline__ uint32_t k8_lane_off(int t, int lane) { return k8_off(t, 4 * lane); }
 __device__ __forceinline__ void store_v8(uint8_t *tile, int t, int lane, uint32_t packed) {
 #pragma unroll
     for (int i = 0; i < 4; i++) tile[v8_off(t, 4 * lane + i)] = (uint8_t)(packed >> (8 * i));
@@ -111,8 +108,8 @@ __device__ void store_token<QWN_KV_CODEC_Q8_HEAD_F16>(uint8_t *tile, int t, floa
     *reinterpret_cast<uint32_t *>(tile + k8_lane_off(t, lane)) = q8_pack4(k, fk);
     store_v8(tile, t, lane, q8_pack4(v, fv));
     if (lane == 0) {
-        *reinterpret_cast<uint16_t *>(tile + 4096 + 2 * t) = sk;
-        *reinterpret_cast<uint16_t *>(tile + 4128 + 2 * t) = sv;
+        *reinterpret_cast<uint16_t *>(tile + 4096 + s16_off(t)) = sk;
+        *reinterpret_cast<uint16_t *>(tile + 4128 + s16_off(t)) = sv;
     }
 }
 
@@ -130,8 +127,8 @@ __device__ void store_token<QWN_KV_CODEC_Q8_B64_F32>(uint8_t *tile, int t, float
     store_v8(tile, t, lane, q8_pack4(v, sv));
     if ((lane & 15) == 0) {
         const int x = lane >> 4;
-        *reinterpret_cast<float *>(tile + 4096 + 64 * x + 4 * t) = sk;
-        *reinterpret_cast<float *>(tile + 4224 + 64 * x + 4 * t) = sv;
+        *reinterpret_cast<float *>(tile + 4096 + s32_off(t, x)) = sk;
+        *reinterpret_cast<float *>(tile + 4224 + s32_off(t, x)) = sv;
     }
 }
 
