@@ -342,27 +342,32 @@ struct Int8T {
             bad |= __shfl_xor_sync(0xffffffffu, bad, 2);
             float s = mx > 0.f ? mx / 127.0f : 1.0f;
             const float s0 = s;
+            // slice j: c = round(v / s_j) with |v / s_j| <= 127 by construction
+            // (|v| <= max|q| for j = 0, |residual| <= s_{j-1}/2 = 127 s_j after);
+            // adding 1.5*2^23 rounds to an integer held in the low mantissa bits,
+            // whose low byte is the two's-complement code
+            constexpr float kRound = 12582912.0f;
             int colsum[2][kX];  // this lane's column (slice 2nb + (gid&1)), per scale group
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const float inv = 1.0f / s;
                 uint32_t packed[8];
-                int sum[kX];
+                float sum[kX];
 #pragma unroll
-                for (int x = 0; x < kX; x++) sum[x] = 0;
+                for (int x = 0; x < kX; x++) sum[x] = 0.f;
 #pragma unroll
                 for (int w = 0; w < 8; w++) {
-                    uint32_t word = 0;
+                    uint32_t bits[4];
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
                         const int i = 4 * w + e;
-                        const float c = fminf(fmaxf(rintf(v[i] * inv), -127.f), 127.f);
+                        const float r = fmaf(v[i], inv, kRound);
+                        const float c = r - kRound;
                         v[i] = fmaf(-c, s, v[i]);
-                        const int ci = (int)c;
-                        sum[kB64 ? (i >> 4) : 0] += ci;
-                        word |= ((uint32_t)ci & 0xFFu) << (8 * e);
+                        sum[kB64 ? (i >> 4) : 0] += c;
+                        bits[e] = __float_as_uint(r);
                     }
-                    packed[w] = word;
+                    packed[w] = prmt(prmt(bits[0], bits[1], 0x0040u), prmt(bits[2], bits[3], 0x0040u), 0x5410u);
                 }
                 if ((j & 1) == (gid & 1)) {
 #pragma unroll
@@ -372,7 +377,7 @@ struct Int8T {
                         f.b[hg][j >> 1][kb][1] = packed[base + 1];
                     }
 #pragma unroll
-                    for (int x = 0; x < kX; x++) colsum[j >> 1][x] = sum[x];
+                    for (int x = 0; x < kX; x++) colsum[j >> 1][x] = (int)sum[x];
                 }
                 s = s / 254.0f;
             }
@@ -742,19 +747,6 @@ __device__ __forceinline__ void walk_advance(const AttnArgs &A, Walk &w, uint32_
         if (w.i >= A.num_seqs) return;
     }
 }
-__device__ __forceinline__ const uint8_t *unit_addr(const AttnArgs &A, const Walk &w) {
-    const uint32_t tg = w.geo.tile0 + w.tile;
-    const uint32_t lp = tg / A.tpp, tin = tg % A.tpp;
-    int32_t pg = -1;
-    if (lp < A.mp) pg = A.page_table[(size_t)w.geo.seq * A.mp + lp];
-    if (pg < 0 || (uint32_t)pg >= A.total_pages) {
-        latch(A.status, QWN_KV_STATUS_BAD_PAGE);
-        pg = 0;  // stay in bounds; the latched status marks the result invalid
-    }
-    return A.pages + (size_t)pg * A.page_bytes +
-           ((size_t)(A.layer * A.kv_heads + w.h) * A.tpp + tin) * A.tile_bytes;
-}
-
 __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t v) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
@@ -765,29 +757,58 @@ __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t v) {
     return v;
 }
 
-// per-warp shared-memory window: sources of the next 32 units and, for the
-// fused append, the segment whose newest token lives in that unit (-1: none)
+// per-warp shared-memory windows over the warp's units, double buffered: for
+// unit base+L of window w, pg = the page id (copied from the page table by
+// cp.async, so the warp never waits on it), off = the tile's byte offset in
+// its page, app = the segment whose newest token lives in that unit when the
+// launch appends (-1: none).  The next window is requested 16 units before it
+// is needed.
 struct WarpWindow {
-    const uint8_t *src[32];
-    int32_t append_seg[32];
+    int32_t pg[2][32];
+    uint32_t off[2][32];
+    int32_t app[2][32];
 };
 
-// Fill the window with units [base, base+32) of this warp, lane L taking unit
+// Request window w for units [base, base+32) of this warp, lane L taking unit
 // base+L, walking forward `skip` units from `from`.
 __device__ __forceinline__ void fill_window(const AttnArgs &A, const Walk &from, uint32_t skip, uint64_t base,
-                                            uint64_t u1, WarpWindow *win) {
+                                            uint64_t u1, WarpWindow *win, int w) {
     const int lane = threadIdx.x & 31;
-    const uint8_t *src = nullptr;
     int32_t app = -1;
+    uint32_t off = 0;
+    bool copied = false;
     if (base + lane < u1) {
         Walk t = from;
         walk_advance(A, t, skip + lane);
-        src = unit_addr(A, t);
+        const uint32_t tg = t.geo.tile0 + t.tile;
+        const uint32_t lp = tg / A.tpp, tin = tg % A.tpp;
+        off = ((A.layer * A.kv_heads + t.h) * A.tpp + tin) * A.tile_bytes;
+        if (lp < A.mp) {
+            const int32_t *src = A.page_table + (size_t)t.geo.seq * A.mp + lp;
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(&win->pg[w][lane])), "l"(src)
+                         : "memory");
+            copied = true;
+        }
         if (A.new_k && t.tile + 1 == t.geo.ntiles) app = (int32_t)(t.i * A.kv_heads + t.h);
     }
-    win->src[lane] = src;
-    win->append_seg[lane] = app;
+    if (!copied) win->pg[w][lane] = -1;
+    win->off[w][lane] = off;
+    win->app[w][lane] = app;
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// wait for this warp's window requests
+__device__ __forceinline__ void window_ready() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncwarp();
+}
+// address of unit L of window w (out-of-range page ids latch BAD_PAGE)
+__device__ __forceinline__ const uint8_t *window_src(const AttnArgs &A, const WarpWindow *win, int w, uint32_t L) {
+    int32_t pg = win->pg[w][L];
+    if (pg < 0 || (uint32_t)pg >= A.total_pages) {
+        latch(A.status, QWN_KV_STATUS_BAD_PAGE);
+        pg = 0;  // stay in bounds; the latched status marks the result invalid
+    }
+    return A.pages + (size_t)pg * A.page_bytes + win->off[w][L];
 }
 
 // quantize and store the newest token of segment `seg` into `tile`
@@ -808,51 +829,58 @@ __device__ __noinline__ void fused_append(const float *new_k, const float *new_v
     __syncwarp();
 }
 
+// Partial slot of a (warp, segment): the G rows of unnormalised o, then m[G]
+// and l[G]; one bulk copy of slot_bytes(G) moves it.
+__device__ __forceinline__ uint32_t slot_bytes(uint32_t G) { return (G * (kHeadDim + 2) * 4 + 15u) & ~15u; }
+
 // Merge the nparts partial slots of segment s_idx into its output rows
-// (row0 = s_idx * G).  The slots were written by other warps, so every read
-// is an L2 round trip; they are batched so that a handful of round trips
-// cover a segment: lane pp % 32 reads (m, l) of part pp while all lanes
-// already load the o rows of the first kBatch parts, and the remaining parts
-// follow kBatch at a time.  GG >= G is the compile-time row count.
+// (row0 = s_idx * G).  The slots were written by other warps, so each read is
+// an L2 round trip made while DRAM is saturated by the streaming warps; the
+// merging warp therefore pulls up to `cap` whole slots into its idle pipeline
+// stages (buf, SB bytes) with bulk copies completed on one mbarrier -- one
+// round trip per chunk -- and combines them from shared memory.  GG >= G is
+// the compile-time row count.  Returns false when the wait gave up.
 template <int GG>
-__device__ __forceinline__ void merge_rows(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
-                                           uint64_t T, uint64_t W) {
-    constexpr int kBatch = 16 / GG;  // float4 loads in flight per lane
+__device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
+                                           uint64_t T, uint64_t W, uint8_t *buf, uint32_t SB, uint64_t *bar,
+                                           uint32_t &par) {
     const int lane = threadIdx.x & 31;
     const uint32_t G = A.group;
+    const uint32_t PB = slot_bytes(G), rowf = G * kHeadDim;
+    const uint32_t cap = SB / PB < 32u ? SB / PB : 32u;
     const uint64_t wa = ((Us + 1) * W - 1) / T;
     auto slot_of = [&](uint32_t pp) -> const float * {
         const uint64_t w = T >= W ? wa + pp : ((Us + pp + 1) * W - 1) / T;
         return A.partials + (size_t)(w + s_idx) * kPartialFloats;
     };
+    // the slots were written by generic stores of other warps (ordered by the
+    // acquire on the segment counter); the bulk copies read them through the
+    // async proxy
+    asm volatile("fence.proxy.async.global;" ::: "memory");
     float M[GG], ls[GG];
     float4 acc[GG];
 #pragma unroll
     for (int g = 0; g < GG; g++) { M[g] = -INFINITY; ls[g] = 0.f; acc[g] = make_float4(0.f, 0.f, 0.f, 0.f); }
-    for (uint32_t c = 0; c < nparts; c += 32) {
-        const uint32_t nq = nparts - c < 32u ? nparts - c : 32u;
+    for (uint32_t c = 0; c < nparts; c += cap) {
+        const uint32_t nq = nparts - c < cap ? nparts - c : cap;
+        if (lane == 0) mbar_expect_tx(bar, nq * PB);
+        __syncwarp();
+        if ((uint32_t)lane < nq) bulk_g2s(buf + lane * PB, slot_of(c + lane), PB, bar);
+        if (!mbar_wait_bounded(bar, par)) {
+            if (lane == 0) latch(A.status, QWN_KV_STATUS_WAIT_TIMEOUT);
+            mbar_wait_bounded(bar, par);  // the copies into buf must land before the warp leaves
+            return false;
+        }
+        par ^= 1u;
         float m[GG], l[GG];
 #pragma unroll
         for (int g = 0; g < GG; g++) { m[g] = -INFINITY; l[g] = 0.f; }
         if ((uint32_t)lane < nq) {
-            const float *ml = slot_of(c + lane) + kMaxGroup * kHeadDim;
+            const float *ml = reinterpret_cast<const float *>(buf + lane * PB) + rowf;
 #pragma unroll
             for (int g = 0; g < GG; g++)
-                if ((uint32_t)g < G) { m[g] = __ldcg(ml + g); l[g] = __ldcg(ml + kMaxGroup + g); }
+                if ((uint32_t)g < G) { m[g] = ml[g]; l[g] = ml[G + g]; }
         }
-        float4 v[kBatch][GG];
-        auto load_batch = [&](uint32_t q0) {
-#pragma unroll
-            for (int b = 0; b < kBatch; b++) {
-                const float *sl = slot_of(c + q0 + b);
-#pragma unroll
-                for (int g = 0; g < GG; g++)
-                    v[b][g] = (q0 + b < nq && (uint32_t)g < G)
-                                  ? __ldcg(reinterpret_cast<const float4 *>(sl + g * kHeadDim) + lane)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        };
-        load_batch(0);
         float w[GG];
 #pragma unroll
         for (int g = 0; g < GG; g++) {
@@ -867,18 +895,18 @@ __device__ __forceinline__ void merge_rows(const AttnArgs &A, uint32_t s_idx, ui
             w[g] = (uint32_t)lane < nq && (uint32_t)g < G ? ex2(m[g] - nm) : 0.f;
             ls[g] += l[g] * w[g];
         }
-        for (uint32_t q0 = 0; q0 < nq; q0 += kBatch) {
-            if (q0) load_batch(q0);
+        for (uint32_t q = 0; q < nq; q++) {
+            const float *sl = reinterpret_cast<const float *>(buf + q * PB);
 #pragma unroll
-            for (int b = 0; b < kBatch; b++) {
-#pragma unroll
-                for (int g = 0; g < GG; g++) {
-                    const float wg = __shfl_sync(0xffffffffu, w[g], (q0 + b) & 31);
-                    acc[g].x += v[b][g].x * wg; acc[g].y += v[b][g].y * wg;
-                    acc[g].z += v[b][g].z * wg; acc[g].w += v[b][g].w * wg;
+            for (int g = 0; g < GG; g++) {
+                const float wg = __shfl_sync(0xffffffffu, w[g], q);
+                if ((uint32_t)g < G) {
+                    const float4 v = reinterpret_cast<const float4 *>(sl + g * kHeadDim)[lane];
+                    acc[g].x += v.x * wg; acc[g].y += v.y * wg; acc[g].z += v.z * wg; acc[g].w += v.w * wg;
                 }
             }
         }
+        __syncwarp();  // all lanes are done with buf before the next chunk lands
     }
     const size_t row0 = (size_t)s_idx * G;
 #pragma unroll
@@ -898,24 +926,29 @@ __device__ __forceinline__ void merge_rows(const AttnArgs &A, uint32_t s_idx, ui
         if (A.seg_ml && lane == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + g] = make_float2(M[g], ls[g]);
     }
     if (lane == 0) A.counters[s_idx] = 0u;  // ready for the next launch
+    return true;
 }
 
-__device__ __forceinline__ void merge_segment(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
-                                              uint64_t T, uint64_t W) {
-    if (A.group <= 2) merge_rows<2>(A, s_idx, nparts, Us, T, W);
-    else if (A.group <= 4) merge_rows<4>(A, s_idx, nparts, Us, T, W);
-    else merge_rows<8>(A, s_idx, nparts, Us, T, W);
+__device__ __forceinline__ bool merge_segment(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
+                                              uint64_t T, uint64_t W, uint8_t *buf, uint32_t SB, uint64_t *bar,
+                                              uint32_t &par) {
+    if (A.group <= 2) return merge_rows<2>(A, s_idx, nparts, Us, T, W, buf, SB, bar, par);
+    if (A.group <= 4) return merge_rows<4>(A, s_idx, nparts, Us, T, W, buf, SB, bar, par);
+    return merge_rows<8>(A, s_idx, nparts, Us, T, W, buf, SB, bar, par);
 }
 
 // End of a warp's share of segment s_idx (first unit Us, ns units).  A warp
-// that saw the whole segment writes the output; otherwise it writes its
-// partial (m, l, o) to slot wid + s_idx and counts itself on the segment's
-// counter.  Returns the number of parts when this warp arrived last and must
-// merge them, else 0.  The merge itself runs after the warp's streaming loop,
-// where the loop's registers are free.
+// that saw the whole segment writes the output and returns 0.  Otherwise it
+// writes its partial (m, l, o) to slot wid + s_idx, counts itself on the
+// segment's counter and returns the number of parts; lane 0's `ticket` is the
+// counter value before its increment, and the warp that drew nparts-1 merges.
+// The ticket is only read after the streaming loop (the merge runs there too,
+// where the loop's registers are free), so the loop never waits for the
+// atomic's round trip.
 template <class OPS>
 __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const typename OPS::State &st, uint32_t s_idx,
-                                                   uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid) {
+                                                   uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid,
+                                                   uint32_t &ticket) {
     const int lane = threadIdx.x & 31;
     // warps whose (non-empty) range meets the segment: warp of unit u is
     // ((u+1)W-1)/T.  With T >= W every warp between the first and the last
@@ -932,16 +965,12 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
         return 0;
     }
     float *slot = A.partials + (size_t)(wid + s_idx) * kPartialFloats;
-    OPS::store_rows(A, st, slot, slot + kMaxGroup * kHeadDim, slot + kMaxGroup * kHeadDim + kMaxGroup, false,
-                    nullptr);
+    OPS::store_rows(A, st, slot, slot + A.group * kHeadDim, slot + A.group * (kHeadDim + 1), false, nullptr);
     // the warp barrier orders the lanes' slot stores before lane 0's release;
     // the acquire side orders the last arriver's reads of the other slots
     __syncwarp();
-    uint32_t old = 0;
-    if (lane == 0) old = atom_add_acq_rel_gpu(&A.counters[s_idx], 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    __syncwarp();
-    return old == nparts - 1 ? nparts : 0u;
+    if (lane == 0) ticket = atom_add_acq_rel_gpu(&A.counters[s_idx], 1u);
+    return nparts;
 }
 
 // ---------------------------------------------------------------------------
@@ -1006,28 +1035,38 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         }
     }
 
-    // window of unit sources: units [wbase, wbase+32) of this warp's range
+    // window `cw` holds units [wbase, wbase+32) of this warp's range
     uint32_t wbase = 0;
-    fill_window(A, cons, 0, u0, u1, win);
+    int cw = 0;
+    fill_window(A, cons, 0, u0, u1, win, 0);
+    window_ready();
     const uint32_t npro = n < (uint32_t)S ? n : (uint32_t)S;
     for (uint32_t j = 0; j < npro; j++) {
-        const int32_t seg = win->append_seg[j];
-        if (seg >= 0) fused_append<CODEC>(A.new_k, A.new_v, A.seq_ids, A.seq_lens, A.kv_heads, seg, win->src[j]);
+        const int32_t seg = win->app[0][j];
+        const uint8_t *src = window_src(A, win, 0, j);
+        if (seg >= 0) fused_append<CODEC>(A.new_k, A.new_v, A.seq_ids, A.seq_lens, A.kv_heads, seg, src);
         if (lane == 0) {
             mbar_expect_tx(&bars[j], B);
-            bulk_g2s(wsm + j * B, win->src[j], B, &bars[j]);
+            bulk_g2s(wsm + j * B, src, B, &bars[j]);
         }
     }
 
     typename OPS::Frag frag;
     typename OPS::State state;
     uint32_t st = 0, par = 0;
-    // merges this warp owes (it arrived last at a shared segment), run after the loop
-    uint32_t pend_n = 0, pend_s0 = 0, pend_n0 = 0, pend_s1 = 0, pend_n1 = 0;
+    // partials this warp wrote (at most two), with lane 0's counter tickets
+    uint32_t pend_n = 0, pend_s0 = 0, pend_n0 = 0, pend_s1 = 0, pend_n1 = 0, pend_t0 = 0, pend_t1 = 0;
     uint64_t pend_u0 = 0, pend_u1 = 0;
 
     for (uint32_t k = 0; k < n; ++k) {
         if (cons.tile == 0 || k == 0) OPS::begin(frag, state, A, cons.i * HK + cons.h);
+        if (cons.tile + 4u == cons.geo.ntiles) {
+            // the next segment's query rows (s_idx + 1 in batch order) into L1,
+            // so that its begin() does not wait for them
+            const size_t next = (size_t)(cons.i * HK + cons.h + 1) * A.group;
+            if (next < (size_t)A.num_seqs * HK * A.group && (uint32_t)lane * 128u < A.group * kHeadDim * 4u)
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(A.query + next * kHeadDim + lane * 32));
+        }
         if (!mbar_wait_bounded(&bars[st], par)) {
             if (lane == 0) latch(A.status, QWN_KV_STATUS_WAIT_TIMEOUT);
             // wait (bounded) for the copies still in flight into this warp's stages
@@ -1049,12 +1088,15 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         // refill this stage with unit k + S
         const uint32_t j = k + (uint32_t)S;
         if (j < n) {
+            if (j - wbase == 16u && wbase + 32u < n)  // request the next window early
+                fill_window(A, cons, wbase + 32u - k, u0 + wbase + 32u, u1, win, cw ^ 1);
             if (j - wbase == 32u) {
                 wbase = j;
-                fill_window(A, cons, (uint32_t)S, u0 + wbase, u1, win);
+                cw ^= 1;
+                window_ready();
             }
-            const int32_t seg = win->append_seg[j - wbase];
-            const uint8_t *src = win->src[j - wbase];
+            const int32_t seg = win->app[cw][j - wbase];
+            const uint8_t *src = window_src(A, win, cw, j - wbase);
             if (seg >= 0) fused_append<CODEC>(A.new_k, A.new_v, A.seq_ids, A.seq_lens, A.kv_heads, seg, src);
             // every shared-memory read of this stage fed a register that was
             // consumed before the __syncwarp above, so the copy cannot
@@ -1069,11 +1111,13 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         // end of this warp's share of the segment?
         if (cons.tile + 1 == cons.geo.ntiles || k + 1 == n) {
             const uint32_t s_idx = cons.i * HK + cons.h;
-            const uint32_t np = finish_segment<OPS>(A, state, s_idx, cons.seg_base, cons.geo.ntiles, T, W, wid);
+            uint32_t ticket = 0;
+            const uint32_t np =
+                finish_segment<OPS>(A, state, s_idx, cons.seg_base, cons.geo.ntiles, T, W, wid, ticket);
             if (np) {
                 const int e = pend_n++;  // at most two: the segment the range starts in and the one it ends in
-                if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.seg_base; }
-                else { pend_s1 = s_idx; pend_n1 = np; pend_u1 = cons.seg_base; }
+                if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.seg_base; pend_t0 = ticket; }
+                else { pend_s1 = s_idx; pend_n1 = np; pend_u1 = cons.seg_base; pend_t1 = ticket; }
             }
         }
         // next unit
@@ -1081,8 +1125,14 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
             if (++cons.tile == cons.geo.ntiles) walk_next_segment(A, cons);
         }
     }
+    // the pipeline is drained: its stages hold the partials being merged,
+    // completed on the next barrier in the ring
     for (uint32_t e = 0; e < pend_n; e++) {
-        merge_segment(A, e ? pend_s1 : pend_s0, e ? pend_n1 : pend_n0, e ? pend_u1 : pend_u0, T, W);
+        const uint32_t np = e ? pend_n1 : pend_n0;
+        if (__shfl_sync(0xffffffffu, e ? pend_t1 : pend_t0, 0) != np - 1) continue;  // not the last arrival
+        if (!merge_segment(A, e ? pend_s1 : pend_s0, np, e ? pend_u1 : pend_u0, T, W, wsm, (uint32_t)(S * B),
+                           &bars[st], par))
+            return;
     }
 }
 

@@ -78,7 +78,7 @@ struct Pool {
     std::mutex mu;
 };
 
-constexpr int kPartialFloats = kMaxGroup * kHeadDim + 2 * kMaxGroup;  // o[8][128], m[8], l[8]
+constexpr int kPartialFloats = kMaxGroup * kHeadDim + 2 * kMaxGroup;  // room for o[G][128], m[G], l[G]
 
 inline Pool *pool_from(const QwnKvPoolHandle *h) {
     if (!h || !header_ok(h->header, sizeof(*h)) || !h->opaque) return nullptr;
