@@ -340,7 +340,9 @@ struct Int8T {
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
             bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
             bad |= __shfl_xor_sync(0xffffffffu, bad, 2);
-            float s = mx > 0.f ? mx / 127.0f : 1.0f;
+            // slice scales s_j = s_0 / 254^j (the C side repeats these steps)
+            float s = mx > 0.f ? mx * (1.0f / 127.0f) : 1.0f;
+            float inv = mx > 0.f ? 127.0f / mx : 1.0f;
             const float s0 = s;
             // slice j: c = round(v / s_j) with |v / s_j| <= 127 by construction
             // (|v| <= max|q| for j = 0, |residual| <= s_{j-1}/2 = 127 s_j after);
@@ -350,7 +352,6 @@ struct Int8T {
             int colsum[2][kX];  // this lane's column (slice 2nb + (gid&1)), per scale group
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                const float inv = 1.0f / s;
                 uint32_t packed[8];
                 float sum[kX];
 #pragma unroll
@@ -379,7 +380,8 @@ struct Int8T {
 #pragma unroll
                     for (int x = 0; x < kX; x++) colsum[j >> 1][x] = (int)sum[x];
                 }
-                s = s / 254.0f;
+                s = s * (1.0f / 254.0f);
+                inv = inv * 254.0f;
             }
             // column sums over the head's 128 dims (the four tig lanes)
 #pragma unroll
@@ -406,7 +408,7 @@ struct Int8T {
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 f.sc[hg][j] = hbad ? __int_as_float(0x7fffffff) : sj * A.scale_log2;
-                sj = sj / 254.0f;
+                sj = sj * (1.0f / 254.0f);
             }
         }
 #pragma unroll
@@ -939,17 +941,14 @@ __device__ __forceinline__ bool merge_segment(const AttnArgs &A, uint32_t s_idx,
 
 // End of a warp's share of segment s_idx (first unit Us, ns units).  A warp
 // that saw the whole segment writes the output and returns 0.  Otherwise it
-// writes its partial (m, l, o) to slot wid + s_idx, counts itself on the
-// segment's counter and returns the number of parts; lane 0's `ticket` is the
-// counter value before its increment, and the warp that drew nparts-1 merges.
-// The ticket is only read after the streaming loop (the merge runs there too,
-// where the loop's registers are free), so the loop never waits for the
-// atomic's round trip.
+// writes its partial (m, l, o) to slot wid + s_idx and returns the number of
+// parts.  The warp counts itself on the segment's counter only after its
+// streaming loop (a release there waits for the slot stores to reach L2, a
+// round trip the loop should not take mid-stream); the warp that draws
+// nparts-1 merges, also after its loop.
 template <class OPS>
 __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const typename OPS::State &st, uint32_t s_idx,
-                                                   uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid,
-                                                   uint32_t &ticket) {
-    const int lane = threadIdx.x & 31;
+                                                   uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid) {
     // warps whose (non-empty) range meets the segment: warp of unit u is
     // ((u+1)W-1)/T.  With T >= W every warp between the first and the last
     // is non-empty; with T < W each unit is a warp of its own.
@@ -966,10 +965,6 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
     }
     float *slot = A.partials + (size_t)(wid + s_idx) * kPartialFloats;
     OPS::store_rows(A, st, slot, slot + A.group * kHeadDim, slot + A.group * (kHeadDim + 1), false, nullptr);
-    // the warp barrier orders the lanes' slot stores before lane 0's release;
-    // the acquire side orders the last arriver's reads of the other slots
-    __syncwarp();
-    if (lane == 0) ticket = atom_add_acq_rel_gpu(&A.counters[s_idx], 1u);
     return nparts;
 }
 
@@ -1054,12 +1049,20 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
     typename OPS::Frag frag;
     typename OPS::State state;
     uint32_t st = 0, par = 0;
-    // partials this warp wrote (at most two), with lane 0's counter tickets
-    uint32_t pend_n = 0, pend_s0 = 0, pend_n0 = 0, pend_s1 = 0, pend_n1 = 0, pend_t0 = 0, pend_t1 = 0;
+    // partials this warp wrote (at most two); the first is counted on its
+    // segment a few tiles after it was written (its stores have landed by then,
+    // so the release costs nothing), the last after the loop
+    uint32_t pend_n = 0, pend_s0 = 0, pend_n0 = 0, pend_s1 = 0, pend_n1 = 0, pend_k0 = 0, tk0 = 0;
+    bool counted0 = false;
     uint64_t pend_u0 = 0, pend_u1 = 0;
 
     for (uint32_t k = 0; k < n; ++k) {
         if (cons.tile == 0 || k == 0) OPS::begin(frag, state, A, cons.i * HK + cons.h);
+        if (pend_n && !counted0 && k == pend_k0 + 4u) {
+            __syncwarp();
+            if (lane == 0) tk0 = atom_add_acq_rel_gpu(&A.counters[pend_s0], 1u);  // ticket read after the loop
+            counted0 = true;
+        }
         if (cons.tile + 4u == cons.geo.ntiles) {
             // the next segment's query rows (s_idx + 1 in batch order) into L1,
             // so that its begin() does not wait for them
@@ -1111,13 +1114,11 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         // end of this warp's share of the segment?
         if (cons.tile + 1 == cons.geo.ntiles || k + 1 == n) {
             const uint32_t s_idx = cons.i * HK + cons.h;
-            uint32_t ticket = 0;
-            const uint32_t np =
-                finish_segment<OPS>(A, state, s_idx, cons.seg_base, cons.geo.ntiles, T, W, wid, ticket);
+            const uint32_t np = finish_segment<OPS>(A, state, s_idx, cons.seg_base, cons.geo.ntiles, T, W, wid);
             if (np) {
                 const int e = pend_n++;  // at most two: the segment the range starts in and the one it ends in
-                if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.seg_base; pend_t0 = ticket; }
-                else { pend_s1 = s_idx; pend_n1 = np; pend_u1 = cons.seg_base; pend_t1 = ticket; }
+                if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.seg_base; pend_k0 = k; }
+                else { pend_s1 = s_idx; pend_n1 = np; pend_u1 = cons.seg_base; }
             }
         }
         // next unit
@@ -1127,9 +1128,20 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
     }
     // the pipeline is drained: its stages hold the partials being merged,
     // completed on the next barrier in the ring
+    // count this warp's partials on their segments: the warp barrier orders
+    // the lanes' slot stores before lane 0's release, the acquire orders the
+    // last arriver's reads of the other slots
+    __syncwarp();
+    uint32_t tk1 = 0;
+    if (lane == 0) {
+        if (pend_n > 0 && !counted0) tk0 = atom_add_acq_rel_gpu(&A.counters[pend_s0], 1u);
+        if (pend_n > 1) tk1 = atom_add_acq_rel_gpu(&A.counters[pend_s1], 1u);
+    }
+    tk0 = __shfl_sync(0xffffffffu, tk0, 0);
+    tk1 = __shfl_sync(0xffffffffu, tk1, 0);
     for (uint32_t e = 0; e < pend_n; e++) {
         const uint32_t np = e ? pend_n1 : pend_n0;
-        if (__shfl_sync(0xffffffffu, e ? pend_t1 : pend_t0, 0) != np - 1) continue;  // not the last arrival
+        if ((e ? tk1 : tk0) != np - 1) continue;  // not the last arrival
         if (!merge_segment(A, e ? pend_s1 : pend_s0, np, e ? pend_u1 : pend_u0, T, W, wsm, (uint32_t)(S * B),
                            &bars[st], par))
             return;
