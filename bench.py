@@ -51,6 +51,20 @@ def kv_bytes(codec: int) -> int:
     return {1: 272, 2: 260, 3: 128, 4: 160}[codec]
 
 
+def profiled_traffic(cfg: int):
+    """DRAM bytes per attention launch (dram__bytes_read + write) from the
+    committed ncu capture of the same kernel on this workload's shapes, or
+    None when no capture covers the workload."""
+    path = os.path.join(ROOT, "profiles", {2: "attn_kernel_q8head_cfg2_full.md"}.get(cfg, ""))
+    if not os.path.isfile(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            if line.startswith("traffic_bytes_per_launch:"):
+                return {"bytes_per_launch": float(line.split(":", 1)[1]), "source": os.path.relpath(path, ROOT)}
+    return None
+
+
 def peaks() -> tuple:
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -313,7 +327,9 @@ def run_ours(args, wl, world, rank, local):
     seq_steps_total = B * world
     value = seq_steps_total / (ms_step / 1000.0)
 
-    # algorithmic bytes (SURVEY 8d formula) for the timed steps, this rank
+    # algorithmic bytes for the timed steps, this rank: K/V codes and scales
+    # of every attended token and of the appended one, the new K/V rows, the
+    # Q and O rows and the page-table entries read
     bkv = kv_bytes(wl["codec"])
     step_bytes, attn_bytes = 0.0, 0.0
     for i in range(K):
@@ -331,6 +347,8 @@ def run_ours(args, wl, world, rank, local):
     line = None
     if rank == 0:
         clocks = sampler.summary(t_wall0 - 0.05, t_wall1 + 0.05)
+        # the capture covers one GPU's full cfg batch; other shapes report none
+        traffic = profiled_traffic(args.config) if world == 1 and not args.batch else None
         line = {
             "metric": METRIC, "value": value, "unit": "seq-steps/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -342,7 +360,9 @@ def run_ours(args, wl, world, rank, local):
                        "l2": "inputs larger than L2 (KV bytes per step >> 126 MB)"},
             "kv_gbs": kv_gbs, "hbm_frac_per_gpu": kv_gbs / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": (traffic or {}).get("bytes_per_launch"),
+                         "traffic_source": (traffic or {}).get("source"),
                          "kernel": "attn_kernel (fused quantize-on-append + split-KV decode attention)",
                          "algorithmic_bytes_per_launch": attn_bytes_per_launch,
                          "avg_launch_ms": attn_avg_ms, "avg_launch_ms_max_rank": attn_avg_max},
