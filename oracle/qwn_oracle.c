@@ -303,10 +303,26 @@ void qor_q4g32_quantize(const float *src, int n, uint8_t *codes, uint16_t *range
  *    4096 + 4*(t&7) + 2*(t>>3), V scale at 4128 + same.  Q8_B64: fp32 K
  *    scale of channel block x at 4096 + 16*(t&7) + 8*x + 4*(t>>3), V at
  *    4224 + same.
- *  - 4-bit K: lane n*4+tig, word g=d>>5 in the lane's 16 bytes, nibble
- *    position (i&1)*4+e*2+(i>>1) with e=(d>>4)&1, tig=(d>>2)&3, i=d&3.
- *  - 4-bit V: lane (d&7)*4+(t>>2), word w=d>>4 (16-byte chunk (w>>2) xor
- *    ((lane>>2)&1)), nibble position (b&1)*4+((d>>3)&1)*2+(b>>1), b=t&3.
+ *  - low-bit codecs (4-bit groups of 32, 3.5-bit TurboQuant) are organised
+ *    in classes of 32 dims with one scale each: codec 4 class c = d>>5 (the
+ *    group), index m = d&31; TurboQuant class c = 2*(d>>6) + (d&1) (group,
+ *    parity), index m = (d&63)>>1.  K codes are the A rows of the integer
+ *    QK^T product: the "K word" of (token t, tig = m>>3, class c) holds the
+ *    8 codes m = 8*tig+i in byte i&3, low nibble for i<4, high for i>=4.
+ *    V codes are the A operand of P x V: m-block mb = 2c + (m>>4), row
+ *    r = m&15, lane ((r&7)<<2)|((t&7)>>1), nibble (r>>3) + 2*(t>>3) + 4*(t&1)
+ *    of the lane's word for mb.
+ *    codec 4 (2560 B): K word at 64t + 16tig + 4c; V word at 1024 + 32*lane
+ *    + 16*((mb>>2) ^ ((lane>>2)&1)) + 4*(mb&3); params (range16, min16) at
+ *    2048 (K) / 2304 (V) + 32*(t&7) + 8c + 4*(t>>3).
+ *    codec 3 (2048 B): K half [0,1024), V half [1024,2048), each: 4-bit even
+ *    codes, 3-bit odd codes (group 0 in the low 3 bits of a nibble, bit 0
+ *    of group 1 in its top bit), a plane of the group-1 odd codes' bits 1-2
+ *    (two bits per nibble position n at bit 2n), params (range16, min16) at
+ *    896 + 16*(t&7) + 8*group + 4*(t>>3).  K: even word at 32t + 8tig +
+ *    4*group, odd word at 512 + 16t + 4tig, plane u16 at 768 + 8t + 2tig.
+ *    V: even word e = 2*group + (mb&1) at 16*lane + 4e, odd word k = mb&1 at
+ *    512 + 8*lane + 4k, plane u16 at 768 + 4*lane + 2k.
  */
 
 size_t qor_tile_bytes(int codec) {
@@ -334,24 +350,41 @@ static size_t v8_off(int t, int d) {
 static size_t s16_off(int t) { return (size_t)(4 * (t & 7) + 2 * (t >> 3)); }
 static size_t s32_off(int t, int x) { return (size_t)(16 * (t & 7) + 8 * x + 4 * (t >> 3)); }
 
-/* nibble address: byte offset and high(1)/low(0) nibble */
+/* low-bit class structure: class and index within the class of dim d */
+static void lb_class(int codec, int d, int *c, int *m) {
+    if (codec == QOR_CODEC_Q4_G32) { *c = d >> 5; *m = d & 31; }
+    else { *c = 2 * (d >> 6) + (d & 1); *m = (d & 63) >> 1; }
+}
+/* K word position: (t, tig, c) and the nibble n (0..7, bit 4n) of code m */
+static int lb_k_nibble(int m) { int i = m & 7; return 2 * (i & 3) + (i >> 2); }
+/* V: lane, m-block and nibble of (t, d) */
+static void lb_v(int codec, int t, int d, int *lane, int *mb, int *nib) {
+    int c, m;
+    lb_class(codec, d, &c, &m);
+    int r = m & 15;
+    *mb = 2 * c + (m >> 4);
+    *lane = ((r & 7) << 2) | ((t & 7) >> 1);
+    *nib = (r >> 3) + 2 * (t >> 3) + 4 * (t & 1);
+}
+/* nibble address: byte offset and high(1)/low(0) nibble (codec 4) */
 static void k4_pos(int t, int d, size_t *byte, int *hi) {
-    int h = (t >> 1) & 1, n = 2 * (t >> 2) + (t & 1);
-    int g = d >> 5, e = (d >> 4) & 1, tig = (d >> 2) & 3, i = d & 3;
-    int lane = n * 4 + tig;
-    int pos = (i & 1) * 4 + e * 2 + (i >> 1);
-    *byte = (size_t)h * 512 + (size_t)lane * 16 + (size_t)g * 4 + (size_t)(pos >> 1);
-    *hi = pos & 1;
+    int c, m;
+    lb_class(QOR_CODEC_Q4_G32, d, &c, &m);
+    int n = lb_k_nibble(m);
+    *byte = (size_t)t * 64 + (size_t)(m >> 3) * 16 + (size_t)c * 4 + (size_t)(n >> 1);
+    *hi = n & 1;
 }
 
 static void v4_pos(int t, int d, size_t *byte, int *hi) {
-    int gid = d & 7, j = d >> 3, tig = t >> 2, b = t & 3, lane = gid * 4 + tig;
-    int w = j >> 1, e = j & 1;
-    int pos = (b & 1) * 4 + e * 2 + (b >> 1);
-    int chunk = (w >> 2) ^ ((lane >> 2) & 1);
-    *byte = 1024 + (size_t)lane * 32 + (size_t)chunk * 16 + (size_t)(w & 3) * 4 + (size_t)(pos >> 1);
-    *hi = pos & 1;
+    int lane, mb, n;
+    lb_v(QOR_CODEC_Q4_G32, t, d, &lane, &mb, &n);
+    int chunk = (mb >> 2) ^ ((lane >> 2) & 1);
+    *byte = 1024 + (size_t)lane * 32 + (size_t)chunk * 16 + (size_t)(mb & 3) * 4 + (size_t)(n >> 1);
+    *hi = n & 1;
 }
+/* low-bit params: (range16, min16) of (t, class c) for codec 4, (t, group x) for codec 3 */
+static size_t q4_param_off(int t, int c) { return (size_t)(32 * (t & 7) + 8 * c + 4 * (t >> 3)); }
+static size_t tq_param_off(int t, int x) { return (size_t)(896 + 16 * (t & 7) + 8 * x + 4 * (t >> 3)); }
 
 static void put_nib(uint8_t *tile, size_t byte, int hi, uint8_t v) {
     if (hi) tile[byte] = (uint8_t)((tile[byte] & 0x0F) | ((v & 0x0F) << 4));
@@ -365,126 +398,55 @@ static uint16_t get_u16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)
 static void put_f32(uint8_t *p, float v) { memcpy(p, &v, 4); }
 static float get_f32(const uint8_t *p) { float v; memcpy(&v, p, 4); return v; }
 
-/*
- * 3.5-bit TurboQuant tile (2048 bytes).  K occupies [0,1024) and V
- * [1024,2048); each half is: even codes (4-bit) 512 B, odd codes low part
- * 256 B, odd codes high part 128 B, params 128 B.
- *  K, slot (h, lane = n*4+tig), group x, position k within the lane's
- *  16-value sub-chunk (dims 64x+16tig+k): even code e=k/2 -> nibble
- *  (e&1)*4+(e>>1) of word x of the lane's even pair; odd code o=k/2 of
- *  group 0 -> nibble (o&1)*4+(o>>1) of the lane's odd word, low 3 bits;
- *  odd code of group 1 -> bit 0 in the top bit of that nibble, bits 1-2 in
- *  the lane's 16-bit high part at bits 2*np..2*np+1 (np the nibble position).
- *  K params: [x][16 tokens] (range16, min16).
- *  V: lane (gid, tig=t>>2), column tile j and token byte b=t&3 from
- *  tq_v_pos below; even-dim columns hold 4-bit codes (16 B per lane),
- *  odd-dim columns 3-bit codes (8 B low part + 4 B high part per lane).
- */
-static void tq_k_pos(int t, int d, int *lane_out, int *h_out, int *x_out, int *k_out) {
-    int h = (t >> 1) & 1, n = 2 * (t >> 2) + (t & 1);
-    int x = d >> 6, tig = (d >> 4) & 3, k = d & 15;
-    *lane_out = n * 4 + tig; *h_out = h; *x_out = x; *k_out = k;
-}
-
-/* V: the PV fragment of lane (gid,tig) in column tile j covers dim
- * D(j,gid) = 64*(j>>3) + 2*(8*(j&3)+gid) + ((j>>2)&1) and tokens 4tig..4tig+3.
- * Even dims (j&4)==0 hold 4-bit codes, odd dims 3-bit codes.  Inverse map: */
-static void tq_v_pos(int t, int d, int *lane_out, int *j_out, int *b_out) {
-    int x = d >> 6, r = d & 63, par = r & 1, q = r >> 1; /* q = 8*(j&3)+gid */
-    int gid = q & 7, jl = q >> 3;
-    int j = x * 8 + par * 4 + jl;
-    *lane_out = gid * 4 + (t >> 2); *j_out = j; *b_out = t & 3;
+/* 3.5-bit TurboQuant codes: see the layout notes above.  Odd codes of group
+ * 0 fill bits 0-2 of a nibble; bit 0 of the group-1 odd code sits in bit 3
+ * of the same nibble and its bits 1-2 in the plane at bit 2n. */
+static void tq_pos(int is_value, int t, int d, size_t *even_byte, int *even_hi, size_t *odd_byte,
+                   int *odd_hi, size_t *plane_byte, int *plane_shift) {
+    int c, m;
+    lb_class(QOR_CODEC_TQ35_G64, d, &c, &m);
+    int x = c >> 1;
+    if (!is_value) {
+        int tig = m >> 3, n = lb_k_nibble(m);
+        *even_byte = (size_t)(32 * t + 8 * tig + 4 * x + (n >> 1));
+        *odd_byte = (size_t)(512 + 16 * t + 4 * tig + (n >> 1));
+        *even_hi = *odd_hi = n & 1;
+        *plane_byte = (size_t)(768 + 8 * t + 2 * tig + ((2 * n) >> 3));
+        *plane_shift = (2 * n) & 7;
+    } else {
+        int lane, mb, n;
+        lb_v(QOR_CODEC_TQ35_G64, t, d, &lane, &mb, &n);
+        int e = 2 * x + (mb & 1), k = mb & 1;
+        *even_byte = (size_t)(16 * lane + 4 * e + (n >> 1));
+        *odd_byte = (size_t)(512 + 8 * lane + 4 * k + (n >> 1));
+        *even_hi = *odd_hi = n & 1;
+        *plane_byte = (size_t)(768 + 4 * lane + 2 * k + ((2 * n) >> 3));
+        *plane_shift = (2 * n) & 7;
+    }
 }
 
 static void tq_store_codes(uint8_t *half, int is_value, int t, int d, uint8_t code) {
-    /* even region 512 B, odd-low 256 B, odd-high 128 B */
-    uint8_t *even = half, *odd_lo = half + 512, *odd_hi = half + 768;
-    if (!is_value) {
-        int lane, h, x, k;
-        tq_k_pos(t, d, &lane, &h, &x, &k);
-        int slot = h * 32 + lane;
-        int e = k >> 1, par = k & 1;
-        int np = (e & 1) * 4 + (e >> 1);
-        if (!par) {
-            size_t byte = (size_t)slot * 8 + (size_t)x * 4 + (size_t)(np >> 1);
-            put_nib(even, byte, np & 1, code);
-        } else {
-            size_t byte = (size_t)slot * 4 + (size_t)(np >> 1);
-            uint8_t nib = get_nib(odd_lo, byte, np & 1);
-            if (x == 0) nib = (uint8_t)((nib & 0x8) | (code & 0x7));
-            else nib = (uint8_t)((nib & 0x7) | ((code & 1) << 3));
-            put_nib(odd_lo, byte, np & 1, nib);
-            if (x == 1) {
-                uint16_t hv = get_u16(odd_hi + slot * 2);
-                hv = (uint16_t)((hv & ~(3u << (2 * np))) | (((code >> 1) & 3u) << (2 * np)));
-                put_u16(odd_hi + slot * 2, hv);
-            }
-        }
+    size_t eb, ob, pb; int eh, oh, ps;
+    tq_pos(is_value, t, d, &eb, &eh, &ob, &oh, &pb, &ps);
+    int x = d >> 6;
+    if (!(d & 1)) {
+        put_nib(half, eb, eh, code);
     } else {
-        int lane, j, b;
-        tq_v_pos(t, d, &lane, &j, &b);
-        /* per lane: 8 even tiles (j&4==0) x 4 tokens = 32 nibbles = 16 B,
-         * 8 odd tiles x 4 tokens x 3 bits = 96 bits: 8 B low + 4 B high */
-        int x = j >> 3, jl = j & 3, par = (j >> 2) & 1;
-        int col = x * 4 + jl; /* 0..7 */
-        int np = (b & 1) * 4 + (col & 1) * 2 + (b >> 1);
-        if (!par) {
-            size_t byte = (size_t)lane * 16 + (size_t)(col >> 1) * 4 + (size_t)(np >> 1);
-            put_nib(even, byte, np & 1, code);
-        } else {
-            /* odd columns: the nibble at (word jl>>1, position npos) keeps the
-             * group-0 code in its low 3 bits and bit 0 of the group-1 code in
-             * its top bit; bits 1-2 of the group-1 code go to the lane's
-             * 32-bit high word at bit 2*((jl>>1)*8+npos). */
-            int npos = (b & 1) * 4 + (jl & 1) * 2 + (b >> 1);
-            size_t byte = (size_t)lane * 8 + (size_t)(jl >> 1) * 4 + (size_t)(npos >> 1);
-            uint8_t nib = get_nib(odd_lo, byte, npos & 1);
-            if (x == 0) nib = (uint8_t)((nib & 0x8) | (code & 0x7));
-            else nib = (uint8_t)((nib & 0x7) | ((code & 1) << 3));
-            put_nib(odd_lo, byte, npos & 1, nib);
-            if (x == 1) {
-                int bitpos = 2 * ((jl >> 1) * 8 + npos);
-                size_t hb = (size_t)lane * 4;
-                uint32_t hv = (uint32_t)odd_hi[hb] | ((uint32_t)odd_hi[hb + 1] << 8) |
-                              ((uint32_t)odd_hi[hb + 2] << 16) | ((uint32_t)odd_hi[hb + 3] << 24);
-                hv = (hv & ~(3u << bitpos)) | (((uint32_t)(code >> 1) & 3u) << bitpos);
-                odd_hi[hb] = (uint8_t)hv; odd_hi[hb + 1] = (uint8_t)(hv >> 8);
-                odd_hi[hb + 2] = (uint8_t)(hv >> 16); odd_hi[hb + 3] = (uint8_t)(hv >> 24);
-            }
-        }
+        uint8_t nib = get_nib(half, ob, oh);
+        if (x == 0) nib = (uint8_t)((nib & 0x8) | (code & 0x7));
+        else nib = (uint8_t)((nib & 0x7) | ((code & 1) << 3));
+        put_nib(half, ob, oh, nib);
+        if (x == 1) half[pb] = (uint8_t)((half[pb] & ~(3u << ps)) | (((code >> 1) & 3u) << ps));
     }
 }
 
 static uint8_t tq_load_code(const uint8_t *half, int is_value, int t, int d) {
-    const uint8_t *even = half, *odd_lo = half + 512, *odd_hi = half + 768;
-    if (!is_value) {
-        int lane, h, x, k;
-        tq_k_pos(t, d, &lane, &h, &x, &k);
-        int slot = h * 32 + lane, e = k >> 1, par = k & 1;
-        int np = (e & 1) * 4 + (e >> 1);
-        if (!par) return get_nib(even, (size_t)slot * 8 + (size_t)x * 4 + (size_t)(np >> 1), np & 1);
-        uint8_t nib = get_nib(odd_lo, (size_t)slot * 4 + (size_t)(np >> 1), np & 1);
-        if (x == 0) return nib & 0x7;
-        uint16_t hv = get_u16(odd_hi + slot * 2);
-        return (uint8_t)((nib >> 3) | (((hv >> (2 * np)) & 3u) << 1));
-    } else {
-        int lane, j, b;
-        tq_v_pos(t, d, &lane, &j, &b);
-        int x = j >> 3, jl = j & 3, par = (j >> 2) & 1;
-        int col = x * 4 + jl;
-        if (!par) {
-            int np = (b & 1) * 4 + (col & 1) * 2 + (b >> 1);
-            return get_nib(even, (size_t)lane * 16 + (size_t)(col >> 1) * 4 + (size_t)(np >> 1), np & 1);
-        }
-        int npos = (b & 1) * 4 + (jl & 1) * 2 + (b >> 1);
-        uint8_t nib = get_nib(odd_lo, (size_t)lane * 8 + (size_t)(jl >> 1) * 4 + (size_t)(npos >> 1), npos & 1);
-        if (x == 0) return nib & 0x7;
-        int bitpos = 2 * ((jl >> 1) * 8 + npos);
-        size_t hb = (size_t)lane * 4;
-        uint32_t hv = (uint32_t)odd_hi[hb] | ((uint32_t)odd_hi[hb + 1] << 8) |
-                      ((uint32_t)odd_hi[hb + 2] << 16) | ((uint32_t)odd_hi[hb + 3] << 24);
-        return (uint8_t)((nib >> 3) | (((hv >> bitpos) & 3u) << 1));
-    }
+    size_t eb, ob, pb; int eh, oh, ps;
+    tq_pos(is_value, t, d, &eb, &eh, &ob, &oh, &pb, &ps);
+    if (!(d & 1)) return get_nib(half, eb, eh);
+    uint8_t nib = get_nib(half, ob, oh);
+    if ((d >> 6) == 0) return nib & 0x7;
+    return (uint8_t)((nib >> 3) | (((half[pb] >> ps) & 3u) << 1));
 }
 
 void qor_tile_store(int codec, uint8_t *tile, int t, const float *k, const float *v) {
@@ -521,10 +483,10 @@ void qor_tile_store(int codec, uint8_t *tile, int t, const float *k, const float
             v4_pos(t, d, &byte, &hi); put_nib(tile, byte, hi, cv[d]);
         }
         for (int g = 0; g < 4; g++) {
-            put_u16(tile + 2048 + g * 64 + t * 4, rk[g]);
-            put_u16(tile + 2048 + g * 64 + t * 4 + 2, mk[g]);
-            put_u16(tile + 2304 + g * 64 + t * 4, rv[g]);
-            put_u16(tile + 2304 + g * 64 + t * 4 + 2, mv[g]);
+            put_u16(tile + 2048 + q4_param_off(t, g), rk[g]);
+            put_u16(tile + 2048 + q4_param_off(t, g) + 2, mk[g]);
+            put_u16(tile + 2304 + q4_param_off(t, g), rv[g]);
+            put_u16(tile + 2304 + q4_param_off(t, g) + 2, mv[g]);
         }
     } else if (codec == QOR_CODEC_TQ35_G64) {
         uint8_t bk[64], bv[64];
@@ -534,11 +496,11 @@ void qor_tile_store(int codec, uint8_t *tile, int t, const float *k, const float
             uint8_t codes_k[64], codes_v[64];
             uint16_t r, m;
             qor_tq35_unpack(bk + x * 32, codes_k, &r, &m);
-            put_u16(tile + 896 + x * 64 + t * 4, r);
-            put_u16(tile + 896 + x * 64 + t * 4 + 2, m);
+            put_u16(tile + tq_param_off(t, x), r);
+            put_u16(tile + tq_param_off(t, x) + 2, m);
             qor_tq35_unpack(bv + x * 32, codes_v, &r, &m);
-            put_u16(tile + 1024 + 896 + x * 64 + t * 4, r);
-            put_u16(tile + 1024 + 896 + x * 64 + t * 4 + 2, m);
+            put_u16(tile + 1024 + tq_param_off(t, x), r);
+            put_u16(tile + 1024 + tq_param_off(t, x) + 2, m);
             for (int i = 0; i < 64; i++) {
                 tq_store_codes(tile, 0, t, x * 64 + i, codes_k[i]);
                 tq_store_codes(tile + 1024, 1, t, x * 64 + i, codes_v[i]);
@@ -566,7 +528,7 @@ void qor_tile_load(int codec, const uint8_t *tile, int t, int is_value, int16_t 
             codes[d] = get_nib(tile, byte, hi);
         }
         for (int g = 0; g < 4; g++) {
-            const uint8_t *p = tile + (is_value ? 2304 : 2048) + g * 64 + t * 4;
+            const uint8_t *p = tile + (is_value ? 2304 : 2048) + q4_param_off(t, g);
             params[2 * g] = qor_tq_f16_to_f32(get_u16(p));
             params[2 * g + 1] = qor_tq_f16_to_f32(get_u16(p + 2));
         }
@@ -574,8 +536,8 @@ void qor_tile_load(int codec, const uint8_t *tile, int t, int is_value, int16_t 
         const uint8_t *half = tile + (is_value ? 1024 : 0);
         for (int d = 0; d < HD; d++) codes[d] = tq_load_code(half, is_value, t, d);
         for (int x = 0; x < 2; x++) {
-            params[2 * x] = qor_tq_f16_to_f32(get_u16(half + 896 + x * 64 + t * 4));
-            params[2 * x + 1] = qor_tq_f16_to_f32(get_u16(half + 896 + x * 64 + t * 4 + 2));
+            params[2 * x] = qor_tq_f16_to_f32(get_u16(half + tq_param_off(t, x)));
+            params[2 * x + 1] = qor_tq_f16_to_f32(get_u16(half + tq_param_off(t, x) + 2));
         }
     }
 }

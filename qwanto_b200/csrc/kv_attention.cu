@@ -66,216 +66,6 @@ __device__ __forceinline__ float2 h2x2f(uint32_t w) {
     return __half22float2(*reinterpret_cast<const __half2 *>(&w));
 }
 
-// A-operand rows gid (hi) and gid+8 (lo) for four values at k-positions
-// (2tig, 2tig+1) and (2tig+8, 2tig+9); packed conversions
-__device__ __forceinline__ void make_a(const float (&v)[4], uint32_t (&a)[4]) {
-    const __half2 h01 = __floats2half2_rn(v[0], v[1]);
-    const __half2 h23 = __floats2half2_rn(v[2], v[3]);
-    const float2 b01 = __half22float2(h01), b23 = __half22float2(h23);
-    const __half2 l01 = __floats2half2_rn(v[0] - b01.x, v[1] - b01.y);
-    const __half2 l23 = __floats2half2_rn(v[2] - b23.x, v[3] - b23.y);
-    a[0] = *reinterpret_cast<const uint32_t *>(&h01);
-    a[1] = *reinterpret_cast<const uint32_t *>(&l01);
-    a[2] = *reinterpret_cast<const uint32_t *>(&h23);
-    a[3] = *reinterpret_cast<const uint32_t *>(&l23);
-}
-
-// ---------------------------------------------------------------------------
-// softmax bookkeeping shared by the codecs.  s[i]: base-2 scores of this
-// lane's four tokens (4tig+i) for row gid, -inf when masked.  Returns the
-// probabilities p[i] after rescaling the accumulators when the max grows.
-// ---------------------------------------------------------------------------
-template <class Acc>
-__device__ __forceinline__ void online_softmax(const float (&s)[4], float (&p)[4], float &m, float &l,
-                                               Acc &acc) {
-    float tmax = fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3]));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-    const float m_new = fmaxf(m, tmax);
-    if (__any_sync(0xffffffffu, m_new > m)) {
-        const float alpha = ex2(m - m_new);
-        l *= alpha;
-        acc.rescale_all(alpha);
-        m = m_new;
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++) p[i] = ex2(s[i] - m);
-    l += (p[0] + p[1]) + (p[2] + p[3]);
-}
-
-// Value normaliser: nu is a power of two set from the first tile of the
-// segment; p*scale/nu is then an f16 of moderate size.  It is raised (with
-// an exact power-of-two rescale of the accumulators) only when a later scale
-// exceeds nu*2^14, which keeps p*scale/nu < 2^15 inside the f16 range.
-template <class Acc>
-__device__ __forceinline__ void update_nu(const float (&vs)[4], int x, Acc &acc) {
-    const float lmax = fmaxf(fmaxf(vs[0], vs[1]), fmaxf(vs[2], vs[3]));
-    const bool first = acc.nu[x] == 0.f;
-    if (__any_sync(0xffffffffu, first || lmax > acc.nu[x] * kNuHeadroom)) {
-        float vmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, 1));
-        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-        const float nn = fmaxf(pow2ceil(vmax), kNuFloor);
-        if (first) {
-            acc.nu[x] = nn;
-        } else if (nn > acc.nu[x]) {
-            acc.rescale_part(x, acc.nu[x] / nn);
-            acc.nu[x] = nn;
-        }
-        acc.inv_nu[x] = 1.0f / acc.nu[x];
-    }
-}
-
-// ---------------------------------------------------------------------------
-// codecs
-// ---------------------------------------------------------------------------
-template <int CODEC> struct Codec;
-
-// 4-bit codes, groups of 32 with fp16 range + fp16 min (2560-byte tile)
-template <> struct Codec<QWN_KV_CODEC_Q4_G32> {
-    static constexpr int kBytes = 2560, kStages = 6, kNu = 4;
-    struct Frag { uint32_t a[8][4]; float qsum[4]; };
-    struct Acc {
-        float o[16][4];
-        float z[4];  // sum_t p_t * min_t,g (this lane's tokens, row gid)
-        float nu[kNu], inv_nu[kNu];
-        __device__ void reset() {
-#pragma unroll
-            for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-#pragma unroll
-            for (int g = 0; g < 4; g++) { z[g] = 0.f; nu[g] = 0.f; inv_nu[g] = 0.f; }
-        }
-        __device__ void rescale_all(float f) {
-#pragma unroll
-            for (int j = 0; j < 16; j++) { o[j][0] *= f; o[j][1] *= f; o[j][2] *= f; o[j][3] *= f; }
-#pragma unroll
-            for (int g = 0; g < 4; g++) z[g] *= f;
-        }
-        __device__ void rescale_part(int g, float f) {
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int jj = 4 * g + j;
-                o[jj][0] *= f; o[jj][1] *= f; o[jj][2] *= f; o[jj][3] *= f;
-            }
-        }
-    };
-    __device__ static int dim_of(int j, int tig, int c) { return 8 * j + 2 * tig + c; }
-    // k-step s: group g = s>>1, dims 32g + 16(s&1) + 4tig + {0,1 | 2,3}
-    __device__ static void load_q(Frag &f, const float *q, int tig) {
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            float part = 0.f;
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                float v[4] = {0.f, 0.f, 0.f, 0.f};
-                if (q) {
-                    const float4 x = *reinterpret_cast<const float4 *>(q + 32 * g + 16 * e + 4 * tig);
-                    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-                }
-                part += (v[0] + v[1]) + (v[2] + v[3]);
-                make_a(v, f.a[2 * g + e]);
-            }
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
-            part += __shfl_xor_sync(0xffffffffu, part, 2);
-            f.qsum[g] = part;
-        }
-    }
-    // z[] must be reduced across the four lanes of a row before this is used
-    __device__ static float out_value(const Acc &acc, int j, int c, float zsum) {
-        return (acc.o[j][c] + acc.o[j][c + 2]) * acc.nu[j >> 2] + zsum;
-    }
-    __device__ static void qk(const uint8_t *tile, const Frag &f, float (&raw)[4]) {
-        const int lane = threadIdx.x & 31, tig = lane & 3;
-        const uint4 kw0 = *reinterpret_cast<const uint4 *>(tile + lane * 16);
-        const uint4 kw1 = *reinterpret_cast<const uint4 *>(tile + 512 + lane * 16);
-        const uint32_t w0[4] = {kw0.x, kw0.y, kw0.z, kw0.w}, w1[4] = {kw1.x, kw1.y, kw1.z, kw1.w};
-        raw[0] = raw[1] = raw[2] = raw[3] = 0.f;
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t r[4], u[4];
-            nib8_to_h2x4(w0[g], r);
-            nib8_to_h2x4(w1[g], u);
-            mma16816(c0, f.a[2 * g], r[0], r[1]);
-            mma16816(c1, f.a[2 * g], u[0], u[1]);
-            mma16816(c0, f.a[2 * g + 1], r[2], r[3]);
-            mma16816(c1, f.a[2 * g + 1], u[2], u[3]);
-            const uint4 kp = *reinterpret_cast<const uint4 *>(tile + 2048 + 64 * g + 16 * tig);
-            const float2 p0 = h2x2f(kp.x), p1 = h2x2f(kp.y), p2 = h2x2f(kp.z), p3 = h2x2f(kp.w);
-            const float zq = f.qsum[g];
-            raw[0] += p0.x * (1.0f / 15.0f) * (c0[0] + c0[2]) + p0.y * zq;
-            raw[1] += p1.x * (1.0f / 15.0f) * (c0[1] + c0[3]) + p1.y * zq;
-            raw[2] += p2.x * (1.0f / 15.0f) * (c1[0] + c1[2]) + p2.y * zq;
-            raw[3] += p3.x * (1.0f / 15.0f) * (c1[1] + c1[3]) + p3.y * zq;
-        }
-    }
-    __device__ static void pv(const uint8_t *tile, Acc &acc, const float (&p)[4], const bool (&ok)[4]) {
-        const int lane = threadIdx.x & 31, tig = lane & 3;
-        uint32_t a[4][4];
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            const uint4 vp = *reinterpret_cast<const uint4 *>(tile + 2304 + 64 * g + 16 * tig);
-            const float2 p0 = h2x2f(vp.x), p1 = h2x2f(vp.y), p2 = h2x2f(vp.z), p3 = h2x2f(vp.w);
-            float vs[4] = {p0.x * (1.0f / 15.0f), p1.x * (1.0f / 15.0f), p2.x * (1.0f / 15.0f),
-                           p3.x * (1.0f / 15.0f)};
-            const float mn[4] = {p0.y, p1.y, p2.y, p3.y};
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                vs[i] = ok[i] ? vs[i] : 0.f;
-                acc.z[g] += ok[i] ? p[i] * mn[i] : 0.f;
-            }
-            update_nu(vs, g, acc);
-            float pt[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) pt[i] = p[i] * vs[i] * acc.inv_nu[g];
-            make_a(pt, a[g]);
-        }
-        const uint8_t *vt = tile + 1024 + lane * 32;
-        const int sw = (lane >> 2) & 1;
-#pragma unroll
-        for (int cc = 0; cc < 2; cc++) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(vt + ((cc ^ sw) << 4));
-            const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                const int wi = 4 * cc + r;  // n-tiles 2wi, 2wi+1 (group wi>>1)
-                uint32_t b[4];
-                nib8_to_h2x4(wv[r], b);
-                mma16816(acc.o[2 * wi], a[wi >> 1], b[0], b[1]);
-                mma16816(acc.o[2 * wi + 1], a[wi >> 1], b[2], b[3]);
-            }
-        }
-    }
-};
-
-// one tile: scores, online softmax, P x V.  Returns the tile's probability
-// mass of this lane's tokens (for eviction scores).
-template <int CODEC>
-__device__ __forceinline__ float tile_step(const uint8_t *tile, const typename Codec<CODEC>::Frag &f,
-                                           typename Codec<CODEC>::Acc &acc, float &m, float &l, int t_lo,
-                                           int t_hi, float scale_log2) {
-    using CD = Codec<CODEC>;
-    const int tig = threadIdx.x & 3;
-    float raw[4];
-    CD::qk(tile, f, raw);
-    float s[4];
-    bool ok[4];
-    if (t_lo == 0 && t_hi == 16) {  // warp-uniform: full tile
-#pragma unroll
-        for (int i = 0; i < 4; i++) { s[i] = raw[i] * scale_log2; ok[i] = true; }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int t = 4 * tig + i;
-            ok[i] = t >= t_lo && t < t_hi;
-            s[i] = ok[i] ? raw[i] * scale_log2 : -INFINITY;
-        }
-    }
-    float p[4];
-    online_softmax(s, p, m, l, acc);
-    CD::pv(tile, acc, p, ok);
-    return (p[0] + p[1]) + (p[2] + p[3]);
-}
-
 // ---------------------------------------------------------------------------
 // int8 codecs (Q8_HEAD_F16, Q8_B64_F32): products with the tile as the A
 // operand.  The query heads of the GQA group fill the N columns, so one
@@ -624,6 +414,430 @@ struct Int8T {
 };
 
 // ---------------------------------------------------------------------------
+// low-bit codecs (Q4_G32, TQ35_G64): the same products as Int8T with the
+// codes in classes of 32 dims that share one scale -- codec 4 class = group
+// of 32; TurboQuant class = (group of 64, parity), even dims 4-bit codes
+// scaled by range/15, odd dims 3-bit codes by range/7.  Each class is one
+// k-block of the integer QK^T (codes 0..15 as u8, no bias) and two m-blocks
+// of P x V.  The query splits into three int8 slices at ratio 2^7
+// (q ~ s2 * (16384 c0 + 128 c1 + c2)), so the slice sums combine exactly in
+// int32 and each class needs one conversion; the class scale multiplies in
+// fp32 and the group minimum enters through the query sum (K) and through
+// z = sum_t p_t * min_t (V).
+// ---------------------------------------------------------------------------
+template <int CODEC, int HG>
+struct LowBitT {
+    static constexpr bool kTQ = CODEC == QWN_KV_CODEC_TQ35_G64;
+    static constexpr int kC = 4;               // classes of 32 dims
+    static constexpr int kG = kTQ ? 2 : 4;     // groups (min values)
+    static constexpr int kBytes = kTQ ? 2048 : 2560, kStages = kTQ ? 8 : 6;
+    struct Frag {
+        uint32_t b[HG][2][kC][2];  // [head group][n-block][class][reg]
+        float s2l[HG];             // unit slice scale x log2(e) x softmax scale
+        float qs[HG][kG];          // query sum per group, same factor
+    };
+    struct State {
+        float o[HG][8][4];
+        float z[HG][kG];  // sum_t p_t * min (this lane's tokens)
+        float m[HG], l[HG];
+        float nu[kC], inv_nu[kC];
+    };
+    // dim of (class c, index m)
+    __device__ static int dim_of(int c, int m) { return kTQ ? 64 * (c >> 1) + 2 * m + (c & 1) : 32 * c + m; }
+    __device__ static int group_of_class(int c) { return kTQ ? (c >> 1) : c; }
+
+    __device__ static void begin(Frag &f, State &st, const AttnArgs &A, uint32_t s_idx) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        const uint32_t G = A.group;
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            const uint32_t hq = 4 * hg + (gid >> 1);
+            // v[8c + i] = q[dim_of(c, 8 tig + i)]
+            float v[32];
+            if (hq < G) {
+                const float *q = A.query + ((size_t)s_idx * G + hq) * kHeadDim;
+                if constexpr (kTQ) {
+                    // dims 64x + 16tig + j: even j -> class 2x, odd -> 2x+1
+#pragma unroll
+                    for (int x = 0; x < 2; x++)
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; c4++) {
+                            const float4 w = *reinterpret_cast<const float4 *>(q + 64 * x + 16 * tig + 4 * c4);
+                            v[8 * (2 * x) + 2 * c4] = w.x;
+                            v[8 * (2 * x + 1) + 2 * c4] = w.y;
+                            v[8 * (2 * x) + 2 * c4 + 1] = w.z;
+                            v[8 * (2 * x + 1) + 2 * c4 + 1] = w.w;
+                        }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 4; c++)
+#pragma unroll
+                        for (int h2 = 0; h2 < 2; h2++) {
+                            const float4 w = *reinterpret_cast<const float4 *>(q + 32 * c + 8 * tig + 4 * h2);
+                            v[8 * c + 4 * h2] = w.x; v[8 * c + 4 * h2 + 1] = w.y;
+                            v[8 * c + 4 * h2 + 2] = w.z; v[8 * c + 4 * h2 + 3] = w.w;
+                        }
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) v[i] = 0.f;
+            }
+            float mx = 0.f;
+            int bad = 0;
+            float qs[kG];
+#pragma unroll
+            for (int g = 0; g < kG; g++) qs[g] = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                if (isfinite(v[i])) mx = fmaxf(mx, fabsf(v[i]));
+                else bad = 1;
+                qs[group_of_class(i >> 3)] += v[i];
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
+            bad |= __shfl_xor_sync(0xffffffffu, bad, 2);
+#pragma unroll
+            for (int g = 0; g < kG; g++) {
+                qs[g] += __shfl_xor_sync(0xffffffffu, qs[g], 1);
+                qs[g] += __shfl_xor_sync(0xffffffffu, qs[g], 2);
+            }
+            // slices: s1 = s0/128, s2 = s0/16384 exactly; |c1|, |c2| <= 64
+            const float s0 = mx > 0.f ? mx * (1.0f / 127.0f) : 1.0f;
+            const float inv0 = mx > 0.f ? 127.0f / mx : 1.0f;
+            constexpr float kRound = 12582912.0f;
+            uint32_t packed[3][8];
+            {
+                float s = s0, inv = inv0;
+#pragma unroll
+                for (int j = 0; j < 3; j++) {
+#pragma unroll
+                    for (int w = 0; w < 8; w++) {
+                        uint32_t bits[4];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int i = 4 * w + e;
+                            const float r = fmaf(v[i], inv, kRound);
+                            v[i] = fmaf(-(r - kRound), s, v[i]);
+                            bits[e] = __float_as_uint(r);
+                        }
+                        packed[j][w] = prmt(prmt(bits[0], bits[1], 0x0040u), prmt(bits[2], bits[3], 0x0040u), 0x5410u);
+                    }
+                    s = s * (1.0f / 128.0f);
+                    inv = inv * 128.0f;
+                }
+            }
+            // B columns: n-block 0 col gid = (head gid>>1, slice gid&1);
+            // n-block 1 col gid = (head gid>>1, slice 2) when gid even, else 0
+#pragma unroll
+            for (int c = 0; c < kC; c++) {
+                f.b[hg][0][c][0] = (gid & 1) ? packed[1][2 * c] : packed[0][2 * c];
+                f.b[hg][0][c][1] = (gid & 1) ? packed[1][2 * c + 1] : packed[0][2 * c + 1];
+                f.b[hg][1][c][0] = (gid & 1) ? 0u : packed[2][2 * c];
+                f.b[hg][1][c][1] = (gid & 1) ? 0u : packed[2][2 * c + 1];
+            }
+            // C side: this lane's head is 4hg + tig, held by the lanes gid = 2tig
+            const float hs0 = __shfl_sync(0xffffffffu, s0, 8 * tig);
+            const int hbad = __shfl_sync(0xffffffffu, bad, 8 * tig);
+            f.s2l[hg] = hbad ? __int_as_float(0x7fffffff) : hs0 * (1.0f / 16384.0f) * A.scale_log2;
+#pragma unroll
+            for (int g = 0; g < kG; g++) f.qs[hg][g] = __shfl_sync(0xffffffffu, qs[g], 8 * tig) * A.scale_log2;
+        }
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            st.m[hg] = -INFINITY;
+            st.l[hg] = 0.f;
+#pragma unroll
+            for (int g = 0; g < kG; g++) st.z[hg][g] = 0.f;
+#pragma unroll
+            for (int mb = 0; mb < 8; mb++) st.o[hg][mb][0] = st.o[hg][mb][1] = st.o[hg][mb][2] = st.o[hg][mb][3] = 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < kC; c++) { st.nu[c] = 0.f; st.inv_nu[c] = 0.f; }
+    }
+
+    // the three group-1 TurboQuant odd-code bits: bit 0 in bit 3 of each nibble
+    // of `odd`, bits 1-2 in the 2-bit fields of `plane` (field n -> nibble n)
+    __device__ static uint32_t tq_hi_codes(uint32_t odd, uint32_t plane) {
+        uint32_t s = plane & 0xFFFFu;
+        s = (s | (s << 8)) & 0x00FF00FFu;
+        s = (s | (s << 4)) & 0x0F0F0F0Fu;
+        s = (s | (s << 2)) & 0x33333333u;
+        return ((odd >> 3) & 0x11111111u) | (s << 1);
+    }
+
+    __device__ static void step(const uint8_t *tile, const Frag &f, State &st, int t_lo, int t_hi,
+                                float (&psum)[HG]) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        // ---- K code words of tokens gid (w0) and gid+8 (w1), per class
+        uint32_t kw[2][kC];
+        float kp[2][kC];  // class scale (range/15 or range/7) per token
+        float km[2][kG];  // group minimum per token
+        const uint8_t *kpar;
+        if constexpr (kTQ) {
+#pragma unroll
+            for (int tk = 0; tk < 2; tk++) {
+                const int t = gid + 8 * tk;
+                const uint2 ev = *reinterpret_cast<const uint2 *>(tile + 32 * t + 8 * tig);
+                const uint32_t od = *reinterpret_cast<const uint32_t *>(tile + 512 + 16 * t + 4 * tig);
+                const uint32_t pl = *reinterpret_cast<const uint16_t *>(tile + 768 + 8 * t + 2 * tig);
+                kw[tk][0] = ev.x;
+                kw[tk][1] = od & 0x77777777u;
+                kw[tk][2] = ev.y;
+                kw[tk][3] = tq_hi_codes(od, pl);
+            }
+            kpar = tile + 896;
+        } else {
+#pragma unroll
+            for (int tk = 0; tk < 2; tk++) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(tile + 64 * (gid + 8 * tk) + 16 * tig);
+                kw[tk][0] = w.x; kw[tk][1] = w.y; kw[tk][2] = w.z; kw[tk][3] = w.w;
+            }
+            kpar = tile + 2048;
+        }
+        // params of tokens gid, gid+8: (range16, min16) words [class or group][token]
+        {
+            uint32_t pw[kG][2];
+            if constexpr (kTQ) {
+                const uint4 p = *reinterpret_cast<const uint4 *>(kpar + 16 * gid);
+                pw[0][0] = p.x; pw[0][1] = p.y; pw[kG - 1][0] = p.z; pw[kG - 1][1] = p.w;
+            } else {
+                const uint4 p0 = *reinterpret_cast<const uint4 *>(kpar + 32 * gid);
+                const uint4 p1 = *reinterpret_cast<const uint4 *>(kpar + 32 * gid + 16);
+                pw[0][0] = p0.x; pw[0][1] = p0.y; pw[1][0] = p0.z; pw[1][1] = p0.w;
+                pw[kG - 2][0] = p1.x; pw[kG - 2][1] = p1.y; pw[kG - 1][0] = p1.z; pw[kG - 1][1] = p1.w;
+            }
+#pragma unroll
+            for (int g = 0; g < kG; g++)
+#pragma unroll
+                for (int tk = 0; tk < 2; tk++) {
+                    const float2 rm = h2x2f(pw[g][tk]);
+                    km[tk][g] = rm.y;
+                    if constexpr (kTQ) {
+                        kp[tk][2 * g] = rm.x * (1.0f / 15.0f);
+                        kp[tk][2 * g + 1] = rm.x * (1.0f / 7.0f);
+                    } else {
+                        kp[tk][g] = rm.x * (1.0f / 15.0f);
+                    }
+                }
+        }
+        const bool full = t_lo == 0 && t_hi == 16;  // warp-uniform
+        const bool ok0 = full || (gid >= t_lo && gid < t_hi);
+        const bool ok1 = full || (gid + 8 >= t_lo && gid + 8 < t_hi);
+        // ---- scores
+        float s[HG][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float raw[2] = {0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < kC; c++) {
+                const uint32_t a0 = kw[0][c] & 0x0F0F0F0Fu, a1 = kw[1][c] & 0x0F0F0F0Fu;
+                const uint32_t a2 = (kw[0][c] >> 4) & 0x0F0F0F0Fu, a3 = (kw[1][c] >> 4) & 0x0F0F0F0Fu;
+                int acc[2][4];
+#pragma unroll
+                for (int nb = 0; nb < 2; nb++) imma16832_z(acc[nb], a0, a1, a2, a3, f.b[hg][nb][c][0], f.b[hg][nb][c][1]);
+#pragma unroll
+                for (int tk = 0; tk < 2; tk++) {
+                    // columns 2tig (slice 0 | slice 2) and 2tig+1 (slice 1)
+                    const int I = (acc[0][2 * tk] * 128 + acc[0][2 * tk + 1]) * 128 + acc[1][2 * tk];
+                    raw[tk] = fmaf(__int2float_rn(I), kp[tk][c], raw[tk]);
+                }
+            }
+#pragma unroll
+            for (int tk = 0; tk < 2; tk++) {
+                float sc = raw[tk] * f.s2l[hg];
+#pragma unroll
+                for (int g = 0; g < kG; g++) sc = fmaf(km[tk][g], f.qs[hg][g], sc);
+                s[hg][tk] = (tk ? ok1 : ok0) ? sc : -INFINITY;
+            }
+        }
+        // ---- online softmax per head
+        float p[HG][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float tmax = fmaxf(s[hg][0], s[hg][1]);
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+            const float m_new = fmaxf(st.m[hg], tmax);
+            if (__any_sync(0xffffffffu, m_new > st.m[hg])) {
+                const float alpha = ex2(st.m[hg] - m_new);
+                st.l[hg] *= alpha;
+#pragma unroll
+                for (int g = 0; g < kG; g++) st.z[hg][g] *= alpha;
+#pragma unroll
+                for (int mb = 0; mb < 8; mb++) {
+                    st.o[hg][mb][0] *= alpha; st.o[hg][mb][1] *= alpha;
+                    st.o[hg][mb][2] *= alpha; st.o[hg][mb][3] *= alpha;
+                }
+                st.m[hg] = m_new;
+            }
+            p[hg][0] = ex2(s[hg][0] - st.m[hg]);
+            p[hg][1] = ex2(s[hg][1] - st.m[hg]);
+            st.l[hg] += p[hg][0] + p[hg][1];
+            psum[hg] = p[hg][0] + p[hg][1];
+        }
+        // ---- V params: class scales and group minima of tokens gid, gid+8
+        float vp[2][kC], vm[2][kG];
+        {
+            const uint8_t *vpar = kTQ ? tile + 1024 + 896 : tile + 2304;
+            uint32_t pw[kG][2];
+            if constexpr (kTQ) {
+                const uint4 q4 = *reinterpret_cast<const uint4 *>(vpar + 16 * gid);
+                pw[0][0] = q4.x; pw[0][1] = q4.y; pw[kG - 1][0] = q4.z; pw[kG - 1][1] = q4.w;
+            } else {
+                const uint4 p0 = *reinterpret_cast<const uint4 *>(vpar + 32 * gid);
+                const uint4 p1 = *reinterpret_cast<const uint4 *>(vpar + 32 * gid + 16);
+                pw[0][0] = p0.x; pw[0][1] = p0.y; pw[1][0] = p0.z; pw[1][1] = p0.w;
+                pw[kG - 2][0] = p1.x; pw[kG - 2][1] = p1.y; pw[kG - 1][0] = p1.z; pw[kG - 1][1] = p1.w;
+            }
+#pragma unroll
+            for (int g = 0; g < kG; g++)
+#pragma unroll
+                for (int tk = 0; tk < 2; tk++) {
+                    const bool ok = tk ? ok1 : ok0;
+                    const float2 rm = h2x2f(pw[g][tk]);
+                    vm[tk][g] = ok ? rm.y : 0.f;
+                    if constexpr (kTQ) {
+                        vp[tk][2 * g] = ok ? rm.x * (1.0f / 15.0f) : 0.f;
+                        vp[tk][2 * g + 1] = ok ? rm.x * (1.0f / 7.0f) : 0.f;
+                    } else {
+                        vp[tk][g] = ok ? rm.x * (1.0f / 15.0f) : 0.f;
+                    }
+                }
+        }
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++)
+#pragma unroll
+            for (int g = 0; g < kG; g++) st.z[hg][g] = fmaf(p[hg][0], vm[0][g], fmaf(p[hg][1], vm[1][g], st.z[hg][g]));
+        // ---- normalisers per class (shared by all heads)
+        {
+            float lmax[kC];
+            bool need = false;
+#pragma unroll
+            for (int c = 0; c < kC; c++) {
+                lmax[c] = fmaxf(vp[0][c], vp[1][c]);
+                need |= st.nu[c] == 0.f || lmax[c] > st.nu[c] * kNuHeadroom;
+            }
+            if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+                for (int c = 0; c < kC; c++) {
+                    float vmax = fmaxf(lmax[c], __shfl_xor_sync(0xffffffffu, lmax[c], 4));
+                    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 8));
+                    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 16));
+                    const float nn = fmaxf(pow2ceil(vmax), kNuFloor);
+                    if (st.nu[c] == 0.f) {
+                        st.nu[c] = nn;
+                    } else if (nn > st.nu[c]) {
+                        const float r = st.nu[c] / nn;
+#pragma unroll
+                        for (int hg = 0; hg < HG; hg++)
+#pragma unroll
+                            for (int h2 = 0; h2 < 2; h2++) {
+                                float *o = st.o[hg][2 * c + h2];
+                                o[0] *= r; o[1] *= r; o[2] *= r; o[3] *= r;
+                            }
+                        st.nu[c] = nn;
+                    }
+                    st.inv_nu[c] = 1.0f / st.nu[c];
+                }
+            }
+        }
+        // ---- P' per class as f16 hi+lo, transposed into the PV B operand
+        uint32_t bp[HG][kC][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++)
+#pragma unroll
+            for (int c = 0; c < kC; c++) {
+                const float pt0 = p[hg][0] * vp[0][c] * st.inv_nu[c];
+                const float pt1 = p[hg][1] * vp[1][c] * st.inv_nu[c];
+                const __half2 hi = __floats2half2_rn(pt0, pt1);
+                const float2 hf = __half22float2(hi);
+                const __half2 lo = __floats2half2_rn(pt0 - hf.x, pt1 - hf.y);
+                const uint32_t hu = *reinterpret_cast<const uint32_t *>(&hi);
+                const uint32_t lu = *reinterpret_cast<const uint32_t *>(&lo);
+                bp[hg][c][0] = movmatrix_trans(prmt(hu, lu, 0x5410u));
+                bp[hg][c][1] = movmatrix_trans(prmt(hu, lu, 0x7632u));
+            }
+        // ---- V code words per m-block -> exact f16 A fragments; P x V
+        uint32_t vw[8];
+        if constexpr (kTQ) {
+            const uint8_t *vh = tile + 1024;
+            const uint4 ev = *reinterpret_cast<const uint4 *>(vh + 16 * lane);
+            const uint2 od = *reinterpret_cast<const uint2 *>(vh + 512 + 8 * lane);
+            const uint32_t pl = *reinterpret_cast<const uint32_t *>(vh + 768 + 4 * lane);
+            vw[0] = ev.x; vw[1] = ev.y;                    // class 0 (group 0, even)
+            vw[2] = od.x & 0x77777777u; vw[3] = od.y & 0x77777777u;  // class 1 (group 0, odd)
+            vw[4] = ev.z; vw[5] = ev.w;                    // class 2 (group 1, even)
+            vw[6] = tq_hi_codes(od.x, pl); vw[7] = tq_hi_codes(od.y, pl >> 16);  // class 3
+        } else {
+            const uint8_t *vt = tile + 1024 + lane * 32;
+            const int sw = (lane >> 2) & 1;
+            const uint4 c0 = *reinterpret_cast<const uint4 *>(vt + ((0 ^ sw) << 4));
+            const uint4 c1 = *reinterpret_cast<const uint4 *>(vt + ((1 ^ sw) << 4));
+            vw[0] = c0.x; vw[1] = c0.y; vw[2] = c0.z; vw[3] = c0.w;
+            vw[4] = c1.x; vw[5] = c1.y; vw[6] = c1.z; vw[7] = c1.w;
+        }
+#pragma unroll
+        for (int mb = 0; mb < 8; mb++) {
+            uint32_t a[4];
+            nib8_to_h2x4(vw[mb], a);
+#pragma unroll
+            for (int hg = 0; hg < HG; hg++) mma16816(st.o[hg][mb], a, bp[hg][mb >> 1][0], bp[hg][mb >> 1][1]);
+        }
+    }
+
+    __device__ static void mass(const AttnArgs &A, uint64_t unit, const State &st, float (&psum)[HG]) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float u = psum[hg];
+            u += __shfl_xor_sync(0xffffffffu, u, 4);
+            u += __shfl_xor_sync(0xffffffffu, u, 8);
+            u += __shfl_xor_sync(0xffffffffu, u, 16);
+            const uint32_t h = 4 * hg + tig;
+            if (gid == 0 && h < A.group) A.tile_mass[unit * kMaxGroup + h] = make_float2(u, st.m[hg]);
+        }
+    }
+
+    __device__ static void store_rows(const AttnArgs &A, const State &st, float *o_base, float *m_out, float *l_out,
+                                      bool normalize, float2 *seg_ml) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float lt = st.l[hg];
+            lt += __shfl_xor_sync(0xffffffffu, lt, 4);
+            lt += __shfl_xor_sync(0xffffffffu, lt, 8);
+            lt += __shfl_xor_sync(0xffffffffu, lt, 16);
+            float zt[kG];
+#pragma unroll
+            for (int g = 0; g < kG; g++) {
+                float z = st.z[hg][g];
+                z += __shfl_xor_sync(0xffffffffu, z, 4);
+                z += __shfl_xor_sync(0xffffffffu, z, 8);
+                z += __shfl_xor_sync(0xffffffffu, z, 16);
+                zt[g] = z;
+            }
+            const uint32_t h = 4 * hg + tig;
+            if (h >= A.group) continue;
+            const float inv = normalize ? (lt > 0.f ? 1.0f / lt : 0.f) : 1.0f;
+            float *row = o_base + (size_t)h * kHeadDim;
+#pragma unroll
+            for (int mb = 0; mb < 8; mb++) {
+                const int c = mb >> 1, g = group_of_class(c);
+                const int m0 = 16 * (mb & 1) + gid;
+                row[dim_of(c, m0)] = ((st.o[hg][mb][0] + st.o[hg][mb][1]) * st.nu[c] + zt[g]) * inv;
+                row[dim_of(c, m0 + 8)] = ((st.o[hg][mb][2] + st.o[hg][mb][3]) * st.nu[c] + zt[g]) * inv;
+            }
+            if (gid == 0) {
+                if (m_out) { m_out[h] = st.m[hg]; l_out[h] = lt; }
+                if (seg_ml) seg_ml[h] = make_float2(st.m[hg], lt);
+            }
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------
 // per-codec operations used by the kernel: begin (load the query rows of a
 // segment, reset the state), step (one tile), mass (eviction scores of the
 // tile), store_rows (the segment's G output rows, or a partial)
@@ -631,61 +845,10 @@ struct Int8T {
 template <int CODEC, int HG>
 struct Ops : Int8T<CODEC, HG> {};
 
-// 4-bit codes: query heads in the M rows (hi rows 0..G-1, lo rows 8..8+G-1)
 template <int HG>
-struct Ops<QWN_KV_CODEC_Q4_G32, HG> {
-    using CD = Codec<QWN_KV_CODEC_Q4_G32>;
-    static constexpr int kBytes = CD::kBytes, kStages = CD::kStages;
-    struct Frag { typename CD::Frag f; float scale_log2; };
-    struct State { typename CD::Acc acc; float m, l; };
-    __device__ static void begin(Frag &f, State &st, const AttnArgs &A, uint32_t s_idx) {
-        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-        const float *q = (uint32_t)gid < A.group ? A.query + ((size_t)s_idx * A.group + gid) * kHeadDim : nullptr;
-        CD::load_q(f.f, q, tig);
-        f.scale_log2 = A.scale_log2;
-        st.acc.reset();
-        st.m = -INFINITY;
-        st.l = 0.f;
-    }
-    __device__ static void step(const uint8_t *tile, const Frag &f, State &st, int t_lo, int t_hi,
-                                float (&psum)[HG]) {
-        psum[0] = tile_step<QWN_KV_CODEC_Q4_G32>(tile, f.f, st.acc, st.m, st.l, t_lo, t_hi, f.scale_log2);
-    }
-    __device__ static void mass(const AttnArgs &A, uint64_t unit, const State &st, float (&psum)[HG]) {
-        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-        float u = psum[0];
-        u += __shfl_xor_sync(0xffffffffu, u, 1);
-        u += __shfl_xor_sync(0xffffffffu, u, 2);
-        if (tig == 0 && (uint32_t)gid < A.group) A.tile_mass[unit * kMaxGroup + gid] = make_float2(u, st.m);
-    }
-    __device__ static void store_rows(const AttnArgs &A, const State &st, float *o_base, float *m_out, float *l_out,
-                                      bool normalize, float2 *seg_ml) {
-        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-        float lr = st.l;
-        lr += __shfl_xor_sync(0xffffffffu, lr, 1);
-        lr += __shfl_xor_sync(0xffffffffu, lr, 2);
-        float zs[4];
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            float z = st.acc.z[g];
-            z += __shfl_xor_sync(0xffffffffu, z, 1);
-            z += __shfl_xor_sync(0xffffffffu, z, 2);
-            zs[g] = z;
-        }
-        if ((uint32_t)gid >= A.group) return;
-        const float inv = normalize ? (lr > 0.f ? 1.0f / lr : 0.f) : 1.0f;
-        float *o = o_base + (size_t)gid * kHeadDim;
-#pragma unroll
-        for (int jn = 0; jn < 16; jn++)
-            *reinterpret_cast<float2 *>(o + CD::dim_of(jn, tig, 0)) =
-                make_float2(CD::out_value(st.acc, jn, 0, zs[jn >> 2]) * inv,
-                            CD::out_value(st.acc, jn, 1, zs[jn >> 2]) * inv);
-        if (tig == 0) {
-            if (m_out) { m_out[gid] = st.m; l_out[gid] = lr; }
-            if (seg_ml) seg_ml[gid] = make_float2(st.m, lr);
-        }
-    }
-};
+struct Ops<QWN_KV_CODEC_Q4_G32, HG> : LowBitT<QWN_KV_CODEC_Q4_G32, HG> {};
+template <int HG>
+struct Ops<QWN_KV_CODEC_TQ35_G64, HG> : LowBitT<QWN_KV_CODEC_TQ35_G64, HG> {};
 
 // ---------------------------------------------------------------------------
 // batch geometry
@@ -1172,26 +1335,22 @@ constexpr size_t codec_smem() {
     return (size_t)kWarpsPerCta * O::kStages * (O::kBytes + 8) + (size_t)kWarpsPerCta * sizeof(WarpWindow);
 }
 
-// kernel variants: head groups of four query heads (int8 codecs), one for Q4
+// kernel variants: one or two head groups of four query heads
 template <int CODEC>
 cudaError_t configure_codec() {
     const int smem = (int)codec_smem<CODEC>();
     cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if constexpr (CODEC != QWN_KV_CODEC_Q4_G32)
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(attn_kernel<CODEC, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_kernel<CODEC, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     return e;
 }
 template <int CODEC>
 cudaError_t launch_variant(uint32_t ctas, const AttnArgs &A, cudaStream_t s) {
     const size_t smem = codec_smem<CODEC>();
-    if constexpr (CODEC != QWN_KV_CODEC_Q4_G32) {
-        if (A.group > 4) {
-            attn_kernel<CODEC, 2><<<ctas, kWarpsPerCta * 32, smem, s>>>(A);
-            return cudaGetLastError();
-        }
-    }
-    attn_kernel<CODEC, 1><<<ctas, kWarpsPerCta * 32, smem, s>>>(A);
+    if (A.group > 4)
+        attn_kernel<CODEC, 2><<<ctas, kWarpsPerCta * 32, smem, s>>>(A);
+    else
+        attn_kernel<CODEC, 1><<<ctas, kWarpsPerCta * 32, smem, s>>>(A);
     return cudaGetLastError();
 }
 
@@ -1215,6 +1374,7 @@ size_t attention_smem_bytes(uint32_t codec) {
         case QWN_KV_CODEC_Q8_HEAD_F16: return codec_smem<QWN_KV_CODEC_Q8_HEAD_F16>();
         case QWN_KV_CODEC_Q8_B64_F32: return codec_smem<QWN_KV_CODEC_Q8_B64_F32>();
         case QWN_KV_CODEC_Q4_G32: return codec_smem<QWN_KV_CODEC_Q4_G32>();
+        case QWN_KV_CODEC_TQ35_G64: return codec_smem<QWN_KV_CODEC_TQ35_G64>();
         default: return 0;
     }
 }
@@ -1224,6 +1384,7 @@ const void *attention_kernel_ptr(uint32_t codec) {
         case QWN_KV_CODEC_Q8_HEAD_F16: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16, 1>;
         case QWN_KV_CODEC_Q8_B64_F32: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32, 1>;
         case QWN_KV_CODEC_Q4_G32: return (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 1>;
+        case QWN_KV_CODEC_TQ35_G64: return (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 1>;
         default: return nullptr;
     }
 }
@@ -1266,6 +1427,7 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
         case QWN_KV_CODEC_Q8_HEAD_F16: return launch_codec<QWN_KV_CODEC_Q8_HEAD_F16>(p, A, s);
         case QWN_KV_CODEC_Q8_B64_F32: return launch_codec<QWN_KV_CODEC_Q8_B64_F32>(p, A, s);
         case QWN_KV_CODEC_Q4_G32: return launch_codec<QWN_KV_CODEC_Q4_G32>(p, A, s);
+        case QWN_KV_CODEC_TQ35_G64: return launch_codec<QWN_KV_CODEC_TQ35_G64>(p, A, s);
         default: return cudaErrorNotSupported;
     }
 }
@@ -1334,7 +1496,7 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
     using namespace qkv;
     if (!r || !header_ok(r->header, sizeof(*r))) return QWN_CUDA_STATUS_ABI_MISMATCH;
     const size_t tb = tile_bytes_of(r->codec);
-    if (!tb || r->codec == QWN_KV_CODEC_TQ35_G64 || r->head_dim != (uint32_t)kHeadDim || r->kv_heads == 0 ||
+    if (!tb || r->head_dim != (uint32_t)kHeadDim || r->kv_heads == 0 ||
         r->page_tokens == 0 || r->page_tokens % 16 || r->layer >= r->layers || r->query_heads == 0 ||
         r->query_heads % r->kv_heads || r->query_heads / r->kv_heads > (uint32_t)kMaxGroup || !r->pages_dev ||
         !r->page_table_dev || !r->seq_lens_dev || !r->query_dev || !r->output_dev || r->total_pages == 0 ||
@@ -1364,7 +1526,8 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
             }
             if ((e = static_setup<QWN_KV_CODEC_Q8_B64_F32>(dev)) != cudaSuccess ||
                 (e = static_setup<QWN_KV_CODEC_Q8_HEAD_F16>(dev)) != cudaSuccess ||
-                (e = static_setup<QWN_KV_CODEC_Q4_G32>(dev)) != cudaSuccess) {
+                (e = static_setup<QWN_KV_CODEC_Q4_G32>(dev)) != cudaSuccess ||
+                (e = static_setup<QWN_KV_CODEC_TQ35_G64>(dev)) != cudaSuccess) {
                 set_cuda_error("qwn_kv_attention_static: kernel set-up", e);
                 return QWN_CUDA_STATUS_RUNTIME_ERROR;
             }
@@ -1407,7 +1570,8 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
     switch (r->codec) {
         case QWN_KV_CODEC_Q8_HEAD_F16: e = launch_variant<QWN_KV_CODEC_Q8_HEAD_F16>(ctas, A, s); break;
         case QWN_KV_CODEC_Q8_B64_F32: e = launch_variant<QWN_KV_CODEC_Q8_B64_F32>(ctas, A, s); break;
-        default: e = launch_variant<QWN_KV_CODEC_Q4_G32>(ctas, A, s); break;
+        case QWN_KV_CODEC_Q4_G32: e = launch_variant<QWN_KV_CODEC_Q4_G32>(ctas, A, s); break;
+        default: e = launch_variant<QWN_KV_CODEC_TQ35_G64>(ctas, A, s); break;
     }
     count_launch();
     if (e != cudaSuccess) {

@@ -551,10 +551,6 @@ static int decode_impl(Pool *p, const QwnKvDecodeRequest *r, cudaStream_t s) {
         set_error("qwn_kv_decode: invalid request");
         return QWN_CUDA_STATUS_INVALID_ARGUMENT;
     }
-    if (p->codec == QWN_KV_CODEC_TQ35_G64 && !attention_kernel_ptr(p->codec)) {
-        set_error("qwn_kv_decode: codec has no attention kernel in this build");
-        return QWN_CUDA_STATUS_UNSUPPORTED;
-    }
     cudaError_t e = cudaSuccess;
     // attention over the whole sequence ends in the tile of the newest token:
     // the attention kernel quantizes and stores it before reading that tile

@@ -132,87 +132,77 @@ __device__ void store_token<QWN_KV_CODEC_Q8_B64_F32>(uint8_t *tile, int t, float
     }
 }
 
+// 4-bit groups of 32: lane L holds dims 4L..4L+3, group c = L>>3.  K word
+// (t, tig = (L&7)>>1, c) at 64t + 16tig + 4c takes dim i of lane L in the low
+// nibble of byte i (L even) or the high nibble (L odd).  V: the byte for
+// (t, m-block, row gid) holds rows gid (lanes with L&2 == 0) and gid+8 (L+2).
 template <>
 __device__ void store_token<QWN_KV_CODEC_Q4_G32>(uint8_t *tile, int t, float4 k, float4 v, int lane) {
-    // K
-    {
-        float mn, mx;
-        minmax_first(k, lane, 8, mn, mx);
-        const float range = __fsub_rn(mx, mn);
-        const float inv = range > 1e-8f ? __fdiv_rn(1.0f, range) : 0.f;
-        const uint32_t c0 = tq_code(k.x, mn, inv, 15.f), c1 = tq_code(k.y, mn, inv, 15.f);
-        const uint32_t c2 = tq_code(k.z, mn, inv, 15.f), c3 = tq_code(k.w, mn, inv, 15.f);
-        const int n = 2 * (t >> 2) + (t & 1), h = (t >> 1) & 1;
-        const int g = lane >> 3, e = (lane >> 2) & 1, tg = lane & 3;
-        uint8_t *base = tile + h * 512 + (n * 4 + tg) * 16 + g * 4;
-        base[e] = (uint8_t)(c0 | (c2 << 4));
-        base[2 + e] = (uint8_t)(c1 | (c3 << 4));
-        if ((lane & 7) == 0)
-            *reinterpret_cast<uint32_t *>(tile + 2048 + 64 * g + 4 * t) =
-                (uint32_t)tq_f32_to_f16(range) | ((uint32_t)tq_f32_to_f16(mn) << 16);
-    }
-    // V
-    {
-        float mn, mx;
-        minmax_first(v, lane, 8, mn, mx);
-        const float range = __fsub_rn(mx, mn);
-        const float inv = range > 1e-8f ? __fdiv_rn(1.0f, range) : 0.f;
-        const float vv[4] = {v.x, v.y, v.z, v.w};
+    const int c = lane >> 3;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int d = 4 * lane + i;
-            const uint32_t code = tq_code(vv[i], mn, inv, 15.f);
-            const int gidd = d & 7, j = d >> 3, lv = gidd * 4 + (t >> 2), b = t & 3;
-            const int w = j >> 1, e = j & 1;
-            const int pos = (b & 1) * 4 + e * 2 + (b >> 1);
-            const int chunk = (w >> 2) ^ ((lv >> 2) & 1);
-            const uint32_t byte = 1024 + lv * 32 + chunk * 16 + (w & 3) * 4 + (pos >> 1);
-            put_bits(tile, byte, (pos & 1) * 4, 0xFu, code);
+    for (int which = 0; which < 2; which++) {
+        const float4 x4 = which ? v : k;
+        float mn, mx;
+        minmax_first(x4, lane, 8, mn, mx);
+        const float range = __fsub_rn(mx, mn);
+        const float inv = range > 1e-8f ? __fdiv_rn(1.0f, range) : 0.f;
+        const uint32_t q[4] = {tq_code(x4.x, mn, inv, 15.f), tq_code(x4.y, mn, inv, 15.f),
+                               tq_code(x4.z, mn, inv, 15.f), tq_code(x4.w, mn, inv, 15.f)};
+        if (!which) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t hi = __shfl_down_sync(0xffffffffu, q[i], 1);
+                word |= (q[i] | (hi << 4)) << (8 * i);
+            }
+            if (!(lane & 1))
+                *reinterpret_cast<uint32_t *>(tile + 64 * t + 16 * ((lane & 7) >> 1) + 4 * c) = word;
+        } else {
+            const int mb = 2 * c + ((lane & 7) >> 2);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t hi = __shfl_down_sync(0xffffffffu, q[i], 2);
+                if (!(lane & 2)) {
+                    const int lv = 4 * (4 * (lane & 1) + i) + ((t & 7) >> 1);
+                    const int chunk = (mb >> 2) ^ ((lv >> 2) & 1);
+                    tile[1024 + 32 * lv + 16 * chunk + 4 * (mb & 3) + (t >> 3) + 2 * (t & 1)] =
+                        (uint8_t)(q[i] | (hi << 4));
+                }
+            }
         }
-        if ((lane & 7) == 0) {
-            const int g = lane >> 3;
-            *reinterpret_cast<uint32_t *>(tile + 2304 + 64 * g + 4 * t) =
+        if ((lane & 7) == 0)
+            *reinterpret_cast<uint32_t *>(tile + (which ? 2304 : 2048) + 32 * (t & 7) + 8 * c + 4 * (t >> 3)) =
                 (uint32_t)tq_f32_to_f16(range) | ((uint32_t)tq_f32_to_f16(mn) << 16);
-        }
     }
 }
 
-// 3.5-bit reference TurboQuant codes in the tile layout (see qwn_oracle.c)
+// 3.5-bit reference TurboQuant codes in the tile layout (restated in
+// qwn_oracle.c): class c = 2*(d>>6) + (d&1), index m = (d&63)>>1
+__device__ __forceinline__ int lb_k_nibble(int m) { return 2 * (m & 3) + ((m >> 2) & 1); }
 __device__ void tq35_put(uint8_t *half, int is_value, int t, int d, uint32_t code) {
+    const int x = d >> 6, m = (d & 63) >> 1;
+    uint32_t eb, ob, pb, n;
     if (!is_value) {
-        const int h = (t >> 1) & 1, n = 2 * (t >> 2) + (t & 1);
-        const int x = d >> 6, tg = (d >> 4) & 3, k = d & 15;
-        const int slot = h * 32 + n * 4 + tg;
-        const int e = k >> 1, np = (e & 1) * 4 + (e >> 1);
-        if (!(k & 1)) {
-            put_bits(half, slot * 8 + x * 4 + (np >> 1), (np & 1) * 4, 0xFu, code);
-        } else {
-            const uint32_t byte = 512 + slot * 4 + (np >> 1), sh = (np & 1) * 4;
-            if (x == 0) {
-                put_bits(half, byte, sh, 0x7u, code);
-            } else {
-                put_bits(half, byte, sh + 3, 0x1u, code & 1u);
-                const uint32_t hb = 768 + slot * 2;  // 16-bit field, bits 2*np
-                put_bits(half, hb + ((2 * np) >> 3), (2 * np) & 7, 0x3u, code >> 1);
-            }
-        }
+        const int tig = m >> 3;
+        n = (uint32_t)lb_k_nibble(m);
+        eb = 32 * t + 8 * tig + 4 * x;
+        ob = 512 + 16 * t + 4 * tig;
+        pb = 768 + 8 * t + 2 * tig;
     } else {
-        const int x = d >> 6, r = d & 63, par = r & 1, q = r >> 1, gidd = q & 7, jl = q >> 3;
-        const int lv = gidd * 4 + (t >> 2), b = t & 3;
-        if (!par) {
-            const int col = x * 4 + jl, np = (b & 1) * 4 + (col & 1) * 2 + (b >> 1);
-            put_bits(half, lv * 16 + (col >> 1) * 4 + (np >> 1), (np & 1) * 4, 0xFu, code);
-        } else {
-            const int npos = (b & 1) * 4 + (jl & 1) * 2 + (b >> 1);
-            const uint32_t byte = 512 + lv * 8 + (jl >> 1) * 4 + (npos >> 1), sh = (npos & 1) * 4;
-            if (x == 0) {
-                put_bits(half, byte, sh, 0x7u, code);
-            } else {
-                put_bits(half, byte, sh + 3, 0x1u, code & 1u);
-                const int bitpos = 2 * ((jl >> 1) * 8 + npos);
-                put_bits(half, 768 + lv * 4 + (bitpos >> 3), bitpos & 7, 0x3u, code >> 1);
-            }
-        }
+        const int c = 2 * x + (d & 1), r = m & 15, mb = 2 * c + (m >> 4);
+        const int lv = ((r & 7) << 2) | ((t & 7) >> 1);
+        n = (uint32_t)((r >> 3) + 2 * (t >> 3) + 4 * (t & 1));
+        eb = 16 * lv + 4 * (2 * x + (mb & 1));
+        ob = 512 + 8 * lv + 4 * (mb & 1);
+        pb = 768 + 4 * lv + 2 * (mb & 1);
+    }
+    if (!(d & 1)) {
+        put_bits(half, eb + (n >> 1), (n & 1) * 4, 0xFu, code);
+    } else if (x == 0) {
+        put_bits(half, ob + (n >> 1), (n & 1) * 4, 0x7u, code);
+    } else {
+        put_bits(half, ob + (n >> 1), (n & 1) * 4 + 3, 0x1u, code & 1u);
+        put_bits(half, pb + ((2 * n) >> 3), (2 * n) & 7, 0x3u, code >> 1);
     }
 }
 
@@ -235,7 +225,7 @@ __device__ void store_token<QWN_KV_CODEC_TQ35_G64>(uint8_t *tile, int t, float4 
         }
         if ((lane & 15) == 0) {
             const int x = lane >> 4;
-            *reinterpret_cast<uint32_t *>(half + 896 + 64 * x + 4 * t) =
+            *reinterpret_cast<uint32_t *>(half + 896 + 16 * (t & 7) + 8 * x + 4 * (t >> 3)) =
                 (uint32_t)tq_f32_to_f16(range) | ((uint32_t)tq_f32_to_f16(mn) << 16);
         }
     }

@@ -12,7 +12,7 @@ from kvharness import Twin, assert_close
 
 pytestmark = pytest.mark.gpu
 
-CODECS = [1, 2, 4]
+CODECS = [1, 2, 3, 4]
 
 
 def test_generator_bit_exact(cuda, oracle_mod):
