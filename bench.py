@@ -36,6 +36,19 @@ HD = 128
 
 
 def workload(cfg: int) -> dict:
+    if cfg == 1:
+        return dict(name="cfg1 Qwen2-1.5B-shaped single-layer decode, 1 sequence from 2048 tokens, "
+                         "int8 per-token-head KV + fp16 scale", codec=2, layers=1, H=12, HK=2, P=16, batch=1,
+                    lo=2048, hi=2048, seed=1, outliers=0, steps=256)
+    if cfg == 4:
+        return dict(name="cfg4 27B-shaped long-context single sequence, 131072 tokens, page 64, "
+                         "int8 per-token-head KV + fp16 scale, split-KV across GPUs", codec=2, layers=1, H=48,
+                    HK=8, P=64, batch=1, lo=131072, hi=131072, seed=4, outliers=0, steps=50)
+    if cfg == 5:
+        return dict(name="cfg5 page-pool churn: 1,048,576 pages x 16 tokens, 256 sequences, append + attend, "
+                         "p=0.05 score-based eviction to 2048 tokens + compaction", codec=2, layers=1, H=32, HK=8,
+                    P=16, batch=256, lo=2048, hi=4096, seed=5, outliers=0, steps=50, pool_pages=1 << 20,
+                    evict_p=0.05, budget=2048)
     if cfg == 2:
         return dict(name="cfg2 Qwen3-4B-shaped batched decode, int8 per-token-head KV + fp16 scale",
                     codec=2, layers=36, H=32, HK=8, P=16, batch=32, lo=1024, hi=8192, seed=2,
@@ -176,8 +189,9 @@ def run_reference(args, wl, world, rank):
     if rank != 0:
         return 0
     lens = global_lengths(wl, 1)
-    layers_sample = 2
-    res = reference_rate(wl, lens, max(1, args.steps), max(0, args.warmup), layers_sample)
+    layers_sample = min(2, wl["layers"])
+    steps = max(1, min(args.steps, 20)) if wl["batch"] * wl["lo"] > 100000 else max(1, args.steps)
+    res = reference_rate(wl, lens, steps, max(0, args.warmup), layers_sample)
     if res is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (the reference CPU library) is not built"}))
         return 0
@@ -357,7 +371,8 @@ def run_ours(args, wl, world, rank, local):
                        "layers": L, "query_heads": H, "kv_heads": HK, "head_dim": HD, "page_tokens": P,
                        "context": f"U[{wl['lo']},{wl['hi']}] (+{W} warmup tokens)",
                        "mean_context": float(lens.mean()), "parallelism": f"sequence-sharded x{world}",
-                       "l2": "inputs larger than L2 (KV bytes per step >> 126 MB)"},
+                       "l2": ("L2-resident (the whole cache is ~1 MB): the HBM fraction is not meaningful"
+                              if args.config == 1 else "inputs larger than L2 (KV bytes per step >> 126 MB)")},
             "kv_gbs": kv_gbs, "hbm_frac_per_gpu": kv_gbs / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
@@ -378,13 +393,273 @@ def run_ours(args, wl, world, rank, local):
     torch.cuda.empty_cache()
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        res = reference_rate(wl, lens, 2, 1, 2)
+        ls = min(2, L)
+        res = reference_rate(wl, lens, 2 if L > 1 else 20, 1, ls)
         if res:
             rate, dt, threads, cname = res
             line["cpu_baseline"] = {"value": rate, "unit": "seq-steps/s", "cores": threads, "kind": "reference",
-                                    "sample": f"{len(lens)} sequences (same lengths), first 2 of {L} layers, "
-                                              f"2 timed steps, scaled x{L / 2:g}; reference codec {cname}"}
+                                    "sample": f"{len(lens)} sequences (same lengths), first {ls} of {L} layers, "
+                                              f"{2 if L > 1 else 20} timed steps, scaled x{L / ls:g}; "
+                                              f"reference codec {cname}"}
     if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def _finish_line(args, wl, world, rank, value, ms_step, attn_bytes, attn_ms, attn_ms_max, launches, status,
+                 clocks, extra_config, scaling, e2e=None):
+    peak, peak_kind = peaks()
+    achieved = attn_bytes / (attn_ms / 1000.0) / 1e9 if attn_ms > 0 else 0.0
+    line = {
+        "metric": METRIC, "value": value, "unit": "seq-steps/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling,
+        "vs_baseline": None, "dtype": "int8" if wl["codec"] in (1, 2) else "u4", "data": "synthetic",
+        "config": dict({"workload": wl["name"], "layers": wl["layers"], "query_heads": wl["H"],
+                        "kv_heads": wl["HK"], "head_dim": HD, "page_tokens": wl["P"]}, **extra_config),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": attn_bytes,
+                     "avg_launch_ms": attn_ms, "avg_launch_ms_max_rank": attn_ms_max},
+        "gpu_launches": int(launches), "status_bits": status, "clocks": clocks,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    return line
+
+
+def run_split(args, wl, world, rank, local):
+    """cfg4: one long sequence.  At N GPUs every rank holds the cache and
+    attends its contiguous page-aligned KV range (qwn_kv_partial writing
+    o | m | l into one block); the blocks are all-gathered over NCCL and
+    merged on every rank (qwn_kv_merge_partials_packed).  The rank owning
+    the tail stores each new token.  Total work is fixed: strong scaling."""
+    import torch
+    import qwanto_b200 as qb
+    from qwanto_b200.sharding import kv_ranges
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    H, HK, P, c0 = wl["H"], wl["HK"], wl["P"], wl["lo"]
+    K, W = args.steps, args.warmup
+    max_pages = (c0 + W + K + 2 + P - 1) // P + 1
+    pool = qb.KvPool(wl["codec"], 1, HK, P, max_pages + 4, 1, max_pages, max_query_heads=H, permutation_seed=1000,
+                     device=local)
+    seed = 1000 * wl["seed"]
+    pool.prefill_synthetic([0], [c0], seed, None, stream)
+    ids = torch.zeros(1, dtype=torch.int32, device=dev)
+    ring = min(W + K, args.ring)
+    q = torch.empty((ring, H * HD), dtype=torch.float32, device=dev)
+    k = torch.empty((ring, HK * HD), dtype=torch.float32, device=dev)
+    v = torch.empty((ring, HK * HD), dtype=torch.float32, device=dev)
+    for s in range(ring):
+        pos = torch.tensor([c0 + s], dtype=torch.int32, device=dev)
+        qb.generate_rows(q[s], 1, H * HD, 1, seed, 0, ids, pos, None, stream)
+        qb.generate_rows(k[s], 1, HK * HD, 2, seed, 0, ids, pos, None, stream)
+        qb.generate_rows(v[s], 1, HK * HD, 3, seed, 0, ids, pos, None, stream)
+    out = torch.empty((H * HD,), dtype=torch.float32, device=dev)
+    blk = H * (HD + 2)
+    send = torch.empty((blk,), dtype=torch.float32, device=dev)
+    recv = torch.empty((world, blk), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+
+    # fixed page ranges of the prefilled context; the last rank owns the tail,
+    # where every new token goes
+    ranges = kv_ranges(c0, world, P)
+
+    def step(s, i=None):
+        r = s % ring
+        c = c0 + s + 1  # length after this step's token
+        pool.seq_append(1, None, None, stream)
+        if i is not None:
+            ev_a[i].record(stream)
+        if world == 1:
+            pool.decode(0, 1, H, q[r], out, key=k[r], value=v[r], stream=stream)
+        else:
+            a, b = ranges[rank]
+            if rank == world - 1:
+                b = c
+                pool.append(0, 1, k[r], v[r], None, stream)
+            pool.partial(0, 1, H, q[r], send[H * HD: H * HD + H], send[H * HD + H:], send[: H * HD],
+                         t_begin=a, t_end=b, stream=stream)
+            dist.all_gather_into_tensor(recv, send)
+            qb.merge_partials_packed(world, H, recv, out, stream)
+        if i is not None:
+            ev_b[i].record(stream)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    for s in range(W):
+        step(s)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    launches0 = qb.launch_count()
+    t_wall0 = time.perf_counter()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(K):
+        step(W + i, i)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    launches = qb.launch_count() - launches0
+    if world > 1:
+        dist.barrier()
+    ms_total = start.elapsed_time(end)
+    t_wall1 = time.perf_counter()
+    sampler.stop()
+    status = pool.check()
+    attn_ms = float(np.mean([ev_a[i].elapsed_time(ev_b[i]) for i in range(K)]))
+    t_local = torch.tensor([ms_total, attn_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
+    ms_total, attn_max = t_local.tolist()
+    ms_step = ms_total / K
+    # this rank's algorithmic bytes per step: its KV range, the appended
+    # token (tail rank), Q, the exchanged partial blocks and the output
+    a, b = ranges[rank]
+    if rank == world - 1:
+        b = c0 + W + K // 2
+    attn_bytes = float((b - a) * HK * kv_bytes(wl["codec"]) + H * HD * 4 * 2 + world * blk * 4
+                       + ((b - a) + P - 1) // P * 4)
+    line = None
+    if rank == 0:
+        line = _finish_line(args, wl, world, rank, 1000.0 / ms_step, ms_step, attn_bytes, attn_ms, attn_max,
+                            launches, status, sampler.summary(t_wall0 - 0.05, t_wall1 + 0.05),
+                            {"global_batch": 1, "context": c0, "parallelism": f"split-KV x{world} (NCCL all-gather "
+                             f"of (m, l, o) blocks, {blk * 4} B per rank)",
+                             "l2": "inputs larger than L2 (272 MB of KV per layer-step)"}, "strong")
+        line["unit"] = "layer-steps/s"
+    pool.close()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            res = reference_rate(wl, np.array([c0], np.int32), 3, 1, 1)
+            if res:
+                rate, dt, threads, cname = res
+                line["cpu_baseline"] = {"value": rate, "unit": "layer-steps/s", "cores": threads, "kind": "reference",
+                                        "sample": f"1 sequence of {c0} tokens, 3 timed steps; reference codec {cname}"}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_churn(args, wl, world, rank, local):
+    """cfg5: a 1,048,576-page pool, 256 sequences per GPU; each step every
+    sequence appends a token and attends (page attention mass exported), and
+    with probability evict_p (seeded, per sequence-step) a sequence evicts
+    its lowest-score pages down to the token budget and compacts.  Sequences
+    shard over GPUs (weak scaling)."""
+    import torch
+    import qwanto_b200 as qb
+    from qwanto_b200.sharding import balanced_count_shard
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    glens = global_lengths(wl, world)
+    mine = balanced_count_shard(glens, world)[rank]
+    lens = glens[mine].astype(np.int64)
+    B, H, HK, P = len(lens), wl["H"], wl["HK"], wl["P"]
+    K, W = args.steps, args.warmup
+    max_pages = (int(lens.max()) + W + K + 2 + P - 1) // P + 1
+    pool = qb.KvPool(wl["codec"], 1, HK, P, wl["pool_pages"], B, max_pages, max_query_heads=H,
+                     permutation_seed=5000 + rank, device=local)
+    seed = 1000 * wl["seed"] + rank
+    pool.prefill_synthetic(list(range(B)), lens.tolist(), seed, None, stream)
+    ring = min(W + K, args.ring)
+    ids = torch.arange(B, dtype=torch.int32, device=dev)
+    q = torch.empty((ring, B, H * HD), dtype=torch.float32, device=dev)
+    k = torch.empty((ring, B, HK * HD), dtype=torch.float32, device=dev)
+    v = torch.empty((ring, B, HK * HD), dtype=torch.float32, device=dev)
+    for s in range(ring):
+        pos = torch.tensor(lens + s, dtype=torch.int32, device=dev)
+        qb.generate_rows(q[s], B, H * HD, 1, seed, 0, ids, pos, None, stream)
+        qb.generate_rows(k[s], B, HK * HD, 2, seed, 0, ids, pos, None, stream)
+        qb.generate_rows(v[s], B, HK * HD, 3, seed, 0, ids, pos, None, stream)
+    out = torch.empty((B, H * HD), dtype=torch.float32, device=dev)
+    mass = torch.zeros((B, max_pages), dtype=torch.float32, device=dev)
+    rng = np.random.default_rng(wl["seed"] * 7919 + rank)
+    flags_host = (rng.random((W + K, B)) < wl["evict_p"]).astype(np.uint8)
+    flags = torch.tensor(flags_host, device=dev)
+    budget = wl["budget"]
+    # host mirror of the lengths (eviction removes whole pages until len <= budget)
+    hl = lens.copy()
+    attn_bytes_steps = []
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+
+    def step(s, i=None):
+        r = s % ring
+        hl[:] += 1
+        pool.seq_append(B, None, None, stream)
+        if i is not None:
+            ev_a[i].record(stream)
+            attn_bytes_steps.append(float(np.sum(hl * HK * kv_bytes(wl["codec"]) + HK * kv_bytes(wl["codec"])
+                                              + 2 * HK * HD * 4 + 2 * H * HD * 4 + np.ceil(hl / P) * 4)))
+        pool.decode(0, B, H, q[r], out, key=k[r], value=v[r], page_mass=mass, stream=stream)
+        if i is not None:
+            ev_b[i].record(stream)
+        pool.evict(B, mass, flags[s], budget, None, stream)
+        f = flags_host[s].astype(bool) & (hl > budget)
+        hl[f] -= P * ((hl[f] - budget + P - 1) // P)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    for s in range(W):
+        step(s)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    launches0 = qb.launch_count()
+    t_wall0 = time.perf_counter()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(K):
+        step(W + i, i)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    launches = qb.launch_count() - launches0
+    if world > 1:
+        torch.distributed.barrier()
+    ms_total = start.elapsed_time(end)
+    t_wall1 = time.perf_counter()
+    sampler.stop()
+    status = pool.check()
+    gpu_lens = pool.lens()[:B]
+    lens_match = bool(np.array_equal(gpu_lens.astype(np.int64), hl))
+    attn_ms = float(np.mean([ev_a[i].elapsed_time(ev_b[i]) for i in range(K)]))
+    t_local = torch.tensor([ms_total, attn_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t_local, op=torch.distributed.ReduceOp.MAX)
+    ms_total, attn_max = t_local.tolist()
+    ms_step = ms_total / K
+    line = None
+    if rank == 0:
+        line = _finish_line(args, wl, world, rank, B * world / (ms_step / 1000.0), ms_step,
+                            float(np.mean(attn_bytes_steps)), attn_ms, attn_max, launches, status,
+                            sampler.summary(t_wall0 - 0.05, t_wall1 + 0.05),
+                            {"global_batch": int(B * world), "per_gpu_batch": int(B),
+                             "pool_pages": wl["pool_pages"], "evict_p": wl["evict_p"], "token_budget": budget,
+                             "evictions_timed": int(np.sum(flags_host[W:])),
+                             "lengths_match_host_model": lens_match,
+                             "parallelism": f"sequence-sharded x{world}",
+                             "l2": "inputs larger than L2 (KV bytes per step >> 126 MB)"}, "weak")
+        line["roofline"]["kernel"] = "attn_kernel with page-mass export (the eviction launches are in ms_per_step)"
+    pool.close()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            res = reference_rate(wl, lens.astype(np.int32), 2, 1, 1)
+            if res:
+                rate, dt, threads, cname = res
+                line["cpu_baseline"] = {"value": rate, "unit": "seq-steps/s", "cores": threads, "kind": "reference",
+                                        "sample": f"{B} sequences (same lengths), append + attend, 2 timed steps, "
+                                                  f"no eviction; reference codec {cname}"}
         print(json.dumps(line), flush=True)
     return 0
 
@@ -392,7 +667,7 @@ def run_ours(args, wl, world, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=0, help="timed steps (default 20; cfg1 256, cfg4/5 50)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=2)
@@ -405,6 +680,8 @@ def main():
     if args.warmup < 3:
         args.warmup = 3  # the timing rules want >= 3 warm-up steps
     wl = workload(args.config)
+    if not args.steps:
+        args.steps = wl.get("steps", 20)
     if args.layers:
         wl["layers"] = args.layers
         wl["name"] += f" [layers overridden to {args.layers}]"
@@ -415,7 +692,12 @@ def main():
         # CPU only: rank 0 runs the reference, the other ranks exit at once
         return run_reference(args, wl, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
     world, rank, local = dist_setup()
-    rc = run_ours(args, wl, world, rank, local)
+    if args.config == 4:
+        rc = run_split(args, wl, world, rank, local)
+    elif args.config == 5:
+        rc = run_churn(args, wl, world, rank, local)
+    else:
+        rc = run_ours(args, wl, world, rank, local)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

@@ -169,6 +169,13 @@ QWN_CUDA_ABI_API int qwn_kv_partial(QwnKvPoolHandle *pool, const QwnKvPartialReq
 QWN_CUDA_ABI_API int qwn_kv_merge_partials(uint32_t parts, uint32_t rows, const float *m_dev,
                                            const float *l_dev, const float *o_dev,
                                            float *out_dev, void *stream);
+/* The same merge with each part packed as one block of rows*130 floats:
+ * o[rows][128], then m[rows], then l[rows] (the layout qwn_kv_partial writes
+ * when its o/m/l pointers point into one block), so a single all-gather of
+ * the blocks carries every part.  No counterpart in the reference (its
+ * decoder has no split-KV path); the merge rule is qwn_kv_merge_partials'. */
+QWN_CUDA_ABI_API int qwn_kv_merge_partials_packed(uint32_t parts, uint32_t rows, const float *packed_dev,
+                                                  float *out_dev, void *stream);
 
 /* Store tokens [first_pos, first_pos+n_tokens) of one sequence and layer
  * (already reserved with qwn_kv_seq_append): key/value [n_tokens][kv_heads][128]. */

@@ -26,7 +26,7 @@ from ._lib import (CODEC_Q4_G32, CODEC_Q8_B64_F32, CODEC_Q8_HEAD_F16, CODEC_TQ35
                    init, lib)
 
 __all__ = ["CudaContext", "KvPool", "lib", "QwnCudaError", "generate_rows", "merge_partials",
-           "CODEC_Q8_B64_F32", "CODEC_Q8_HEAD_F16", "CODEC_TQ35_G64", "CODEC_Q4_G32", "launch_count"]
+           "CODEC_Q8_B64_F32", "CODEC_Q8_HEAD_F16", "CODEC_TQ35_G64", "CODEC_Q4_G32", "launch_count", "merge_partials_packed"]
 
 TILE_BYTES = {CODEC_Q8_B64_F32: 4352, CODEC_Q8_HEAD_F16: 4160, CODEC_TQ35_G64: 2048, CODEC_Q4_G32: 2560}
 # per token-head K+V bytes at head_dim 128 (the roofline's algorithmic bytes)
@@ -77,6 +77,12 @@ def generate_rows(out, rows: int, width: int, kind: int, seed: int, layer: int, 
 def merge_partials(parts: int, rows: int, m, l, o, out, stream=None) -> None:
     check("qwn_kv_merge_partials", lib().qwn_kv_merge_partials(parts, rows, _ptr(m), _ptr(l), _ptr(o),
                                                                 _ptr(out), _stream(stream)))
+
+
+def merge_partials_packed(parts: int, rows: int, packed, out, stream=None) -> None:
+    """Merge `parts` blocks of rows*130 floats (o[rows][128], m[rows], l[rows])."""
+    check("qwn_kv_merge_partials_packed", lib().qwn_kv_merge_partials_packed(parts, rows, _ptr(packed), _ptr(out),
+                                                                              _stream(stream)))
 
 
 class KvPool:

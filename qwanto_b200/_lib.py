@@ -198,6 +198,7 @@ _SIGS = {
     "qwn_kv_partial": (C.c_int, [_P(Handle), _P(PartialRequest)]),
     "qwn_kv_merge_partials": (C.c_int, [C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_void_p]),
+    "qwn_kv_merge_partials_packed": (C.c_int, [C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p]),
     "qwn_kv_store_tokens": (C.c_int, [_P(Handle), C.c_int32, C.c_uint32, C.c_uint32, C.c_uint32,
                                       C.c_void_p, C.c_void_p, C.c_void_p]),
     "qwn_kv_generate_rows": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64,

@@ -1311,20 +1311,22 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
     }
 }
 
-// merge of partial states produced on several devices (base-2 domain)
-__global__ void merge_kernel(uint32_t parts, uint32_t rows, const float *m, const float *l,
-                             const float *o, float *out) {
+// merge of partial states produced on several devices (base-2 domain); part
+// p's (m, l) of a row sit at p*stride_ml + row, its o row at p*stride_o +
+// row*128
+__global__ void merge_kernel(uint32_t parts, uint32_t rows, const float *m, const float *l, const float *o,
+                             float *out, size_t stride_ml, size_t stride_o) {
     const uint32_t row = blockIdx.x;
     const uint32_t d = threadIdx.x;
     if (row >= rows || d >= kHeadDim) return;
     float ms = -INFINITY;
-    for (uint32_t p = 0; p < parts; p++) ms = fmaxf(ms, m[(size_t)p * rows + row]);
+    for (uint32_t p = 0; p < parts; p++) ms = fmaxf(ms, m[p * stride_ml + row]);
     float ls = 0.f, acc = 0.f;
     for (uint32_t p = 0; p < parts; p++) {
-        const float mp = m[(size_t)p * rows + row];
+        const float mp = m[p * stride_ml + row];
         const float w = mp == -INFINITY ? 0.f : ex2(mp - ms);
-        ls += l[(size_t)p * rows + row] * w;
-        acc += o[((size_t)p * rows + row) * kHeadDim + d] * w;
+        ls += l[p * stride_ml + row] * w;
+        acc += o[p * stride_o + (size_t)row * kHeadDim + d] * w;
     }
     out[(size_t)row * kHeadDim + d] = ls > 0.f ? acc / ls : 0.f;
 }
@@ -1433,9 +1435,9 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
 }
 
 cudaError_t launch_merge(uint32_t parts, uint32_t rows, const float *m, const float *l,
-                         const float *o, float *out, cudaStream_t s) {
+                         const float *o, float *out, size_t stride_ml, size_t stride_o, cudaStream_t s) {
     if (rows == 0) return cudaSuccess;
-    merge_kernel<<<rows, kHeadDim, 0, s>>>(parts, rows, m, l, o, out);
+    merge_kernel<<<rows, kHeadDim, 0, s>>>(parts, rows, m, l, o, out, stride_ml, stride_o);
     count_launch();
     return cudaGetLastError();
 }

@@ -117,7 +117,7 @@ struct AttnLaunch {
 };
 cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s);
 cudaError_t launch_merge(uint32_t parts, uint32_t rows, const float *m, const float *l,
-                         const float *o, float *out, cudaStream_t s);
+                         const float *o, float *out, size_t stride_ml, size_t stride_o, cudaStream_t s);
 cudaError_t launch_evict(Pool *p, uint32_t n, const int32_t *seq_ids, const float *mass,
                          const uint8_t *flags, uint32_t budget, cudaStream_t s);
 cudaError_t launch_pool_init_state(Pool *p, cudaStream_t s);

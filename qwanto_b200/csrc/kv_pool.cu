@@ -633,8 +633,19 @@ QWN_CUDA_ABI_API int qwn_kv_partial(QwnKvPoolHandle *h, const QwnKvPartialReques
 QWN_CUDA_ABI_API int qwn_kv_merge_partials(uint32_t parts, uint32_t rows, const float *m, const float *l,
                                            const float *o, float *out, void *stream) {
     if (!m || !l || !o || !out || parts == 0) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
-    cudaError_t e = launch_merge(parts, rows, m, l, o, out, static_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_merge(parts, rows, m, l, o, out, rows, (size_t)rows * kHeadDim,
+                                 static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) { set_cuda_error("qwn_kv_merge_partials", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_merge_partials_packed(uint32_t parts, uint32_t rows, const float *packed, float *out,
+                                                  void *stream) {
+    if (!packed || !out || parts == 0) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    const size_t stride = (size_t)rows * (kHeadDim + 2);
+    const float *o = packed, *m = packed + (size_t)rows * kHeadDim, *l = m + rows;
+    cudaError_t e = launch_merge(parts, rows, m, l, o, out, stride, stride, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_merge_partials_packed", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
     return QWN_CUDA_STATUS_OK;
 }
 

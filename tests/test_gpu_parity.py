@@ -143,6 +143,16 @@ def test_partial_merge_equals_full(cuda):
         assert_close(merged.cpu().numpy(), full.cpu().numpy().reshape(48, 128), "merge")
         ref = tw.ora.attention(0, 0, 2500, tw.row(1, 0, 0, 2499, 48 * 128), 48, 1.0 / np.sqrt(128.0))
         assert_close(merged.cpu().numpy(), ref, "merge vs oracle")
+        # the packed form: each part one block o | m | l, as the split-KV bench all-gathers it
+        packed = torch.zeros((parts, 48 * 130), device="cuda")
+        for i in range(parts):
+            blk = packed[i]
+            tw.gpu.partial(0, 1, 48, q, blk[48 * 128: 48 * 129], blk[48 * 129:], blk[: 48 * 128],
+                           t_begin=bounds[i], t_end=bounds[i + 1])
+        merged2 = torch.zeros((48, 128), device="cuda")
+        qb.merge_partials_packed(parts, 48, packed, merged2)
+        torch.cuda.synchronize()
+        assert torch.equal(merged2, merged)
     finally:
         tw.close()
 
