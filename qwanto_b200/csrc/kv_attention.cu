@@ -32,6 +32,11 @@ namespace qkv {
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
+// a warp range holds at least this many units (small batches use fewer warps)
+constexpr uint64_t kMinUnitsPerWarp = 8;
+// segments split into more parts merge in two levels: groups of this many
+// parts first, then the group results
+constexpr uint32_t kMergeGroup = 16;
 constexpr float kNuFloor = 7.888609052210118e-31f;  // 2^-100
 constexpr float kNuHeadroom = 16384.0f;            // rescale only when a scale exceeds nu * 2^14
 
@@ -49,7 +54,8 @@ struct AttnArgs {
     float *output;
     float scale_log2;
     float *partials;
-    uint32_t *counters;
+    uint32_t *counters;   // [segments]: parts (or merged groups) counted per segment
+    uint32_t *gcounters;  // [warps + segments]: parts counted per merge group (slot index of its first part)
     float2 *tile_mass;
     float2 *seg_ml;
     float *part_m, *part_l, *part_o;  // non-null: export unnormalised (m, l, o)
@@ -1006,17 +1012,15 @@ __device__ __forceinline__ uint32_t slot_bytes(uint32_t G) { return (G * (kHeadD
 // round trip per chunk -- and combines them from shared memory.  GG >= G is
 // the compile-time row count.  Returns false when the wait gave up.
 template <int GG>
-__device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
-                                           uint64_t T, uint64_t W, uint8_t *buf, uint32_t SB, uint64_t *bar,
-                                           uint32_t &par) {
+__device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, uint64_t base_w, uint32_t stride_w,
+                                           uint32_t nparts, float *dst_slot, uint8_t *buf, uint32_t SB,
+                                           uint64_t *bar, uint32_t &par) {
     const int lane = threadIdx.x & 31;
     const uint32_t G = A.group;
     const uint32_t PB = slot_bytes(G), rowf = G * kHeadDim;
     const uint32_t cap = SB / PB < 32u ? SB / PB : 32u;
-    const uint64_t wa = ((Us + 1) * W - 1) / T;
     auto slot_of = [&](uint32_t pp) -> const float * {
-        const uint64_t w = T >= W ? wa + pp : ((Us + pp + 1) * W - 1) / T;
-        return A.partials + (size_t)(w + s_idx) * kPartialFloats;
+        return A.partials + (size_t)(base_w + (uint64_t)pp * stride_w + s_idx) * kPartialFloats;
     };
     // the slots were written by generic stores of other warps (ordered by the
     // acquire on the segment counter); the bulk copies read them through the
@@ -1079,6 +1083,11 @@ __device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, ui
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ls[g] += __shfl_xor_sync(0xffffffffu, ls[g], o);
         if ((uint32_t)g >= G) continue;
+        if (dst_slot) {  // a merged group, stored as one unnormalised partial
+            reinterpret_cast<float4 *>(dst_slot + g * kHeadDim)[lane] = acc[g];
+            if (lane == 0) { dst_slot[rowf + g] = M[g]; dst_slot[rowf + G + g] = ls[g]; }
+            continue;
+        }
         const size_t row = row0 + g;
         if (A.part_o) {
             reinterpret_cast<float4 *>(A.part_o + row * kHeadDim)[lane] = acc[g];
@@ -1090,16 +1099,15 @@ __device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, ui
         }
         if (A.seg_ml && lane == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + g] = make_float2(M[g], ls[g]);
     }
-    if (lane == 0) A.counters[s_idx] = 0u;  // ready for the next launch
     return true;
 }
 
-__device__ __forceinline__ bool merge_segment(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
-                                              uint64_t T, uint64_t W, uint8_t *buf, uint32_t SB, uint64_t *bar,
-                                              uint32_t &par) {
-    if (A.group <= 2) return merge_rows<2>(A, s_idx, nparts, Us, T, W, buf, SB, bar, par);
-    if (A.group <= 4) return merge_rows<4>(A, s_idx, nparts, Us, T, W, buf, SB, bar, par);
-    return merge_rows<8>(A, s_idx, nparts, Us, T, W, buf, SB, bar, par);
+__device__ __forceinline__ bool merge_parts(const AttnArgs &A, uint32_t s_idx, uint64_t base_w, uint32_t stride_w,
+                                            uint32_t nparts, float *dst_slot, uint8_t *buf, uint32_t SB,
+                                            uint64_t *bar, uint32_t &par) {
+    if (A.group <= 2) return merge_rows<2>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
+    if (A.group <= 4) return merge_rows<4>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
+    return merge_rows<8>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
 }
 
 // End of a warp's share of segment s_idx (first unit Us, ns units).  A warp
@@ -1112,11 +1120,10 @@ __device__ __forceinline__ bool merge_segment(const AttnArgs &A, uint32_t s_idx,
 template <class OPS>
 __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const typename OPS::State &st, uint32_t s_idx,
                                                    uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid) {
-    // warps whose (non-empty) range meets the segment: warp of unit u is
-    // ((u+1)W-1)/T.  With T >= W every warp between the first and the last
-    // is non-empty; with T < W each unit is a warp of its own.
+    // warps whose range meets the segment: warp of unit u is ((u+1)W-1)/T,
+    // and with T >= W (the kernel caps W) every warp range is non-empty
     const uint64_t wa = ((Us + 1) * W - 1) / T, wb = ((Us + ns) * W - 1) / T;
-    const uint32_t nparts = T >= W ? (uint32_t)(wb - wa + 1) : (uint32_t)ns;
+    const uint32_t nparts = (uint32_t)(wb - wa + 1);
     const size_t row0 = (size_t)s_idx * A.group;
     if (nparts == 1) {
         float2 *sm = A.seg_ml ? A.seg_ml + (size_t)s_idx * kMaxGroup : nullptr;
@@ -1129,6 +1136,15 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
     float *slot = A.partials + (size_t)(wid + s_idx) * kPartialFloats;
     OPS::store_rows(A, st, slot, slot + A.group * kHeadDim, slot + A.group * (kHeadDim + 1), false, nullptr);
     return nparts;
+}
+
+// counter a part of segment s_idx (nparts parts, first unit Us) counts on:
+// the segment's when it merges in one level, else its merge group's
+__device__ __forceinline__ uint32_t *part_counter(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
+                                                  uint64_t T, uint64_t W, uint64_t wid) {
+    if (nparts <= kMergeGroup) return &A.counters[s_idx];
+    const uint64_t wa = ((Us + 1) * W - 1) / T;
+    return &A.gcounters[wa + ((wid - wa) / kMergeGroup) * kMergeGroup + s_idx];
 }
 
 // ---------------------------------------------------------------------------
@@ -1151,8 +1167,8 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
     __syncwarp();
 
     const uint32_t HK = A.kv_heads;
-    const uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
-    const uint64_t wid = (uint64_t)blockIdx.x * kWarpsPerCta + warp;
+    uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
+    uint64_t wid = (uint64_t)blockIdx.x * kWarpsPerCta + warp;
 
     // total units of the batch
     uint64_t T = 0;
@@ -1164,6 +1180,13 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         T += u;
     }
     if (T == 0) return;
+    if ((T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp < W) {
+        // a small batch: fewer, longer warp ranges (every split is a partial
+        // to merge), spread over the SMs by numbering warps across CTAs
+        W = (T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
+        wid = (uint64_t)warp * gridDim.x + blockIdx.x;
+        if (wid >= W) return;
+    }
     const uint64_t u0 = wid * T / W, u1 = (wid + 1) * T / W;
     if (u0 >= u1) return;
     const uint32_t n = (uint32_t)(u1 - u0);
@@ -1223,8 +1246,8 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
         if (cons.tile == 0 || k == 0) OPS::begin(frag, state, A, cons.i * HK + cons.h);
         if (pend_n && !counted0 && k == pend_k0 + 4u) {
             __syncwarp();
-            if (lane == 0) tk0 = atom_add_acq_rel_gpu(&A.counters[pend_s0], 1u);  // ticket read after the loop
-            counted0 = true;
+            if (lane == 0) tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, pend_n0, pend_u0, T, W, wid), 1u);
+            counted0 = true;  // the ticket is read after the loop
         }
         if (cons.tile + 4u == cons.geo.ntiles) {
             // the next segment's query rows (s_idx + 1 in batch order) into L1,
@@ -1297,17 +1320,40 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnAr
     __syncwarp();
     uint32_t tk1 = 0;
     if (lane == 0) {
-        if (pend_n > 0 && !counted0) tk0 = atom_add_acq_rel_gpu(&A.counters[pend_s0], 1u);
-        if (pend_n > 1) tk1 = atom_add_acq_rel_gpu(&A.counters[pend_s1], 1u);
+        if (pend_n > 0 && !counted0) tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, pend_n0, pend_u0, T, W, wid), 1u);
+        if (pend_n > 1) tk1 = atom_add_acq_rel_gpu(part_counter(A, pend_s1, pend_n1, pend_u1, T, W, wid), 1u);
     }
     tk0 = __shfl_sync(0xffffffffu, tk0, 0);
     tk1 = __shfl_sync(0xffffffffu, tk1, 0);
     for (uint32_t e = 0; e < pend_n; e++) {
-        const uint32_t np = e ? pend_n1 : pend_n0;
-        if ((e ? tk1 : tk0) != np - 1) continue;  // not the last arrival
-        if (!merge_segment(A, e ? pend_s1 : pend_s0, np, e ? pend_u1 : pend_u0, T, W, wsm, (uint32_t)(S * B),
-                           &bars[st], par))
+        const uint32_t np = e ? pend_n1 : pend_n0, s_idx = e ? pend_s1 : pend_s0;
+        const uint64_t wa = (((e ? pend_u1 : pend_u0) + 1) * W - 1) / T;
+        const uint32_t tk = e ? tk1 : tk0;
+        uint8_t *buf = wsm;
+        const uint32_t SB = (uint32_t)(S * B);
+        if (np <= kMergeGroup) {
+            if (tk != np - 1) continue;  // not the last arrival
+            if (!merge_parts(A, s_idx, wa, 1, np, nullptr, buf, SB, &bars[st], par)) return;
+            if (lane == 0) A.counters[s_idx] = 0u;  // ready for the next launch
+            continue;
+        }
+        // two levels: this warp's group of kMergeGroup consecutive parts
+        const uint64_t gbase = wa + ((wid - wa) / kMergeGroup) * kMergeGroup;
+        const uint32_t gsize = (uint32_t)min((uint64_t)kMergeGroup, wa + np - gbase);
+        if (tk != gsize - 1) continue;
+        float *gslot = A.partials + (size_t)(gbase + s_idx) * kPartialFloats;
+        if (!merge_parts(A, s_idx, gbase, 1, gsize, gslot, buf, SB, &bars[st], par)) return;
+        if (lane == 0) A.gcounters[gbase + s_idx] = 0u;
+        // publish the group result (in its first part's slot) and count it
+        __syncwarp();
+        uint32_t t2 = 0;
+        if (lane == 0) t2 = atom_add_acq_rel_gpu(&A.counters[s_idx], 1u);
+        t2 = __shfl_sync(0xffffffffu, t2, 0);
+        if (t2 != (np + kMergeGroup - 1) / kMergeGroup - 1) continue;
+        if (!merge_parts(A, s_idx, wa, kMergeGroup, (np + kMergeGroup - 1) / kMergeGroup, nullptr, buf, SB,
+                         &bars[st], par))
             return;
+        if (lane == 0) A.counters[s_idx] = 0u;
     }
 }
 
@@ -1417,6 +1463,7 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
     A.scale_log2 = a.scale * kLog2e;
     A.partials = p->partials;
     A.counters = p->counters;
+    A.gcounters = p->counters + p->max_segments;
     A.tile_mass = a.page_mass ? p->tile_mass : nullptr;
     A.seg_ml = a.page_mass ? p->seg_ml : nullptr;
     A.part_m = a.part_m;
@@ -1471,7 +1518,7 @@ namespace qkv {
 namespace {
 constexpr int kStaticSlots = 1024;
 constexpr int kStaticSegments = 256;
-constexpr size_t kStaticFloats = (size_t)kStaticSlots * kPartialFloats + kStaticSegments;
+constexpr size_t kStaticFloats = (size_t)kStaticSlots * kPartialFloats + kStaticSegments + kStaticSlots;
 static __device__ __align__(256) float g_static_scratch[kStaticFloats];
 constexpr int kStaticMaxDevices = 64;
 std::mutex g_static_mu;
@@ -1540,8 +1587,9 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
     float *scratch = g_static_addr[dev];
     uint32_t *counters = reinterpret_cast<uint32_t *>(scratch + (size_t)kStaticSlots * kPartialFloats);
     cudaStream_t s = static_cast<cudaStream_t>(r->stream);
-    // the merge counters must start at zero; the slots are written before read
-    e = cudaMemsetAsync(counters, 0, sizeof(uint32_t) * kStaticSegments, s);
+    // the merge counters (per segment, then per merge group) must start at
+    // zero; the slots are written before they are read
+    e = cudaMemsetAsync(counters, 0, sizeof(uint32_t) * (kStaticSegments + kStaticSlots), s);
     if (e != cudaSuccess) { set_cuda_error("qwn_kv_attention_static: clear", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
     const uint32_t segs = r->num_seqs * r->kv_heads;
     uint32_t ctas = g_static_ctas[dev][r->codec];
@@ -1568,6 +1616,7 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
     A.scale_log2 = (r->scale > 0.f ? r->scale : 1.0f / sqrtf((float)kHeadDim)) * kLog2e;
     A.partials = scratch;
     A.counters = counters;
+    A.gcounters = counters + kStaticSegments;
     A.status = r->status_dev;
     switch (r->codec) {
         case QWN_KV_CODEC_Q8_HEAD_F16: e = launch_variant<QWN_KV_CODEC_Q8_HEAD_F16>(ctas, A, s); break;

@@ -62,7 +62,7 @@ struct Pool {
     uint32_t *status = nullptr;
     // attention scratch
     float *partials = nullptr;          // [warps + segments][kPartialFloats]
-    uint32_t *counters = nullptr;       // [segments]
+    uint32_t *counters = nullptr;       // [segments] then [warps + segments] (merge groups)
     float2 *tile_mass = nullptr;        // [units][kMaxGroup] (u, m) per tile and row
     float2 *seg_ml = nullptr;           // [segments][kMaxGroup] final (m, l)
     uint8_t *evict_dead = nullptr;      // [max_seqs][max_pages_per_seq]
@@ -79,6 +79,9 @@ struct Pool {
 };
 
 constexpr int kPartialFloats = kMaxGroup * kHeadDim + 2 * kMaxGroup;  // room for o[G][128], m[G], l[G]
+// merge counters of a pool: one per segment, then one per partial slot
+// (the counter of a merge group sits at its first part's slot index)
+inline size_t counter_count(const Pool *p) { return (size_t)p->max_segments * 2 + p->attn_warps; }
 
 inline Pool *pool_from(const QwnKvPoolHandle *h) {
     if (!h || !header_ok(h->header, sizeof(*h)) || !h->opaque) return nullptr;

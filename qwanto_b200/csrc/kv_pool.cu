@@ -309,7 +309,7 @@ cudaError_t launch_pool_init_state(Pool *p, cudaStream_t s) {
     if ((e = cudaMemsetAsync(p->page_scores, 0, sizeof(float) * (size_t)p->max_seqs * p->max_pages_per_seq, s)))
         return e;
     if ((e = cudaMemsetAsync(p->status, 0, sizeof(uint32_t), s))) return e;
-    if ((e = cudaMemsetAsync(p->counters, 0, sizeof(uint32_t) * p->max_segments, s))) return e;
+    if ((e = cudaMemsetAsync(p->counters, 0, sizeof(uint32_t) * counter_count(p), s))) return e;
     // free stack: total-1-i, optionally permuted (Fisher-Yates on the host)
     std::vector<int32_t> stack(p->total_pages);
     for (uint32_t i = 0; i < p->total_pages; i++) stack[i] = (int32_t)(p->total_pages - 1 - i);
@@ -451,7 +451,7 @@ QWN_CUDA_ABI_API int qwn_kv_pool_create(const QwnKvPoolOptions *o, QwnKvPoolHand
               cudaMalloc(&p->page_scores, sizeof(float) * table_elems) == cudaSuccess &&
               cudaMalloc(&p->status, sizeof(uint32_t)) == cudaSuccess &&
               cudaMalloc(&p->partials, part_bytes) == cudaSuccess &&
-              cudaMalloc(&p->counters, sizeof(uint32_t) * p->max_segments) == cudaSuccess &&
+              cudaMalloc(&p->counters, sizeof(uint32_t) * counter_count(p)) == cudaSuccess &&
               cudaMalloc(&p->tile_mass, mass_bytes) == cudaSuccess &&
               cudaMalloc(&p->seg_ml, segml_bytes) == cudaSuccess &&
               cudaMalloc(&p->evict_dead, table_elems) == cudaSuccess &&
@@ -529,7 +529,7 @@ QWN_CUDA_ABI_API int qwn_kv_pool_check(QwnKvPoolHandle *h, uint32_t *bits) {
     cudaMemcpy(&st, p->status, sizeof(st), cudaMemcpyDeviceToHost);
     cudaMemset(p->status, 0, sizeof(uint32_t));
     if (st & QWN_KV_STATUS_WAIT_TIMEOUT)  // an abandoned merge leaves counters behind
-        cudaMemset(p->counters, 0, sizeof(uint32_t) * p->max_segments);
+        cudaMemset(p->counters, 0, sizeof(uint32_t) * counter_count(p));
     *bits = st;
     return QWN_CUDA_STATUS_OK;
 }

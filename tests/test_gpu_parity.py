@@ -83,6 +83,23 @@ def test_long_context_and_subset_batch(cuda, codec):
         tw.close()
 
 
+@pytest.mark.parametrize("codec", [2, 3])
+def test_single_long_sequence_two_level_merge(cuda, codec):
+    """One 24k-token sequence: every (sequence, kv head) segment is split over
+    ~220 warps, so the partials merge in two levels (groups of 16, then the
+    group results); page size 64, 6 query heads per kv head."""
+    tw = Twin(cuda, codec, layers=1, kv_heads=8, page_tokens=64, total_pages=400, max_seqs=1,
+              max_pages=400, query_heads=48, perm_seed=3, seed=31)
+    try:
+        tw.prefill([0], [24000])
+        for _ in range(2):
+            g, o, _ = tw.step([0])
+            assert_close(g, o, f"codec {codec} two-level merge")
+        tw.assert_state_equal()
+    finally:
+        tw.close()
+
+
 def test_outlier_channels_q4(cuda, oracle_mod):
     """Config-3 style K with 1% outlier channels x8, 4-bit groups of 32."""
     tw = Twin(cuda, 4, layers=2, kv_heads=8, page_tokens=16, total_pages=120, max_seqs=3, max_pages=40,
