@@ -94,7 +94,8 @@ template <int CODEC, int HG>
 struct Int8T {
     static constexpr bool kB64 = CODEC == QWN_KV_CODEC_Q8_B64_F32;
     static constexpr int kX = kB64 ? 2 : 1;  // scale groups along head_dim
-    static constexpr int kBytes = kB64 ? 4352 : 4160, kStages = 4;
+    // two head groups keep twice the state: 2 CTAs per SM, deeper pipelines
+    static constexpr int kBytes = kB64 ? 4352 : 4160, kStages = HG == 1 ? 4 : 6;
     struct Frag {
         uint32_t b[HG][2][4][2];   // IMMA B: [head group][n-block][k-block][reg]
         uint32_t magic[HG][kX][4]; // per (scale group, slice) of this lane's head
@@ -436,7 +437,7 @@ struct LowBitT {
     static constexpr bool kTQ = CODEC == QWN_KV_CODEC_TQ35_G64;
     static constexpr int kC = 4;               // classes of 32 dims
     static constexpr int kG = kTQ ? 2 : 4;     // groups (min values)
-    static constexpr int kBytes = kTQ ? 2048 : 2560, kStages = kTQ ? 8 : 6;
+    static constexpr int kBytes = kTQ ? 2048 : 2560, kStages = HG == 1 ? (kTQ ? 8 : 6) : (kTQ ? 12 : 9);
     struct Frag {
         uint32_t b[HG][2][kC][2];  // [head group][n-block][class][reg]
         float s2l[HG];             // unit slice scale x log2(e) x softmax scale
@@ -1151,7 +1152,7 @@ __device__ __forceinline__ uint32_t *part_counter(const AttnArgs &A, uint32_t s_
 // the kernel
 // ---------------------------------------------------------------------------
 template <int CODEC, int HG>
-__global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnArgs A) {
+__global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kernel(const AttnArgs A) {
     using OPS = Ops<CODEC, HG>;
     constexpr int S = OPS::kStages, B = OPS::kBytes;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1377,28 +1378,29 @@ __global__ void merge_kernel(uint32_t parts, uint32_t rows, const float *m, cons
     out[(size_t)row * kHeadDim + d] = ls > 0.f ? acc / ls : 0.f;
 }
 
-template <int CODEC>
+template <int CODEC, int HG>
 constexpr size_t codec_smem() {
-    using O = Ops<CODEC, 1>;
+    using O = Ops<CODEC, HG>;
     return (size_t)kWarpsPerCta * O::kStages * (O::kBytes + 8) + (size_t)kWarpsPerCta * sizeof(WarpWindow);
 }
 
 // kernel variants: one or two head groups of four query heads
 template <int CODEC>
 cudaError_t configure_codec() {
-    const int smem = (int)codec_smem<CODEC>();
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)codec_smem<CODEC, 1>());
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attn_kernel<CODEC, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        e = cudaFuncSetAttribute(attn_kernel<CODEC, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)codec_smem<CODEC, 2>());
     return e;
 }
+// ctas[hg-1]: the resident grid of each variant
 template <int CODEC>
-cudaError_t launch_variant(uint32_t ctas, const AttnArgs &A, cudaStream_t s) {
-    const size_t smem = codec_smem<CODEC>();
+cudaError_t launch_variant(const uint32_t (&ctas)[2], const AttnArgs &A, cudaStream_t s) {
     if (A.group > 4)
-        attn_kernel<CODEC, 2><<<ctas, kWarpsPerCta * 32, smem, s>>>(A);
+        attn_kernel<CODEC, 2><<<ctas[1], kWarpsPerCta * 32, codec_smem<CODEC, 2>(), s>>>(A);
     else
-        attn_kernel<CODEC, 1><<<ctas, kWarpsPerCta * 32, smem, s>>>(A);
+        attn_kernel<CODEC, 1><<<ctas[0], kWarpsPerCta * 32, codec_smem<CODEC, 1>(), s>>>(A);
     return cudaGetLastError();
 }
 
@@ -1410,29 +1412,42 @@ cudaError_t launch_codec(Pool *p, const AttnArgs &A, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured[p->device & 63] = true;
     }
-    const cudaError_t e = launch_variant<CODEC>(p->attn_ctas, A, s);
+    const uint32_t ctas[2] = {p->attn_ctas, p->attn_ctas2};
+    const cudaError_t e = launch_variant<CODEC>(ctas, A, s);
     count_launch();
     return e;
 }
 
 }  // namespace
 
-size_t attention_smem_bytes(uint32_t codec) {
+size_t attention_smem_bytes(uint32_t codec, int hg) {
     switch (codec) {
-        case QWN_KV_CODEC_Q8_HEAD_F16: return codec_smem<QWN_KV_CODEC_Q8_HEAD_F16>();
-        case QWN_KV_CODEC_Q8_B64_F32: return codec_smem<QWN_KV_CODEC_Q8_B64_F32>();
-        case QWN_KV_CODEC_Q4_G32: return codec_smem<QWN_KV_CODEC_Q4_G32>();
-        case QWN_KV_CODEC_TQ35_G64: return codec_smem<QWN_KV_CODEC_TQ35_G64>();
+        case QWN_KV_CODEC_Q8_HEAD_F16:
+            return hg == 1 ? codec_smem<QWN_KV_CODEC_Q8_HEAD_F16, 1>() : codec_smem<QWN_KV_CODEC_Q8_HEAD_F16, 2>();
+        case QWN_KV_CODEC_Q8_B64_F32:
+            return hg == 1 ? codec_smem<QWN_KV_CODEC_Q8_B64_F32, 1>() : codec_smem<QWN_KV_CODEC_Q8_B64_F32, 2>();
+        case QWN_KV_CODEC_Q4_G32:
+            return hg == 1 ? codec_smem<QWN_KV_CODEC_Q4_G32, 1>() : codec_smem<QWN_KV_CODEC_Q4_G32, 2>();
+        case QWN_KV_CODEC_TQ35_G64:
+            return hg == 1 ? codec_smem<QWN_KV_CODEC_TQ35_G64, 1>() : codec_smem<QWN_KV_CODEC_TQ35_G64, 2>();
         default: return 0;
     }
 }
 
-const void *attention_kernel_ptr(uint32_t codec) {
+const void *attention_kernel_ptr(uint32_t codec, int hg) {
     switch (codec) {
-        case QWN_KV_CODEC_Q8_HEAD_F16: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16, 1>;
-        case QWN_KV_CODEC_Q8_B64_F32: return (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32, 1>;
-        case QWN_KV_CODEC_Q4_G32: return (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 1>;
-        case QWN_KV_CODEC_TQ35_G64: return (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 1>;
+        case QWN_KV_CODEC_Q8_HEAD_F16:
+            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16, 1>
+                           : (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16, 2>;
+        case QWN_KV_CODEC_Q8_B64_F32:
+            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32, 1>
+                           : (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32, 2>;
+        case QWN_KV_CODEC_Q4_G32:
+            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 1>
+                           : (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 2>;
+        case QWN_KV_CODEC_TQ35_G64:
+            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 1>
+                           : (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 2>;
         default: return nullptr;
     }
 }
@@ -1523,19 +1538,22 @@ static __device__ __align__(256) float g_static_scratch[kStaticFloats];
 constexpr int kStaticMaxDevices = 64;
 std::mutex g_static_mu;
 float *g_static_addr[kStaticMaxDevices] = {};
-uint32_t g_static_ctas[kStaticMaxDevices][5] = {};
+uint32_t g_static_ctas[kStaticMaxDevices][5][2] = {};
 
 template <int CODEC>
 cudaError_t static_setup(int dev) {
-    const size_t smem = codec_smem<CODEC>();
     cudaError_t e = configure_codec<CODEC>();
     if (e != cudaSuccess) return e;
-    int sms = 0, per_sm = 0;
+    int sms = 0;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_kernel<CODEC, 1>, kWarpsPerCta * 32, smem)) !=
-        cudaSuccess)
-        return e;
-    g_static_ctas[dev][CODEC] = (uint32_t)(sms * (per_sm > 0 ? per_sm : 1));
+    for (int hg = 1; hg <= 2; hg++) {
+        int per_sm = 0;
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attention_kernel_ptr(CODEC, hg),
+                                                               kWarpsPerCta * 32, attention_smem_bytes(CODEC, hg))) !=
+            cudaSuccess)
+            return e;
+        g_static_ctas[dev][CODEC][hg - 1] = (uint32_t)(sms * (per_sm > 0 ? per_sm : 1));
+    }
     return cudaSuccess;
 }
 }  // namespace
@@ -1592,9 +1610,10 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
     e = cudaMemsetAsync(counters, 0, sizeof(uint32_t) * (kStaticSegments + kStaticSlots), s);
     if (e != cudaSuccess) { set_cuda_error("qwn_kv_attention_static: clear", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
     const uint32_t segs = r->num_seqs * r->kv_heads;
-    uint32_t ctas = g_static_ctas[dev][r->codec];
     const uint32_t max_ctas = (kStaticSlots - segs) / kWarpsPerCta;  // warps + segments <= slots
-    if (ctas > max_ctas) ctas = max_ctas;
+    uint32_t ctas[2] = {g_static_ctas[dev][r->codec][0], g_static_ctas[dev][r->codec][1]};
+    for (uint32_t &c : ctas)
+        if (c > max_ctas) c = max_ctas;
     AttnArgs A{};
     A.pages = static_cast<const uint8_t *>(r->pages_dev);
     A.tile_bytes = (uint32_t)tb;

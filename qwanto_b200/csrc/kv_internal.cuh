@@ -68,7 +68,7 @@ struct Pool {
     uint8_t *evict_dead = nullptr;      // [max_seqs][max_pages_per_seq]
     int32_t *evict_count = nullptr;     // [max_seqs]
     int32_t *ident = nullptr;           // [max_seqs] 0..max_seqs-1
-    uint32_t attn_ctas = 0, attn_warps = 0;
+    uint32_t attn_ctas = 0, attn_ctas2 = 0, attn_warps = 0;  // grids of the 1- and 2-head-group kernels
     uint64_t max_units = 0, max_segments = 0;
     // host-step staging
     float *stage_q = nullptr, *stage_k = nullptr, *stage_v = nullptr, *stage_o = nullptr;

@@ -30,8 +30,8 @@ std::string last_error() {
     return g_last_error;
 }
 
-size_t attention_smem_bytes(uint32_t codec);
-const void *attention_kernel_ptr(uint32_t codec);
+size_t attention_smem_bytes(uint32_t codec, int hg);
+const void *attention_kernel_ptr(uint32_t codec, int hg);
 
 namespace {
 
@@ -412,18 +412,25 @@ QWN_CUDA_ABI_API int qwn_kv_pool_create(const QwnKvPoolOptions *o, QwnKvPoolHand
     p->page_bytes = tb * p->tiles_per_page * (size_t)o->layers * o->kv_heads;
     p->pool_bytes = p->page_bytes * (size_t)o->total_pages;
 
-    // persistent attention grid: resident CTAs x SMs
-    int sms = 0, per_sm = 0;
+    // persistent attention grids, resident CTAs x SMs, per kernel variant
+    // (one or two head groups of four query heads)
+    int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
-    const void *kern = attention_kernel_ptr(p->codec);
-    const size_t smem = attention_smem_bytes(p->codec);
-    if (kern) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarpsPerCta * 32, smem);
+    uint32_t ctas[2] = {0, 0};
+    for (int hg = 1; hg <= 2; hg++) {
+        int per_sm = 0;
+        const void *kern = attention_kernel_ptr(p->codec, hg);
+        const size_t smem = attention_smem_bytes(p->codec, hg);
+        if (kern) {
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarpsPerCta * 32, smem);
+        }
+        if (per_sm < 1) per_sm = 1;
+        ctas[hg - 1] = (uint32_t)(sms > 0 ? sms : 148) * (uint32_t)per_sm;
     }
-    if (per_sm < 1) per_sm = 1;
-    p->attn_ctas = (uint32_t)(sms > 0 ? sms : 148) * (uint32_t)per_sm;
-    p->attn_warps = p->attn_ctas * kWarpsPerCta;
+    p->attn_ctas = ctas[0];
+    p->attn_ctas2 = ctas[1];
+    p->attn_warps = (ctas[0] > ctas[1] ? ctas[0] : ctas[1]) * kWarpsPerCta;
     p->max_segments = (uint64_t)o->max_seqs * o->kv_heads;
     p->max_units = (uint64_t)o->max_seqs * o->max_pages_per_seq * p->tiles_per_page * o->kv_heads;
     const size_t part_bytes = ((size_t)p->attn_warps + p->max_segments) * kPartialFloats * sizeof(float);
