@@ -10,7 +10,8 @@
 // segment merges the partials in warp order (deterministic).
 //
 // Each warp owns a private pipeline of kStages shared-memory stages filled by
-// 1-D cp.async.bulk copies (no multicast) completed on per-stage mbarriers.
+// 1-D cp.async.bulk copies into its own shared memory, completed on per-stage
+// mbarriers.
 // The tile layout in HBM is arranged so that each lane's mma.sync fragments
 // are a few conflict-free 128-bit shared loads.  Dequantisation happens in
 // registers: biased int8 / 4-bit codes become exact f16 by byte permutes, the

@@ -218,7 +218,7 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
-// 1-D bulk copy global -> shared, completion counted on an mbarrier (no multicast)
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on an mbarrier
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
                                          uint64_t *bar) {
     asm volatile(
