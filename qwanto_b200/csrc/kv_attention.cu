@@ -1167,6 +1167,10 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         fence_barrier_init();
     }
     __syncwarp();
+    // let the stream's next kernel start its CTAs as SMs free up; wait for the
+    // previous kernel's results before the first global access
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const uint32_t HK = A.kv_heads;
     uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
@@ -1395,14 +1399,28 @@ cudaError_t configure_codec() {
                                  (int)codec_smem<CODEC, 2>());
     return e;
 }
-// ctas[hg-1]: the resident grid of each variant
+// ctas[hg-1]: the resident grid of each variant.  Launched as a
+// programmatic dependent: its CTAs may start on SMs the previous kernel of
+// the stream has left while that kernel finishes, and wait (griddepcontrol)
+// for it to complete before touching global memory.
 template <int CODEC>
 cudaError_t launch_variant(const uint32_t (&ctas)[2], const AttnArgs &A, cudaStream_t s) {
-    if (A.group > 4)
-        attn_kernel<CODEC, 2><<<ctas[1], kWarpsPerCta * 32, codec_smem<CODEC, 2>(), s>>>(A);
-    else
-        attn_kernel<CODEC, 1><<<ctas[0], kWarpsPerCta * 32, codec_smem<CODEC, 1>(), s>>>(A);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.blockDim = dim3(kWarpsPerCta * 32);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (A.group > 4) {
+        cfg.gridDim = dim3(ctas[1]);
+        cfg.dynamicSmemBytes = codec_smem<CODEC, 2>();
+        return cudaLaunchKernelEx(&cfg, attn_kernel<CODEC, 2>, A);
+    }
+    cfg.gridDim = dim3(ctas[0]);
+    cfg.dynamicSmemBytes = codec_smem<CODEC, 1>();
+    return cudaLaunchKernelEx(&cfg, attn_kernel<CODEC, 1>, A);
 }
 
 template <int CODEC>
