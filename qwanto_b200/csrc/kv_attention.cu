@@ -35,6 +35,10 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 // a warp range holds at least this many units (small batches use fewer warps)
 constexpr uint64_t kMinUnitsPerWarp = 8;
+// the even split counts each segment as its tiles plus this many virtual
+// units at its start: a warp that starts a new segment (query slicing, a
+// partial written) gets correspondingly fewer tiles
+constexpr uint32_t kVirtualUnits = 2;
 // segments split into more parts merge in two levels: groups of this many
 // parts first, then the group results
 constexpr uint32_t kMergeGroup = 16;
@@ -896,11 +900,13 @@ __device__ __forceinline__ Geo geo_of(const AttnArgs &A, uint32_t i) {
 struct Walk {
     uint32_t i, h, tile;
     uint64_t seg_base;  // global unit index of (i, h, tile 0)
+    uint64_t vbase;     // virtual index of the segment's start (kVirtualUnits before tile 0)
     Geo geo;
 };
 
 __device__ __forceinline__ void walk_next_segment(const AttnArgs &A, Walk &w) {
     w.seg_base += w.geo.ntiles;
+    w.vbase += w.geo.ntiles + kVirtualUnits;
     w.tile = 0;
     if (++w.h == A.kv_heads) {
         w.h = 0;
@@ -942,15 +948,15 @@ struct WarpWindow {
     int32_t app[2][32];
 };
 
-// Request window w for units [base, base+32) of this warp, lane L taking unit
-// base+L, walking forward `skip` units from `from`.
-__device__ __forceinline__ void fill_window(const AttnArgs &A, const Walk &from, uint32_t skip, uint64_t base,
-                                            uint64_t u1, WarpWindow *win, int w) {
+// Request window w for the warp's units [base, base+32) (of n), lane L taking
+// unit base+L, walking forward `skip` units from `from`.
+__device__ __forceinline__ void fill_window(const AttnArgs &A, const Walk &from, uint32_t skip, uint32_t base,
+                                            uint32_t n, WarpWindow *win, int w) {
     const int lane = threadIdx.x & 31;
     int32_t app = -1;
     uint32_t off = 0;
     bool copied = false;
-    if (base + lane < u1) {
+    if (base + lane < n) {
         Walk t = from;
         walk_advance(A, t, skip + lane);
         const uint32_t tg = t.geo.tile0 + t.tile;
@@ -1122,9 +1128,10 @@ __device__ __forceinline__ bool merge_parts(const AttnArgs &A, uint32_t s_idx, u
 template <class OPS>
 __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const typename OPS::State &st, uint32_t s_idx,
                                                    uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid) {
-    // warps whose range meets the segment: warp of unit u is ((u+1)W-1)/T,
-    // and with T >= W (the kernel caps W) every warp range is non-empty
-    const uint64_t wa = ((Us + 1) * W - 1) / T, wb = ((Us + ns) * W - 1) / T;
+    // warps whose range meets the segment's tiles (virtual units Us+V ..
+    // Us+V+ns-1): warp of virtual unit u is ((u+1)W-1)/T, T the virtual total;
+    // the kernel caps W so that every warp range holds real units
+    const uint64_t wa = ((Us + kVirtualUnits + 1) * W - 1) / T, wb = ((Us + kVirtualUnits + ns) * W - 1) / T;
     const uint32_t nparts = (uint32_t)(wb - wa + 1);
     const size_t row0 = (size_t)s_idx * A.group;
     if (nparts == 1) {
@@ -1145,7 +1152,7 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
 __device__ __forceinline__ uint32_t *part_counter(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
                                                   uint64_t T, uint64_t W, uint64_t wid) {
     if (nparts <= kMergeGroup) return &A.counters[s_idx];
-    const uint64_t wa = ((Us + 1) * W - 1) / T;
+    const uint64_t wa = ((Us + kVirtualUnits + 1) * W - 1) / T;
     return &A.gcounters[wa + ((wid - wa) / kMergeGroup) * kMergeGroup + s_idx];
 }
 
@@ -1176,14 +1183,20 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
     uint64_t wid = (uint64_t)blockIdx.x * kWarpsPerCta + warp;
 
-    // total units of the batch
-    uint64_t T = 0;
+    // real units T of the batch and virtual units Tv (each non-empty segment
+    // counts kVirtualUnits more)
+    uint64_t T = 0, Tv = 0;
     for (uint32_t base = 0; base < A.num_seqs; base += 32) {
         const uint32_t i = base + lane;
-        uint32_t u = i < A.num_seqs ? geo_of(A, i).ntiles * HK : 0;
+        const uint32_t nt = i < A.num_seqs ? geo_of(A, i).ntiles : 0;
+        uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits) * HK : 0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
+        for (int o = 16; o > 0; o >>= 1) {
+            u += __shfl_xor_sync(0xffffffffu, u, o);
+            uv += __shfl_xor_sync(0xffffffffu, uv, o);
+        }
         T += u;
+        Tv += uv;
     }
     if (T == 0) return;
     if ((T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp < W) {
@@ -1193,39 +1206,61 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         wid = (uint64_t)warp * gridDim.x + blockIdx.x;
         if (wid >= W) return;
     }
-    const uint64_t u0 = wid * T / W, u1 = (wid + 1) * T / W;
-    if (u0 >= u1) return;
-    const uint32_t n = (uint32_t)(u1 - u0);
+    // this warp's virtual range [v0, v1)
+    const uint64_t v0 = wid * Tv / W, v1 = (wid + 1) * Tv / W;
+    if (v0 >= v1) return;
 
-    // locate u0
+    // locate v0: its segment, and the warp's first real unit
     Walk cons;
     {
-        uint64_t acc = 0;
+        uint64_t acc = 0, accv = 0;
         for (uint32_t base = 0; base < A.num_seqs; base += 32) {
             const uint32_t i = base + lane;
-            const uint32_t u = i < A.num_seqs ? geo_of(A, i).ntiles * HK : 0;
-            const uint32_t incl = warp_incl_scan(u);
-            const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
-            if (u0 < acc + tot) {
-                const uint32_t ball = __ballot_sync(0xffffffffu, acc + incl > u0);
+            const uint32_t nt = i < A.num_seqs ? geo_of(A, i).ntiles : 0;
+            const uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits) * HK : 0;
+            const uint32_t incl = warp_incl_scan(u), inclv = warp_incl_scan(uv);
+            const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31), totv = __shfl_sync(0xffffffffu, inclv, 31);
+            if (v0 < accv + totv) {
+                const uint32_t ball = __ballot_sync(0xffffffffu, accv + inclv > v0);
                 const int L = __ffs(ball) - 1;
                 const uint32_t excl = __shfl_sync(0xffffffffu, incl - u, L);
+                const uint32_t exclv = __shfl_sync(0xffffffffu, inclv - uv, L);
                 cons.i = base + L;
                 cons.geo = geo_of(A, cons.i);
-                const uint64_t rem = u0 - (acc + excl);
-                cons.h = (uint32_t)(rem / cons.geo.ntiles);
-                cons.tile = (uint32_t)(rem % cons.geo.ntiles);
+                const uint32_t span = cons.geo.ntiles + kVirtualUnits;
+                const uint64_t rem = v0 - (accv + exclv);
+                cons.h = (uint32_t)(rem / span);
+                const uint32_t off = (uint32_t)(rem % span);
+                cons.tile = off < kVirtualUnits ? 0u : off - kVirtualUnits;
                 cons.seg_base = acc + excl + (uint64_t)cons.h * cons.geo.ntiles;
+                cons.vbase = accv + exclv + (uint64_t)cons.h * span;
                 break;
             }
             acc += tot;
+            accv += totv;
         }
     }
+    // real units in [v0, v1): the range minus the virtual units at segment starts
+    uint32_t n = 0;
+    {
+        Walk t = cons;
+        uint64_t pos = t.vbase + kVirtualUnits + t.tile;
+        if (pos < v0) pos = v0;
+        while (pos < v1) {
+            const uint64_t seg_end = t.vbase + kVirtualUnits + t.geo.ntiles;
+            n += (uint32_t)((v1 < seg_end ? v1 : seg_end) - pos);
+            if (seg_end >= v1) break;
+            walk_next_segment(A, t);
+            if (t.i >= A.num_seqs) break;
+            pos = t.vbase + kVirtualUnits;
+        }
+    }
+    if (n == 0) return;
 
     // window `cw` holds units [wbase, wbase+32) of this warp's range
     uint32_t wbase = 0;
     int cw = 0;
-    fill_window(A, cons, 0, u0, u1, win, 0);
+    fill_window(A, cons, 0, 0, n, win, 0);
     window_ready();
     const uint32_t npro = n < (uint32_t)S ? n : (uint32_t)S;
     for (uint32_t j = 0; j < npro; j++) {
@@ -1252,7 +1287,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         if (cons.tile == 0 || k == 0) OPS::begin(frag, state, A, cons.i * HK + cons.h);
         if (pend_n && !counted0 && k == pend_k0 + 4u) {
             __syncwarp();
-            if (lane == 0) tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, pend_n0, pend_u0, T, W, wid), 1u);
+            if (lane == 0) tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, pend_n0, pend_u0, Tv, W, wid), 1u);
             counted0 = true;  // the ticket is read after the loop
         }
         if (cons.tile + 4u == cons.geo.ntiles) {
@@ -1277,14 +1312,14 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         const int t_hi = min(cons.geo.tok_hi - tile_tok0, 16);
         float psum[HG];
         OPS::step(wsm + st * B, frag, state, t_lo, t_hi, psum);
-        if (A.tile_mass) OPS::mass(A, u0 + k, state, psum);
+        if (A.tile_mass) OPS::mass(A, cons.seg_base + cons.tile, state, psum);
         __syncwarp();
 
         // refill this stage with unit k + S
         const uint32_t j = k + (uint32_t)S;
         if (j < n) {
             if (j - wbase == 16u && wbase + 32u < n)  // request the next window early
-                fill_window(A, cons, wbase + 32u - k, u0 + wbase + 32u, u1, win, cw ^ 1);
+                fill_window(A, cons, wbase + 32u - k, wbase + 32u, n, win, cw ^ 1);
             if (j - wbase == 32u) {
                 wbase = j;
                 cw ^= 1;
@@ -1306,11 +1341,11 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         // end of this warp's share of the segment?
         if (cons.tile + 1 == cons.geo.ntiles || k + 1 == n) {
             const uint32_t s_idx = cons.i * HK + cons.h;
-            const uint32_t np = finish_segment<OPS>(A, state, s_idx, cons.seg_base, cons.geo.ntiles, T, W, wid);
+            const uint32_t np = finish_segment<OPS>(A, state, s_idx, cons.vbase, cons.geo.ntiles, Tv, W, wid);
             if (np) {
                 const int e = pend_n++;  // at most two: the segment the range starts in and the one it ends in
-                if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.seg_base; pend_k0 = k; }
-                else { pend_s1 = s_idx; pend_n1 = np; pend_u1 = cons.seg_base; }
+                if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.vbase; pend_k0 = k; }
+                else { pend_s1 = s_idx; pend_n1 = np; pend_u1 = cons.vbase; }
             }
         }
         // next unit
@@ -1326,14 +1361,15 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     __syncwarp();
     uint32_t tk1 = 0;
     if (lane == 0) {
-        if (pend_n > 0 && !counted0) tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, pend_n0, pend_u0, T, W, wid), 1u);
-        if (pend_n > 1) tk1 = atom_add_acq_rel_gpu(part_counter(A, pend_s1, pend_n1, pend_u1, T, W, wid), 1u);
+        if (pend_n > 0 && !counted0)
+            tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, pend_n0, pend_u0, Tv, W, wid), 1u);
+        if (pend_n > 1) tk1 = atom_add_acq_rel_gpu(part_counter(A, pend_s1, pend_n1, pend_u1, Tv, W, wid), 1u);
     }
     tk0 = __shfl_sync(0xffffffffu, tk0, 0);
     tk1 = __shfl_sync(0xffffffffu, tk1, 0);
     for (uint32_t e = 0; e < pend_n; e++) {
         const uint32_t np = e ? pend_n1 : pend_n0, s_idx = e ? pend_s1 : pend_s0;
-        const uint64_t wa = (((e ? pend_u1 : pend_u0) + 1) * W - 1) / T;
+        const uint64_t wa = (((e ? pend_u1 : pend_u0) + kVirtualUnits + 1) * W - 1) / Tv;
         const uint32_t tk = e ? tk1 : tk0;
         uint8_t *buf = wsm;
         const uint32_t SB = (uint32_t)(S * B);
