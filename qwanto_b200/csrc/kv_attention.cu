@@ -37,8 +37,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint64_t kMinUnitsPerWarp = 8;
 // the even split counts each segment as its tiles plus this many virtual
 // units at its start: a warp that starts a new segment (query slicing, a
-// partial written) gets correspondingly fewer tiles
+// partial written) gets correspondingly fewer tiles; when the launch stores
+// the newest token, kVirtualEnd more at the segment's end charge that store
 constexpr uint32_t kVirtualUnits = 2;
+constexpr uint32_t kVirtualEnd = 2;
 // segments split into more parts merge in two levels: groups of this many
 // parts first, then the group results
 constexpr uint32_t kMergeGroup = 16;
@@ -897,6 +899,9 @@ __device__ __forceinline__ Geo geo_of(const AttnArgs &A, uint32_t i) {
 }
 
 // position of a unit: batch entry i, kv head h, tile within the entry
+// virtual units at a segment's end: the newest token's store, when the launch appends
+__device__ __forceinline__ uint32_t virtual_tail(const AttnArgs &A) { return A.new_k ? kVirtualEnd : 0u; }
+
 struct Walk {
     uint32_t i, h, tile;
     uint64_t seg_base;  // global unit index of (i, h, tile 0)
@@ -906,7 +911,7 @@ struct Walk {
 
 __device__ __forceinline__ void walk_next_segment(const AttnArgs &A, Walk &w) {
     w.seg_base += w.geo.ntiles;
-    w.vbase += w.geo.ntiles + kVirtualUnits;
+    w.vbase += w.geo.ntiles + kVirtualUnits + virtual_tail(A);
     w.tile = 0;
     if (++w.h == A.kv_heads) {
         w.h = 0;
@@ -968,7 +973,16 @@ __device__ __forceinline__ void fill_window(const AttnArgs &A, const Walk &from,
                          : "memory");
             copied = true;
         }
-        if (A.new_k && t.tile + 1 == t.geo.ntiles) app = (int32_t)(t.i * A.kv_heads + t.h);
+        if (A.new_k && t.tile + 1 == t.geo.ntiles) {
+            app = (int32_t)(t.i * A.kv_heads + t.h);
+            // the newest token's K and V rows (512 B each) into L1 for its store
+            const float *rk = A.new_k + (size_t)app * kHeadDim, *rv = A.new_v + (size_t)app * kHeadDim;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(rk + 32 * c));
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(rv + 32 * c));
+            }
+        }
     }
     if (!copied) win->pg[w][lane] = -1;
     win->off[w][lane] = off;
@@ -1189,7 +1203,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     for (uint32_t base = 0; base < A.num_seqs; base += 32) {
         const uint32_t i = base + lane;
         const uint32_t nt = i < A.num_seqs ? geo_of(A, i).ntiles : 0;
-        uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits) * HK : 0;
+        uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits + virtual_tail(A)) * HK : 0;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             u += __shfl_xor_sync(0xffffffffu, u, o);
@@ -1217,7 +1231,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         for (uint32_t base = 0; base < A.num_seqs; base += 32) {
             const uint32_t i = base + lane;
             const uint32_t nt = i < A.num_seqs ? geo_of(A, i).ntiles : 0;
-            const uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits) * HK : 0;
+            const uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits + virtual_tail(A)) * HK : 0;
             const uint32_t incl = warp_incl_scan(u), inclv = warp_incl_scan(uv);
             const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31), totv = __shfl_sync(0xffffffffu, inclv, 31);
             if (v0 < accv + totv) {
@@ -1227,13 +1241,17 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
                 const uint32_t exclv = __shfl_sync(0xffffffffu, inclv - uv, L);
                 cons.i = base + L;
                 cons.geo = geo_of(A, cons.i);
-                const uint32_t span = cons.geo.ntiles + kVirtualUnits;
+                const uint32_t span = cons.geo.ntiles + kVirtualUnits + virtual_tail(A);
                 const uint64_t rem = v0 - (accv + exclv);
                 cons.h = (uint32_t)(rem / span);
                 const uint32_t off = (uint32_t)(rem % span);
                 cons.tile = off < kVirtualUnits ? 0u : off - kVirtualUnits;
                 cons.seg_base = acc + excl + (uint64_t)cons.h * cons.geo.ntiles;
                 cons.vbase = accv + exclv + (uint64_t)cons.h * span;
+                if (cons.tile >= cons.geo.ntiles) {  // v0 is in the segment's tail: start at the next
+                    cons.tile = 0;
+                    walk_next_segment(A, cons);
+                }
                 break;
             }
             acc += tot;
