@@ -872,16 +872,42 @@ struct Geo {
     uint32_t tile0, ntiles;
 };
 
+// (sequence id, length) of the first kLenCache batch entries, filled once per
+// CTA at launch start: every warp's setup walks these, and the CTA reads the
+// sequence table once instead of once per warp
+constexpr uint32_t kLenCache = 256;
+__device__ __forceinline__ int2 *len_cache() {
+    __shared__ int2 cache[kLenCache];
+    return cache;
+}
+__device__ __forceinline__ void fill_len_cache(const AttnArgs &A) {
+    const uint32_t n = A.num_seqs < kLenCache ? A.num_seqs : kLenCache;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const int32_t seq = A.seq_ids ? A.seq_ids[i] : (int32_t)i;
+        const int32_t len = (seq >= 0 && (uint32_t)seq < A.max_seqs) ? A.seq_lens[seq] : 0;
+        len_cache()[i] = make_int2(seq, len);
+    }
+    __syncthreads();
+}
+
 __device__ __forceinline__ Geo geo_of(const AttnArgs &A, uint32_t i) {
     Geo g;
-    g.seq = A.seq_ids ? A.seq_ids[i] : (int32_t)i;
+    int32_t len = 0;
+    if (i < kLenCache) {
+        const int2 c = len_cache()[i];
+        g.seq = c.x;
+        len = c.y;
+    } else {
+        g.seq = A.seq_ids ? A.seq_ids[i] : (int32_t)i;
+    }
     g.tok_lo = g.tok_hi = 0;
     g.tile0 = g.ntiles = 0;
     if (g.seq < 0 || (uint32_t)g.seq >= A.max_seqs) {
         latch(A.status, QWN_KV_STATUS_BAD_SEQUENCE);
         return g;
     }
-    int32_t hi = A.seq_lens[g.seq];
+    if (i >= kLenCache) len = A.seq_lens[g.seq];
+    int32_t hi = len;
     if (A.attend_limit && hi > (int32_t)A.attend_limit) hi = (int32_t)A.attend_limit;
     if (A.t_end && hi > (int32_t)A.t_end) hi = (int32_t)A.t_end;
     const int32_t lo = (int32_t)A.t_begin;
@@ -898,10 +924,10 @@ __device__ __forceinline__ Geo geo_of(const AttnArgs &A, uint32_t i) {
     return g;
 }
 
-// position of a unit: batch entry i, kv head h, tile within the entry
 // virtual units at a segment's end: the newest token's store, when the launch appends
 __device__ __forceinline__ uint32_t virtual_tail(const AttnArgs &A) { return A.new_k ? kVirtualEnd : 0u; }
 
+// position of a unit: batch entry i, kv head h, tile within the entry
 struct Walk {
     uint32_t i, h, tile;
     uint64_t seg_base;  // global unit index of (i, h, tile 0)
@@ -1192,6 +1218,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     // previous kernel's results before the first global access
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    fill_len_cache(A);
 
     const uint32_t HK = A.kv_heads;
     uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
