@@ -63,6 +63,7 @@ struct AttnArgs {
     float *partials;
     uint32_t *counters;   // [segments]: parts (or merged groups) counted per segment
     uint32_t *gcounters;  // [warps + segments]: parts counted per merge group (slot index of its first part)
+    uint32_t *plans;      // launch plans ([0] = epoch); null: compute the setup every launch
     float2 *tile_mass;
     float2 *seg_ml;
     float *part_m, *part_l, *part_o;  // non-null: export unnormalised (m, l, o)
@@ -927,6 +928,21 @@ __device__ __forceinline__ Geo geo_of(const AttnArgs &A, uint32_t i) {
 // virtual units at a segment's end: the newest token's store, when the launch appends
 __device__ __forceinline__ uint32_t virtual_tail(const AttnArgs &A) { return A.new_k ? kVirtualEnd : 0u; }
 
+// floor(x / c) for x < 2^53: a double quotient (off by at most one)
+// corrected to the exact integer, instead of a 64-bit integer division
+__device__ __forceinline__ uint64_t floor_div(uint64_t x, uint64_t c) {
+    uint64_t q = (uint64_t)((double)x / (double)c);
+    if (q * c > x) --q;
+    else if ((q + 1) * c <= x) ++q;
+    return q;
+}
+__device__ __forceinline__ uint64_t muldiv_floor(uint64_t a, uint64_t b, uint64_t c) { return floor_div(a * b, c); }
+
+// the warp whose range [w*T/W, (w+1)*T/W) holds unit u: ((u+1)W - 1) / T
+__device__ __forceinline__ uint64_t warp_of_unit(uint64_t u, uint64_t T, uint64_t W) {
+    return floor_div((u + 1) * W - 1, T);
+}
+
 // position of a unit: batch entry i, kv head h, tile within the entry
 struct Walk {
     uint32_t i, h, tile;
@@ -977,7 +993,18 @@ struct WarpWindow {
     int32_t pg[2][32];
     uint32_t off[2][32];
     int32_t app[2][32];
+    uint32_t hv[2][32];  // h * tiles_per_page + tile in page (layer-free part of off)
 };
+
+// the newest token's K and V rows (512 B each) of segment `app` into L1 for its store
+__device__ __forceinline__ void prefetch_new_rows(const AttnArgs &A, int32_t app) {
+    const float *rk = A.new_k + (size_t)app * kHeadDim, *rv = A.new_v + (size_t)app * kHeadDim;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(rk + 32 * c));
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(rv + 32 * c));
+    }
+}
 
 // Request window w for the warp's units [base, base+32) (of n), lane L taking
 // unit base+L, walking forward `skip` units from `from`.
@@ -985,14 +1012,15 @@ __device__ __forceinline__ void fill_window(const AttnArgs &A, const Walk &from,
                                             uint32_t n, WarpWindow *win, int w) {
     const int lane = threadIdx.x & 31;
     int32_t app = -1;
-    uint32_t off = 0;
+    uint32_t off = 0, hv = 0;
     bool copied = false;
     if (base + lane < n) {
         Walk t = from;
         walk_advance(A, t, skip + lane);
         const uint32_t tg = t.geo.tile0 + t.tile;
         const uint32_t lp = tg / A.tpp, tin = tg % A.tpp;
-        off = ((A.layer * A.kv_heads + t.h) * A.tpp + tin) * A.tile_bytes;
+        hv = t.h * A.tpp + tin;
+        off = (A.layer * A.kv_heads * A.tpp + hv) * A.tile_bytes;
         if (lp < A.mp) {
             const int32_t *src = A.page_table + (size_t)t.geo.seq * A.mp + lp;
             asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(&win->pg[w][lane])), "l"(src)
@@ -1001,18 +1029,13 @@ __device__ __forceinline__ void fill_window(const AttnArgs &A, const Walk &from,
         }
         if (A.new_k && t.tile + 1 == t.geo.ntiles) {
             app = (int32_t)(t.i * A.kv_heads + t.h);
-            // the newest token's K and V rows (512 B each) into L1 for its store
-            const float *rk = A.new_k + (size_t)app * kHeadDim, *rv = A.new_v + (size_t)app * kHeadDim;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                asm volatile("prefetch.global.L1 [%0];" ::"l"(rk + 32 * c));
-                asm volatile("prefetch.global.L1 [%0];" ::"l"(rv + 32 * c));
-            }
+            prefetch_new_rows(A, app);
         }
     }
     if (!copied) win->pg[w][lane] = -1;
     win->off[w][lane] = off;
     win->app[w][lane] = app;
+    win->hv[w][lane] = hv;
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 // wait for this warp's window requests
@@ -1171,7 +1194,7 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
     // warps whose range meets the segment's tiles (virtual units Us+V ..
     // Us+V+ns-1): warp of virtual unit u is ((u+1)W-1)/T, T the virtual total;
     // the kernel caps W so that every warp range holds real units
-    const uint64_t wa = ((Us + kVirtualUnits + 1) * W - 1) / T, wb = ((Us + kVirtualUnits + ns) * W - 1) / T;
+    const uint64_t wa = warp_of_unit(Us + kVirtualUnits, T, W), wb = warp_of_unit(Us + kVirtualUnits + ns - 1, T, W);
     const uint32_t nparts = (uint32_t)(wb - wa + 1);
     const size_t row0 = (size_t)s_idx * A.group;
     if (nparts == 1) {
@@ -1192,7 +1215,7 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
 __device__ __forceinline__ uint32_t *part_counter(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
                                                   uint64_t T, uint64_t W, uint64_t wid) {
     if (nparts <= kMergeGroup) return &A.counters[s_idx];
-    const uint64_t wa = ((Us + kVirtualUnits + 1) * W - 1) / T;
+    const uint64_t wa = warp_of_unit(Us + kVirtualUnits, T, W);
     return &A.gcounters[wa + ((wid - wa) / kMergeGroup) * kMergeGroup + s_idx];
 }
 
@@ -1218,95 +1241,146 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     // previous kernel's results before the first global access
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    fill_len_cache(A);
 
     const uint32_t HK = A.kv_heads;
     uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
     uint64_t wid = (uint64_t)blockIdx.x * kWarpsPerCta + warp;
 
-    // real units T of the batch and virtual units Tv (each non-empty segment
-    // counts kVirtualUnits more)
-    uint64_t T = 0, Tv = 0;
-    for (uint32_t base = 0; base < A.num_seqs; base += 32) {
-        const uint32_t i = base + lane;
-        const uint32_t nt = i < A.num_seqs ? geo_of(A, i).ntiles : 0;
-        uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits + virtual_tail(A)) * HK : 0;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            u += __shfl_xor_sync(0xffffffffu, u, o);
-            uv += __shfl_xor_sync(0xffffffffu, uv, o);
-        }
-        T += u;
-        Tv += uv;
+    // The setup below depends only on the batch geometry, which is the same for
+    // every layer of a decode step: it is cached per warp (per-step launch
+    // plan) under a key of the pool's epoch (bumped by every change of lengths
+    // or page tables) and the launch parameters.  The record is loaded while
+    // the CTA reads the sequence table.
+    uint32_t *plan = A.plans ? A.plans + 32 + ((size_t)blockIdx.x * kWarpsPerCta + warp) * kPlanWords : nullptr;
+    uint32_t pw0 = 0, pw1 = 0, pw2 = 0, pw3 = 0, epoch = 0;
+    if (plan) {
+        pw0 = plan[lane]; pw1 = plan[32 + lane]; pw2 = plan[64 + lane]; pw3 = plan[96 + lane];
+        epoch = A.plans[0];
     }
-    if (T == 0) return;
-    if ((T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp < W) {
-        // a small batch: fewer, longer warp ranges (every split is a partial
-        // to merge), spread over the SMs by numbering warps across CTAs
-        W = (T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
-        wid = (uint64_t)warp * gridDim.x + blockIdx.x;
-        if (wid >= W) return;
-    }
-    // this warp's virtual range [v0, v1)
-    const uint64_t v0 = wid * Tv / W, v1 = (wid + 1) * Tv / W;
-    if (v0 >= v1) return;
+    fill_len_cache(A);
+    const uint32_t key = lane == 0 ? epoch : lane == 1 ? A.num_seqs : lane == 2 ? A.attend_limit
+                       : lane == 3 ? A.t_begin : lane == 4 ? A.t_end : lane == 5 ? (A.new_k ? 1u : 0u)
+                       : lane == 6 ? gridDim.x : 0x504C414Eu;
+    const bool hit = plan != nullptr && __all_sync(0xffffffffu, lane >= 8 || pw0 == key);
 
-    // locate v0: its segment, and the warp's first real unit
     Walk cons;
-    {
-        uint64_t acc = 0, accv = 0;
+    uint32_t n = 0;
+    uint64_t Tv = 0;
+    int cw = 0;
+    uint32_t wbase = 0;
+    if (hit) {
+        auto w32 = [&](int i) { return __shfl_sync(0xffffffffu, pw0, i); };
+        auto w64 = [&](int i) { return (uint64_t)w32(i) | ((uint64_t)w32(i + 1) << 32); };
+        n = w32(20);
+        if (n == 0) return;
+        cons.i = w32(8); cons.h = w32(9); cons.tile = w32(10);
+        cons.seg_base = w64(11); cons.vbase = w64(13);
+        cons.geo.seq = (int32_t)w32(15); cons.geo.tok_lo = (int32_t)w32(16); cons.geo.tok_hi = (int32_t)w32(17);
+        cons.geo.tile0 = w32(18); cons.geo.ntiles = w32(19);
+        Tv = w64(21); W = w64(23); wid = w64(25);
+        win->pg[0][lane] = (int32_t)pw1;
+        win->hv[0][lane] = pw2;
+        win->off[0][lane] = (A.layer * HK * A.tpp + pw2) * A.tile_bytes;
+        win->app[0][lane] = (int32_t)pw3;
+        if ((int32_t)pw3 >= 0) prefetch_new_rows(A, (int32_t)pw3);
+        __syncwarp();
+    } else {
+        // real units T of the batch and virtual units Tv (each non-empty
+        // segment counts kVirtualUnits more)
+        uint64_t T = 0;
         for (uint32_t base = 0; base < A.num_seqs; base += 32) {
             const uint32_t i = base + lane;
             const uint32_t nt = i < A.num_seqs ? geo_of(A, i).ntiles : 0;
-            const uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits + virtual_tail(A)) * HK : 0;
-            const uint32_t incl = warp_incl_scan(u), inclv = warp_incl_scan(uv);
-            const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31), totv = __shfl_sync(0xffffffffu, inclv, 31);
-            if (v0 < accv + totv) {
-                const uint32_t ball = __ballot_sync(0xffffffffu, accv + inclv > v0);
-                const int L = __ffs(ball) - 1;
-                const uint32_t excl = __shfl_sync(0xffffffffu, incl - u, L);
-                const uint32_t exclv = __shfl_sync(0xffffffffu, inclv - uv, L);
-                cons.i = base + L;
-                cons.geo = geo_of(A, cons.i);
-                const uint32_t span = cons.geo.ntiles + kVirtualUnits + virtual_tail(A);
-                const uint64_t rem = v0 - (accv + exclv);
-                cons.h = (uint32_t)(rem / span);
-                const uint32_t off = (uint32_t)(rem % span);
-                cons.tile = off < kVirtualUnits ? 0u : off - kVirtualUnits;
-                cons.seg_base = acc + excl + (uint64_t)cons.h * cons.geo.ntiles;
-                cons.vbase = accv + exclv + (uint64_t)cons.h * span;
-                if (cons.tile >= cons.geo.ntiles) {  // v0 is in the segment's tail: start at the next
-                    cons.tile = 0;
-                    walk_next_segment(A, cons);
-                }
-                break;
+            uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits + virtual_tail(A)) * HK : 0;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                u += __shfl_xor_sync(0xffffffffu, u, o);
+                uv += __shfl_xor_sync(0xffffffffu, uv, o);
             }
-            acc += tot;
-            accv += totv;
+            T += u;
+            Tv += uv;
         }
-    }
-    // real units in [v0, v1): the range minus the virtual units at segment starts
-    uint32_t n = 0;
-    {
-        Walk t = cons;
-        uint64_t pos = t.vbase + kVirtualUnits + t.tile;
-        if (pos < v0) pos = v0;
-        while (pos < v1) {
-            const uint64_t seg_end = t.vbase + kVirtualUnits + t.geo.ntiles;
-            n += (uint32_t)((v1 < seg_end ? v1 : seg_end) - pos);
-            if (seg_end >= v1) break;
-            walk_next_segment(A, t);
-            if (t.i >= A.num_seqs) break;
-            pos = t.vbase + kVirtualUnits;
+        if (T != 0 && (T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp < W) {
+            // a small batch: fewer, longer warp ranges (every split is a partial
+            // to merge), spread over the SMs by numbering warps across CTAs
+            W = (T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
+            wid = (uint64_t)warp * gridDim.x + blockIdx.x;
         }
+        // this warp's virtual range [v0, v1)
+        const uint64_t v0 = muldiv_floor(wid, Tv, W), v1 = muldiv_floor(wid + 1, Tv, W);
+        if (T != 0 && wid < W && v0 < v1) {
+            // locate v0: its segment, and the warp's first real unit
+            uint64_t acc = 0, accv = 0;
+            for (uint32_t base = 0; base < A.num_seqs; base += 32) {
+                const uint32_t i = base + lane;
+                const uint32_t nt = i < A.num_seqs ? geo_of(A, i).ntiles : 0;
+                const uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits + virtual_tail(A)) * HK : 0;
+                const uint32_t incl = warp_incl_scan(u), inclv = warp_incl_scan(uv);
+                const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31), totv = __shfl_sync(0xffffffffu, inclv, 31);
+                if (v0 < accv + totv) {
+                    const uint32_t ball = __ballot_sync(0xffffffffu, accv + inclv > v0);
+                    const int L = __ffs(ball) - 1;
+                    const uint32_t excl = __shfl_sync(0xffffffffu, incl - u, L);
+                    const uint32_t exclv = __shfl_sync(0xffffffffu, inclv - uv, L);
+                    cons.i = base + L;
+                    cons.geo = geo_of(A, cons.i);
+                    const uint32_t span = cons.geo.ntiles + kVirtualUnits + virtual_tail(A);
+                    const uint32_t rem = (uint32_t)(v0 - (accv + exclv));  // < one sequence's virtual units
+                    cons.h = rem / span;
+                    const uint32_t off = rem - cons.h * span;
+                    cons.tile = off < kVirtualUnits ? 0u : off - kVirtualUnits;
+                    cons.seg_base = acc + excl + (uint64_t)cons.h * cons.geo.ntiles;
+                    cons.vbase = accv + exclv + (uint64_t)cons.h * span;
+                    if (cons.tile >= cons.geo.ntiles) {  // v0 is in the segment's tail: start at the next
+                        cons.tile = 0;
+                        walk_next_segment(A, cons);
+                    }
+                    break;
+                }
+                acc += tot;
+                accv += totv;
+            }
+            // real units in [v0, v1): the range minus the virtual units around segments
+            Walk t = cons;
+            uint64_t pos = t.vbase + kVirtualUnits + t.tile;
+            if (pos < v0) pos = v0;
+            while (pos < v1) {
+                const uint64_t seg_end = t.vbase + kVirtualUnits + t.geo.ntiles;
+                n += (uint32_t)((v1 < seg_end ? v1 : seg_end) - pos);
+                if (seg_end >= v1) break;
+                walk_next_segment(A, t);
+                if (t.i >= A.num_seqs) break;
+                pos = t.vbase + kVirtualUnits;
+            }
+        }
+        if (n) {
+            fill_window(A, cons, 0, 0, n, win, 0);
+            window_ready();
+        }
+        if (plan) {  // record the plan for the following launches of this step
+            if (lane == 0) {
+                for (int i = 0; i < 8; i++) plan[i] = 0xFFFFFFFFu;  // key last
+                plan[8] = cons.i; plan[9] = cons.h; plan[10] = cons.tile;
+                plan[11] = (uint32_t)cons.seg_base; plan[12] = (uint32_t)(cons.seg_base >> 32);
+                plan[13] = (uint32_t)cons.vbase; plan[14] = (uint32_t)(cons.vbase >> 32);
+                plan[15] = (uint32_t)cons.geo.seq; plan[16] = (uint32_t)cons.geo.tok_lo;
+                plan[17] = (uint32_t)cons.geo.tok_hi; plan[18] = cons.geo.tile0; plan[19] = cons.geo.ntiles;
+                plan[20] = n;
+                plan[21] = (uint32_t)Tv; plan[22] = (uint32_t)(Tv >> 32);
+                plan[23] = (uint32_t)W; plan[24] = (uint32_t)(W >> 32);
+                plan[25] = (uint32_t)wid; plan[26] = (uint32_t)(wid >> 32);
+            }
+            if (n) {
+                plan[32 + lane] = (uint32_t)win->pg[0][lane];
+                plan[64 + lane] = win->hv[0][lane];
+                plan[96 + lane] = (uint32_t)win->app[0][lane];
+            }
+            __syncwarp();
+            if (lane < 8) plan[lane] = key;
+        }
+        if (n == 0) return;
     }
-    if (n == 0) return;
 
-    // window `cw` holds units [wbase, wbase+32) of this warp's range
-    uint32_t wbase = 0;
-    int cw = 0;
-    fill_window(A, cons, 0, 0, n, win, 0);
-    window_ready();
     const uint32_t npro = n < (uint32_t)S ? n : (uint32_t)S;
     for (uint32_t j = 0; j < npro; j++) {
         const int32_t seg = win->app[0][j];
@@ -1414,7 +1488,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     tk1 = __shfl_sync(0xffffffffu, tk1, 0);
     for (uint32_t e = 0; e < pend_n; e++) {
         const uint32_t np = e ? pend_n1 : pend_n0, s_idx = e ? pend_s1 : pend_s0;
-        const uint64_t wa = (((e ? pend_u1 : pend_u0) + kVirtualUnits + 1) * W - 1) / Tv;
+        const uint64_t wa = warp_of_unit((e ? pend_u1 : pend_u0) + kVirtualUnits, Tv, W);
         const uint32_t tk = e ? tk1 : tk0;
         uint8_t *buf = wsm;
         const uint32_t SB = (uint32_t)(S * B);
@@ -1579,6 +1653,9 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
     A.partials = p->partials;
     A.counters = p->counters;
     A.gcounters = p->counters + p->max_segments;
+    // plans are keyed by the pool's epoch, not by the contents of a caller's
+    // sequence-id array: cache them only for the identity batch
+    A.plans = a.seq_ids ? nullptr : p->plans;
     A.tile_mass = a.page_mass ? p->tile_mass : nullptr;
     A.seg_ml = a.page_mass ? p->seg_ml : nullptr;
     A.part_m = a.part_m;

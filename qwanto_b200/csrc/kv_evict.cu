@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(1024) evict_compact_kernel(uint32_t n, const i
                                                              int32_t *lens, int32_t *npages, int32_t *table,
                                                              float *scores, int32_t *free_stack,
                                                              int32_t *free_top, uint32_t P, uint32_t mp,
-                                                             uint32_t total_pages) {
+                                                             uint32_t total_pages, uint32_t *epoch) {
     using Scan = cub::BlockScan<int, 1024>;
     __shared__ typename Scan::TempStorage tmp;
     int32_t top = *free_top;
@@ -159,7 +159,10 @@ __global__ void __launch_bounds__(1024) evict_compact_kernel(uint32_t n, const i
         }
         __syncthreads();
     }
-    if (threadIdx.x == 0) *free_top = top;
+    if (threadIdx.x == 0) {
+        *free_top = top;
+        atomicAdd(epoch, 1u);  // lengths and tables changed: cached attention plans are stale
+    }
 }
 
 }  // namespace
@@ -192,7 +195,8 @@ cudaError_t launch_evict(Pool *p, uint32_t n, const int32_t *seq_ids, const floa
     if (e != cudaSuccess) return e;
     evict_compact_kernel<<<1, 1024, 0, s>>>(n, seq_ids, p->evict_dead, p->evict_count, p->seq_lens,
                                             p->seq_pages, p->page_table, p->page_scores, p->free_stack,
-                                            p->free_top, p->page_tokens, p->max_pages_per_seq, p->total_pages);
+                                            p->free_top, p->page_tokens, p->max_pages_per_seq, p->total_pages,
+                                            p->plans);
     count_launch();
     return cudaGetLastError();
 }

@@ -63,6 +63,10 @@ struct Pool {
     // attention scratch
     float *partials = nullptr;          // [warps + segments][kPartialFloats]
     uint32_t *counters = nullptr;       // [segments] then [warps + segments] (merge groups)
+    // per-step launch plans of the attention kernel: word 0 is the epoch that
+    // every change of lengths or page tables increments, then kPlanWords per
+    // warp (see kv_attention.cu)
+    uint32_t *plans = nullptr;
     float2 *tile_mass = nullptr;        // [units][kMaxGroup] (u, m) per tile and row
     float2 *seg_ml = nullptr;           // [segments][kMaxGroup] final (m, l)
     uint8_t *evict_dead = nullptr;      // [max_seqs][max_pages_per_seq]
@@ -79,6 +83,9 @@ struct Pool {
 };
 
 constexpr int kPartialFloats = kMaxGroup * kHeadDim + 2 * kMaxGroup;  // room for o[G][128], m[G], l[G]
+// launch plans: a 32-word header (word 0 = epoch), then kPlanWords per warp
+constexpr uint32_t kPlanWords = 128;
+inline size_t plan_words(const Pool *p) { return 32 + (size_t)p->attn_warps * kPlanWords; }
 // merge counters of a pool: one per segment, then one per partial slot
 // (the counter of a merge group sits at its first part's slot index)
 inline size_t counter_count(const Pool *p) { return (size_t)p->max_segments * 2 + p->attn_warps; }

@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(32) seq_append_kernel(uint32_t n, const int32_
                                                         int32_t *lens, int32_t *npages, int32_t *table,
                                                         float *scores, const int32_t *free_stack,
                                                         int32_t *free_top, uint32_t P, uint32_t mp,
-                                                        uint32_t max_seqs, uint32_t *status) {
+                                                        uint32_t max_seqs, uint32_t *status, uint32_t *epoch) {
     const int lane = threadIdx.x;
     int total = 0;
     uint32_t bad = 0;
@@ -208,7 +208,10 @@ __global__ void __launch_bounds__(32) seq_append_kernel(uint32_t n, const int32_
         }
         carry += chunk;
     }
-    if (lane == 0) *free_top = top - carry;
+    if (lane == 0) {
+        *free_top = top - carry;
+        atomicAdd(epoch, 1u);  // lengths and tables changed: cached attention plans are stale
+    }
 }
 
 __global__ void iota_i32(int32_t *p, size_t n) {
@@ -268,7 +271,7 @@ cudaError_t launch_seq_append(Pool *p, uint32_t n, const int32_t *seq_ids, const
     if (n == 0) return cudaSuccess;
     seq_append_kernel<<<1, 32, 0, s>>>(n, seq_ids, counts, p->seq_lens, p->seq_pages, p->page_table,
                                          p->page_scores, p->free_stack, p->free_top, p->page_tokens,
-                                         p->max_pages_per_seq, p->max_seqs, p->status);
+                                         p->max_pages_per_seq, p->max_seqs, p->status, p->plans);
     count_launch();
     return cudaGetLastError();
 }
@@ -310,6 +313,9 @@ cudaError_t launch_pool_init_state(Pool *p, cudaStream_t s) {
         return e;
     if ((e = cudaMemsetAsync(p->status, 0, sizeof(uint32_t), s))) return e;
     if ((e = cudaMemsetAsync(p->counters, 0, sizeof(uint32_t) * counter_count(p), s))) return e;
+    // no cached attention plan survives (epoch 0, every record's key invalid)
+    if ((e = cudaMemsetAsync(p->plans, 0xFF, sizeof(uint32_t) * plan_words(p), s))) return e;
+    if ((e = cudaMemsetAsync(p->plans, 0, sizeof(uint32_t), s))) return e;
     // free stack: total-1-i, optionally permuted (Fisher-Yates on the host)
     std::vector<int32_t> stack(p->total_pages);
     for (uint32_t i = 0; i < p->total_pages; i++) stack[i] = (int32_t)(p->total_pages - 1 - i);
@@ -360,7 +366,7 @@ static void pool_release(Pool *p) {
     cudaSetDevice(p->device);
     cudaFree(p->pages); cudaFree(p->page_table); cudaFree(p->seq_lens); cudaFree(p->seq_pages);
     cudaFree(p->free_stack); cudaFree(p->free_top); cudaFree(p->page_scores); cudaFree(p->status);
-    cudaFree(p->partials); cudaFree(p->counters); cudaFree(p->tile_mass); cudaFree(p->seg_ml);
+    cudaFree(p->partials); cudaFree(p->counters); cudaFree(p->plans); cudaFree(p->tile_mass); cudaFree(p->seg_ml);
     cudaFree(p->evict_dead); cudaFree(p->evict_count); cudaFree(p->ident);
     cudaFree(p->stage_q); cudaFree(p->stage_k); cudaFree(p->stage_v); cudaFree(p->stage_o);
     for (uint32_t i = 0; i < p->layer_events; i++) {
@@ -437,7 +443,8 @@ QWN_CUDA_ABI_API int qwn_kv_pool_create(const QwnKvPoolOptions *o, QwnKvPoolHand
     const size_t mass_bytes = (size_t)p->max_units * kMaxGroup * sizeof(float2);
     const size_t segml_bytes = (size_t)p->max_segments * kMaxGroup * sizeof(float2);
     const size_t table_elems = (size_t)o->max_seqs * o->max_pages_per_seq;
-    p->scratch_bytes = part_bytes + mass_bytes + segml_bytes + p->max_segments * sizeof(uint32_t) + table_elems;
+    p->scratch_bytes = part_bytes + mass_bytes + segml_bytes + counter_count(p) * sizeof(uint32_t) +
+                       plan_words(p) * sizeof(uint32_t) + table_elems;
 
     size_t free_b = 0, total_b = 0;
     cudaMemGetInfo(&free_b, &total_b);
@@ -459,6 +466,7 @@ QWN_CUDA_ABI_API int qwn_kv_pool_create(const QwnKvPoolOptions *o, QwnKvPoolHand
               cudaMalloc(&p->status, sizeof(uint32_t)) == cudaSuccess &&
               cudaMalloc(&p->partials, part_bytes) == cudaSuccess &&
               cudaMalloc(&p->counters, sizeof(uint32_t) * counter_count(p)) == cudaSuccess &&
+              cudaMalloc(&p->plans, sizeof(uint32_t) * plan_words(p)) == cudaSuccess &&
               cudaMalloc(&p->tile_mass, mass_bytes) == cudaSuccess &&
               cudaMalloc(&p->seg_ml, segml_bytes) == cudaSuccess &&
               cudaMalloc(&p->evict_dead, table_elems) == cudaSuccess &&

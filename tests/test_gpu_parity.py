@@ -100,6 +100,48 @@ def test_single_long_sequence_two_level_merge(cuda, codec):
         tw.close()
 
 
+@pytest.mark.parametrize("codec", [2, 4])
+@pytest.mark.parametrize("heads", [(32, 8), (12, 2)])
+def test_identity_batch_cached_plans(cuda, codec, heads):
+    """Calls without a sequence-id array cache the launch setup across the
+    layers of a step; every step's append (and a pool reset) invalidates it."""
+    H, HK = heads
+    tw = Twin(cuda, codec, layers=3, kv_heads=HK, page_tokens=16, total_pages=120, max_seqs=4,
+              max_pages=40, query_heads=H, perm_seed=7, seed=15)
+    try:
+        tw.prefill([0, 1, 2, 3], [37, 300, 1, 129])
+        for _ in range(3):
+            g, o, _ = tw.step([0, 1, 2, 3], identity=True)
+            assert_close(g, o, f"codec {codec} identity batch")
+        tw.assert_state_equal()
+        tw.assert_pages_equal()
+    finally:
+        tw.close()
+
+
+def test_identity_batch_plans_after_eviction(cuda):
+    """Eviction and compaction change lengths and tables between steps; the
+    cached launch setup must not survive it."""
+    torch = cuda
+    tw = Twin(cuda, 2, layers=2, kv_heads=8, page_tokens=16, total_pages=400, max_seqs=8, max_pages=64,
+              query_heads=32, perm_seed=5, seed=8)
+    seqs = list(range(8))
+    try:
+        tw.prefill(seqs, [40, 100, 600, 33, 700, 129, 16, 500])
+        rng = np.random.default_rng(9)
+        for step in range(4):
+            g, o, masses = tw.step(seqs, page_mass=True, identity=True)
+            assert_close(g, o, "churn outputs, identity batch")
+            mass = masses[-1]
+            flags = (rng.random(8) < 0.5).astype(np.uint8)
+            tw.gpu.evict(8, torch.tensor(mass, device="cuda"), torch.tensor(flags, device="cuda"), 96)
+            tw.ora.evict(seqs, mass, flags, 96)
+            assert tw.gpu.check() == 0
+            tw.assert_state_equal()
+    finally:
+        tw.close()
+
+
 def test_outlier_channels_q4(cuda, oracle_mod):
     """Config-3 style K with 1% outlier channels x8, 4-bit groups of 32."""
     tw = Twin(cuda, 4, layers=2, kv_heads=8, page_tokens=16, total_pages=120, max_seqs=3, max_pages=40,
