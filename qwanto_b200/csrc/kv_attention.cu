@@ -34,7 +34,7 @@ namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
 // a warp range holds at least this many units (small batches use fewer warps)
-constexpr uint64_t kMinUnitsPerWarp = 8;
+constexpr uint64_t kMinUnitsPerWarp = 2;
 // the even split counts each segment as its tiles plus this many virtual
 // units at its start: a warp that starts a new segment (query slicing, a
 // partial written) gets correspondingly fewer tiles; when the launch stores
