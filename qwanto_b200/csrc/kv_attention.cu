@@ -448,15 +448,18 @@ struct LowBitT {
     static constexpr int kBytes = kTQ ? 2048 : 2560, kStages = HG == 1 ? (kTQ ? 8 : 6) : (kTQ ? 12 : 9);
     struct Frag {
         uint32_t b[HG][2][kC][2];  // [head group][n-block][class][reg]
-        float s2l[HG];             // unit slice scale x log2(e) x softmax scale
-        float qs[HG][kG];          // query sum per group, same factor
+        float s2l[HG][2];          // unit slice scale x log2(e) x softmax scale x code scale
+                                   // (1/15; TurboQuant odd classes [1]: 1/7)
+        float qs[HG][kG];          // query sum per group x log2(e) x softmax scale
     };
     struct State {
         float o[HG][8][4];
         float z[HG][kG];  // sum_t p_t * min (this lane's tokens)
         float m[HG], l[HG];
-        float nu[kC], inv_nu[kC];
+        float nu[kC], inv_nu[kC], nu_lim[kC];  // normaliser of each class's raw ranges
     };
+    // the code scale of class c: range/15 (4-bit codes), range/7 (3-bit odd TurboQuant codes)
+    __device__ static constexpr float code_scale(int c) { return (kTQ && (c & 1)) ? 1.0f / 7.0f : 1.0f / 15.0f; }
     // dim of (class c, index m)
     __device__ static int dim_of(int c, int m) { return kTQ ? 64 * (c >> 1) + 2 * m + (c & 1) : 32 * c + m; }
     __device__ static int group_of_class(int c) { return kTQ ? (c >> 1) : c; }
@@ -554,7 +557,9 @@ struct LowBitT {
             // C side: this lane's head is 4hg + tig, held by the lanes gid = 2tig
             const float hs0 = __shfl_sync(0xffffffffu, s0, 8 * tig);
             const int hbad = __shfl_sync(0xffffffffu, bad, 8 * tig);
-            f.s2l[hg] = hbad ? __int_as_float(0x7fffffff) : hs0 * (1.0f / 16384.0f) * A.scale_log2;
+            const float s2 = hbad ? __int_as_float(0x7fffffff) : hs0 * (1.0f / 16384.0f) * A.scale_log2;
+            f.s2l[hg][0] = s2 * code_scale(0);
+            f.s2l[hg][1] = s2 * code_scale(1);
 #pragma unroll
             for (int g = 0; g < kG; g++) f.qs[hg][g] = __shfl_sync(0xffffffffu, qs[g], 8 * tig) * A.scale_log2;
         }
@@ -568,7 +573,7 @@ struct LowBitT {
             for (int mb = 0; mb < 8; mb++) st.o[hg][mb][0] = st.o[hg][mb][1] = st.o[hg][mb][2] = st.o[hg][mb][3] = 0.f;
         }
 #pragma unroll
-        for (int c = 0; c < kC; c++) { st.nu[c] = 0.f; st.inv_nu[c] = 0.f; }
+        for (int c = 0; c < kC; c++) { st.nu[c] = 0.f; st.inv_nu[c] = 0.f; st.nu_lim[c] = 0.f; }
     }
 
     // the three group-1 TurboQuant odd-code bits: bit 0 in bit 3 of each nibble
@@ -629,10 +634,10 @@ struct LowBitT {
                     const float2 rm = h2x2f(pw[g][tk]);
                     km[tk][g] = rm.y;
                     if constexpr (kTQ) {
-                        kp[tk][2 * g] = rm.x * (1.0f / 15.0f);
-                        kp[tk][2 * g + 1] = rm.x * (1.0f / 7.0f);
+                        kp[tk][2 * g] = rm.x;
+                        kp[tk][2 * g + 1] = rm.x;
                     } else {
-                        kp[tk][g] = rm.x * (1.0f / 15.0f);
+                        kp[tk][g] = rm.x;
                     }
                 }
         }
@@ -643,7 +648,7 @@ struct LowBitT {
         float s[HG][2];
 #pragma unroll
         for (int hg = 0; hg < HG; hg++) {
-            float raw[2] = {0.f, 0.f};
+            float raw[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [token][odd TurboQuant class]
 #pragma unroll
             for (int c = 0; c < kC; c++) {
                 const uint32_t a0 = kw[0][c] & 0x0F0F0F0Fu, a1 = kw[1][c] & 0x0F0F0F0Fu;
@@ -655,12 +660,14 @@ struct LowBitT {
                 for (int tk = 0; tk < 2; tk++) {
                     // columns 2tig (slice 0 | slice 2) and 2tig+1 (slice 1)
                     const int I = (acc[0][2 * tk] * 128 + acc[0][2 * tk + 1]) * 128 + acc[1][2 * tk];
-                    raw[tk] = fmaf(__int2float_rn(I), kp[tk][c], raw[tk]);
+                    const int o = kTQ ? (c & 1) : 0;
+                    raw[tk][o] = fmaf(__int2float_rn(I), kp[tk][c], raw[tk][o]);
                 }
             }
 #pragma unroll
             for (int tk = 0; tk < 2; tk++) {
-                float sc = raw[tk] * f.s2l[hg];
+                float sc = raw[tk][0] * f.s2l[hg][0];
+                if constexpr (kTQ) sc = fmaf(raw[tk][1], f.s2l[hg][1], sc);
 #pragma unroll
                 for (int g = 0; g < kG; g++) sc = fmaf(km[tk][g], f.qs[hg][g], sc);
                 s[hg][tk] = (tk ? ok1 : ok0) ? sc : -INFINITY;
@@ -706,18 +713,24 @@ struct LowBitT {
                 pw[0][0] = p0.x; pw[0][1] = p0.y; pw[1][0] = p0.z; pw[1][1] = p0.w;
                 pw[kG - 2][0] = p1.x; pw[kG - 2][1] = p1.y; pw[kG - 1][0] = p1.z; pw[kG - 1][1] = p1.w;
             }
+            if (!full) {  // masked tokens contribute nothing (their slots may hold anything)
+#pragma unroll
+                for (int g = 0; g < kG; g++) {
+                    if (!ok0) pw[g][0] = 0u;
+                    if (!ok1) pw[g][1] = 0u;
+                }
+            }
 #pragma unroll
             for (int g = 0; g < kG; g++)
 #pragma unroll
                 for (int tk = 0; tk < 2; tk++) {
-                    const bool ok = tk ? ok1 : ok0;
                     const float2 rm = h2x2f(pw[g][tk]);
-                    vm[tk][g] = ok ? rm.y : 0.f;
+                    vm[tk][g] = rm.y;
                     if constexpr (kTQ) {
-                        vp[tk][2 * g] = ok ? rm.x * (1.0f / 15.0f) : 0.f;
-                        vp[tk][2 * g + 1] = ok ? rm.x * (1.0f / 7.0f) : 0.f;
+                        vp[tk][2 * g] = rm.x;
+                        vp[tk][2 * g + 1] = rm.x;
                     } else {
-                        vp[tk][g] = ok ? rm.x * (1.0f / 15.0f) : 0.f;
+                        vp[tk][g] = rm.x;
                     }
                 }
         }
@@ -732,7 +745,7 @@ struct LowBitT {
 #pragma unroll
             for (int c = 0; c < kC; c++) {
                 lmax[c] = fmaxf(vp[0][c], vp[1][c]);
-                need |= st.nu[c] == 0.f || lmax[c] > st.nu[c] * kNuHeadroom;
+                need |= lmax[c] > st.nu_lim[c];
             }
             if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
@@ -755,6 +768,7 @@ struct LowBitT {
                         st.nu[c] = nn;
                     }
                     st.inv_nu[c] = 1.0f / st.nu[c];
+                    st.nu_lim[c] = st.nu[c] * kNuHeadroom;
                 }
             }
         }
@@ -841,8 +855,9 @@ struct LowBitT {
             for (int mb = 0; mb < 8; mb++) {
                 const int c = mb >> 1, g = group_of_class(c);
                 const int m0 = 16 * (mb & 1) + gid;
-                row[dim_of(c, m0)] = ((st.o[hg][mb][0] + st.o[hg][mb][1]) * st.nu[c] + zt[g]) * inv;
-                row[dim_of(c, m0 + 8)] = ((st.o[hg][mb][2] + st.o[hg][mb][3]) * st.nu[c] + zt[g]) * inv;
+                const float sc = st.nu[c] * code_scale(c);
+                row[dim_of(c, m0)] = ((st.o[hg][mb][0] + st.o[hg][mb][1]) * sc + zt[g]) * inv;
+                row[dim_of(c, m0 + 8)] = ((st.o[hg][mb][2] + st.o[hg][mb][3]) * sc + zt[g]) * inv;
             }
             if (gid == 0) {
                 if (m_out) { m_out[h] = st.m[hg]; l_out[h] = lt; }
