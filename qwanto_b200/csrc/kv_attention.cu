@@ -104,6 +104,7 @@ struct Int8T {
     static constexpr int kX = kB64 ? 2 : 1;  // scale groups along head_dim
     // two head groups keep twice the state: 2 CTAs per SM, deeper pipelines
     static constexpr int kBytes = kB64 ? 4352 : 4160, kStages = HG == 1 ? 4 : 6;
+    static constexpr int kTilesPerStep = 1;
     struct Frag {
         uint32_t b[HG][2][4][2];   // IMMA B: [head group][n-block][k-block][reg]
         uint32_t magic[HG][kX][4]; // per (scale group, slice) of this lane's head
@@ -446,6 +447,9 @@ struct LowBitT {
     static constexpr int kC = 4;               // classes of 32 dims
     static constexpr int kG = kTQ ? 2 : 4;     // groups (min values)
     static constexpr int kBytes = kTQ ? 2048 : 2560, kStages = HG == 1 ? (kTQ ? 8 : 6) : (kTQ ? 12 : 9);
+    // tiles per loop iteration: pairs for the 4-bit single-head-group kernel
+    // (long contexts gain ~3%; TurboQuant's larger step does not)
+    static constexpr int kTilesPerStep = (HG == 1 && !kTQ) ? 2 : 1;
     struct Frag {
         uint32_t b[HG][2][kC][2];  // [head group][n-block][class][reg]
         float s2l[HG][2];          // unit slice scale x log2(e) x softmax scale x code scale
@@ -586,13 +590,10 @@ struct LowBitT {
         return ((odd >> 3) & 0x11111111u) | (s << 1);
     }
 
-    __device__ static void step(const uint8_t *tile, const Frag &f, State &st, int t_lo, int t_hi,
-                                float (&psum)[HG]) {
+    // K code words (u8-expanded per class), class ranges and group minima of
+    // tokens gid (tk 0) and gid+8 (tk 1) of one tile
+    __device__ static void kload(const uint8_t *tile, uint32_t (&kw)[2][kC], float (&kp)[2][kC], float (&km)[2][kG]) {
         const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-        // ---- K code words of tokens gid (w0) and gid+8 (w1), per class
-        uint32_t kw[2][kC];
-        float kp[2][kC];  // class scale (range/15 or range/7) per token
-        float km[2][kG];  // group minimum per token
         const uint8_t *kpar;
         if constexpr (kTQ) {
 #pragma unroll
@@ -616,68 +617,196 @@ struct LowBitT {
             kpar = tile + 2048;
         }
         // params of tokens gid, gid+8: (range16, min16) words [class or group][token]
-        {
-            uint32_t pw[kG][2];
-            if constexpr (kTQ) {
-                const uint4 p = *reinterpret_cast<const uint4 *>(kpar + 16 * gid);
-                pw[0][0] = p.x; pw[0][1] = p.y; pw[kG - 1][0] = p.z; pw[kG - 1][1] = p.w;
-            } else {
-                const uint4 p0 = *reinterpret_cast<const uint4 *>(kpar + 32 * gid);
-                const uint4 p1 = *reinterpret_cast<const uint4 *>(kpar + 32 * gid + 16);
-                pw[0][0] = p0.x; pw[0][1] = p0.y; pw[1][0] = p0.z; pw[1][1] = p0.w;
-                pw[kG - 2][0] = p1.x; pw[kG - 2][1] = p1.y; pw[kG - 1][0] = p1.z; pw[kG - 1][1] = p1.w;
-            }
-#pragma unroll
-            for (int g = 0; g < kG; g++)
-#pragma unroll
-                for (int tk = 0; tk < 2; tk++) {
-                    const float2 rm = h2x2f(pw[g][tk]);
-                    km[tk][g] = rm.y;
-                    if constexpr (kTQ) {
-                        kp[tk][2 * g] = rm.x;
-                        kp[tk][2 * g + 1] = rm.x;
-                    } else {
-                        kp[tk][g] = rm.x;
-                    }
-                }
+        uint32_t pw[kG][2];
+        if constexpr (kTQ) {
+            const uint4 p = *reinterpret_cast<const uint4 *>(kpar + 16 * gid);
+            pw[0][0] = p.x; pw[0][1] = p.y; pw[kG - 1][0] = p.z; pw[kG - 1][1] = p.w;
+        } else {
+            const uint4 p0 = *reinterpret_cast<const uint4 *>(kpar + 32 * gid);
+            const uint4 p1 = *reinterpret_cast<const uint4 *>(kpar + 32 * gid + 16);
+            pw[0][0] = p0.x; pw[0][1] = p0.y; pw[1][0] = p0.z; pw[1][1] = p0.w;
+            pw[kG - 2][0] = p1.x; pw[kG - 2][1] = p1.y; pw[kG - 1][0] = p1.z; pw[kG - 1][1] = p1.w;
         }
-        const bool full = t_lo == 0 && t_hi == 16;  // warp-uniform
-        const bool ok0 = full || (gid >= t_lo && gid < t_hi);
-        const bool ok1 = full || (gid + 8 >= t_lo && gid + 8 < t_hi);
-        // ---- scores
-        float s[HG][2];
 #pragma unroll
-        for (int hg = 0; hg < HG; hg++) {
-            float raw[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [token][odd TurboQuant class]
-#pragma unroll
-            for (int c = 0; c < kC; c++) {
-                const uint32_t a0 = kw[0][c] & 0x0F0F0F0Fu, a1 = kw[1][c] & 0x0F0F0F0Fu;
-                const uint32_t a2 = (kw[0][c] >> 4) & 0x0F0F0F0Fu, a3 = (kw[1][c] >> 4) & 0x0F0F0F0Fu;
-                int acc[2][4];
-#pragma unroll
-                for (int nb = 0; nb < 2; nb++) imma16832_z(acc[nb], a0, a1, a2, a3, f.b[hg][nb][c][0], f.b[hg][nb][c][1]);
-#pragma unroll
-                for (int tk = 0; tk < 2; tk++) {
-                    // columns 2tig (slice 0 | slice 2) and 2tig+1 (slice 1)
-                    const int I = (acc[0][2 * tk] * 128 + acc[0][2 * tk + 1]) * 128 + acc[1][2 * tk];
-                    const int o = kTQ ? (c & 1) : 0;
-                    raw[tk][o] = fmaf(__int2float_rn(I), kp[tk][c], raw[tk][o]);
-                }
-            }
+        for (int g = 0; g < kG; g++)
 #pragma unroll
             for (int tk = 0; tk < 2; tk++) {
-                float sc = raw[tk][0] * f.s2l[hg][0];
-                if constexpr (kTQ) sc = fmaf(raw[tk][1], f.s2l[hg][1], sc);
-#pragma unroll
-                for (int g = 0; g < kG; g++) sc = fmaf(km[tk][g], f.qs[hg][g], sc);
-                s[hg][tk] = (tk ? ok1 : ok0) ? sc : -INFINITY;
+                const float2 rm = h2x2f(pw[g][tk]);
+                km[tk][g] = rm.y;
+                if constexpr (kTQ) {
+                    kp[tk][2 * g] = rm.x;
+                    kp[tk][2 * g + 1] = rm.x;
+                } else {
+                    kp[tk][g] = rm.x;
+                }
             }
+    }
+
+    // base-2 scores of NT tiles, the tiles' integer products interleaved
+    template <int NT>
+    __device__ static void scores(const uint8_t *const (&tiles)[NT], const Frag &f, const int (&t_lo)[NT],
+                                  const int (&t_hi)[NT], float (&s)[NT][HG][2], bool (&ok0)[NT], bool (&ok1)[NT],
+                                  bool (&full)[NT]) {
+        const int gid = (threadIdx.x & 31) >> 2;
+        uint32_t kw[NT][2][kC];
+        float kp[NT][2][kC], km[NT][2][kG];
+#pragma unroll
+        for (int u = 0; u < NT; u++) {
+            kload(tiles[u], kw[u], kp[u], km[u]);
+            full[u] = t_lo[u] == 0 && t_hi[u] == 16;  // warp-uniform
+            ok0[u] = full[u] || (gid >= t_lo[u] && gid < t_hi[u]);
+            ok1[u] = full[u] || (gid + 8 >= t_lo[u] && gid + 8 < t_hi[u]);
         }
-        // ---- online softmax per head
-        float p[HG][2];
 #pragma unroll
         for (int hg = 0; hg < HG; hg++) {
-            float tmax = fmaxf(s[hg][0], s[hg][1]);
+            float raw[NT][2][2];  // [tile][token][odd TurboQuant class]
+#pragma unroll
+            for (int u = 0; u < NT; u++) raw[u][0][0] = raw[u][0][1] = raw[u][1][0] = raw[u][1][1] = 0.f;
+#pragma unroll
+            for (int c = 0; c < kC; c++) {
+                int acc[NT][2][4];
+#pragma unroll
+                for (int u = 0; u < NT; u++) {
+                    const uint32_t a0 = kw[u][0][c] & 0x0F0F0F0Fu, a1 = kw[u][1][c] & 0x0F0F0F0Fu;
+                    const uint32_t a2 = (kw[u][0][c] >> 4) & 0x0F0F0F0Fu, a3 = (kw[u][1][c] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                    for (int nb = 0; nb < 2; nb++)
+                        imma16832_z(acc[u][nb], a0, a1, a2, a3, f.b[hg][nb][c][0], f.b[hg][nb][c][1]);
+                }
+#pragma unroll
+                for (int u = 0; u < NT; u++)
+#pragma unroll
+                    for (int tk = 0; tk < 2; tk++) {
+                        // columns 2tig (slice 0 | slice 2) and 2tig+1 (slice 1)
+                        const int I = (acc[u][0][2 * tk] * 128 + acc[u][0][2 * tk + 1]) * 128 + acc[u][1][2 * tk];
+                        const int o = kTQ ? (c & 1) : 0;
+                        raw[u][tk][o] = fmaf(__int2float_rn(I), kp[u][tk][c], raw[u][tk][o]);
+                    }
+            }
+#pragma unroll
+            for (int u = 0; u < NT; u++)
+#pragma unroll
+                for (int tk = 0; tk < 2; tk++) {
+                    float sc = raw[u][tk][0] * f.s2l[hg][0];
+                    if constexpr (kTQ) sc = fmaf(raw[u][tk][1], f.s2l[hg][1], sc);
+#pragma unroll
+                    for (int g = 0; g < kG; g++) sc = fmaf(km[u][tk][g], f.qs[hg][g], sc);
+                    s[u][hg][tk] = (tk ? ok1[u] : ok0[u]) ? sc : -INFINITY;
+                }
+        }
+    }
+
+    // V class ranges and group minima of tokens gid, gid+8 (zero for masked tokens)
+    __device__ static void vparams(const uint8_t *tile, bool ok0, bool ok1, bool full, float (&vp)[2][kC],
+                                   float (&vm)[2][kG]) {
+        const int gid = (threadIdx.x & 31) >> 2;
+        const uint8_t *vpar = kTQ ? tile + 1024 + 896 : tile + 2304;
+        uint32_t pw[kG][2];
+        if constexpr (kTQ) {
+            const uint4 q4 = *reinterpret_cast<const uint4 *>(vpar + 16 * gid);
+            pw[0][0] = q4.x; pw[0][1] = q4.y; pw[kG - 1][0] = q4.z; pw[kG - 1][1] = q4.w;
+        } else {
+            const uint4 p0 = *reinterpret_cast<const uint4 *>(vpar + 32 * gid);
+            const uint4 p1 = *reinterpret_cast<const uint4 *>(vpar + 32 * gid + 16);
+            pw[0][0] = p0.x; pw[0][1] = p0.y; pw[1][0] = p0.z; pw[1][1] = p0.w;
+            pw[kG - 2][0] = p1.x; pw[kG - 2][1] = p1.y; pw[kG - 1][0] = p1.z; pw[kG - 1][1] = p1.w;
+        }
+        if (!full) {  // masked tokens contribute nothing (their slots may hold anything)
+#pragma unroll
+            for (int g = 0; g < kG; g++) {
+                if (!ok0) pw[g][0] = 0u;
+                if (!ok1) pw[g][1] = 0u;
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < kG; g++)
+#pragma unroll
+            for (int tk = 0; tk < 2; tk++) {
+                const float2 rm = h2x2f(pw[g][tk]);
+                vm[tk][g] = rm.y;
+                if constexpr (kTQ) {
+                    vp[tk][2 * g] = rm.x;
+                    vp[tk][2 * g + 1] = rm.x;
+                } else {
+                    vp[tk][g] = rm.x;
+                }
+            }
+    }
+
+    // V code words of one tile per m-block
+    __device__ static void vload(const uint8_t *tile, uint32_t (&vw)[8]) {
+        const int lane = threadIdx.x & 31;
+        if constexpr (kTQ) {
+            const uint8_t *vh = tile + 1024;
+            const uint4 ev = *reinterpret_cast<const uint4 *>(vh + 16 * lane);
+            const uint2 od = *reinterpret_cast<const uint2 *>(vh + 512 + 8 * lane);
+            const uint32_t pl = *reinterpret_cast<const uint32_t *>(vh + 768 + 4 * lane);
+            vw[0] = ev.x; vw[1] = ev.y;                    // class 0 (group 0, even)
+            vw[2] = od.x & 0x77777777u; vw[3] = od.y & 0x77777777u;  // class 1 (group 0, odd)
+            vw[4] = ev.z; vw[5] = ev.w;                    // class 2 (group 1, even)
+            vw[6] = tq_hi_codes(od.x, pl); vw[7] = tq_hi_codes(od.y, pl >> 16);  // class 3
+        } else {
+            const uint8_t *vt = tile + 1024 + lane * 32;
+            const int sw = (lane >> 2) & 1;
+            const uint4 c0 = *reinterpret_cast<const uint4 *>(vt + ((0 ^ sw) << 4));
+            const uint4 c1 = *reinterpret_cast<const uint4 *>(vt + ((1 ^ sw) << 4));
+            vw[0] = c0.x; vw[1] = c0.y; vw[2] = c0.z; vw[3] = c0.w;
+            vw[4] = c1.x; vw[5] = c1.y; vw[6] = c1.z; vw[7] = c1.w;
+        }
+    }
+
+    // P' = p * range / nu per class as f16 hi+lo, transposed into the PV B
+    // operand; V codes per m-block -> exact f16 A fragments; P x V for NT
+    // tiles, interleaved
+    template <int NT>
+    __device__ static void pv(const uint8_t *const (&tiles)[NT], State &st, const float (&p)[NT][HG][2],
+                              const float (&vp)[NT][2][kC]) {
+        uint32_t bp[NT][HG][kC][2];
+#pragma unroll
+        for (int u = 0; u < NT; u++)
+#pragma unroll
+            for (int hg = 0; hg < HG; hg++)
+#pragma unroll
+                for (int c = 0; c < kC; c++) {
+                    const float pt0 = p[u][hg][0] * vp[u][0][c] * st.inv_nu[c];
+                    const float pt1 = p[u][hg][1] * vp[u][1][c] * st.inv_nu[c];
+                    const __half2 hi = __floats2half2_rn(pt0, pt1);
+                    const float2 hf = __half22float2(hi);
+                    const __half2 lo = __floats2half2_rn(pt0 - hf.x, pt1 - hf.y);
+                    const uint32_t hu = *reinterpret_cast<const uint32_t *>(&hi);
+                    const uint32_t lu = *reinterpret_cast<const uint32_t *>(&lo);
+                    bp[u][hg][c][0] = movmatrix_trans(prmt(hu, lu, 0x5410u));
+                    bp[u][hg][c][1] = movmatrix_trans(prmt(hu, lu, 0x7632u));
+                }
+        uint32_t vw[NT][8];
+#pragma unroll
+        for (int u = 0; u < NT; u++) vload(tiles[u], vw[u]);
+#pragma unroll
+        for (int mb = 0; mb < 8; mb++)
+#pragma unroll
+            for (int u = 0; u < NT; u++) {
+                uint32_t a[4];
+                nib8_to_h2x4(vw[u][mb], a);
+#pragma unroll
+                for (int hg = 0; hg < HG; hg++) mma16816(st.o[hg][mb], a, bp[u][hg][mb >> 1][0], bp[u][hg][mb >> 1][1]);
+            }
+    }
+
+    // NT consecutive tiles of one segment: their scores, one online-softmax
+    // update and one normaliser check for all of them, then P x V per tile
+    template <int NT>
+    __device__ static void stepn(const uint8_t *const (&tiles)[NT], const Frag &f, State &st,
+                                 const int (&t_lo)[NT], const int (&t_hi)[NT], float (&psum)[NT][HG]) {
+        float s[NT][HG][2];
+        bool ok0[NT], ok1[NT], full[NT];
+        scores<NT>(tiles, f, t_lo, t_hi, s, ok0, ok1, full);
+        // ---- online softmax per head
+        float p[NT][HG][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float tmax = fmaxf(s[0][hg][0], s[0][hg][1]);
+#pragma unroll
+            for (int u = 1; u < NT; u++) tmax = fmaxf(tmax, fmaxf(s[u][hg][0], s[u][hg][1]));
             tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
             tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
             tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
@@ -694,57 +823,34 @@ struct LowBitT {
                 }
                 st.m[hg] = m_new;
             }
-            p[hg][0] = ex2(s[hg][0] - st.m[hg]);
-            p[hg][1] = ex2(s[hg][1] - st.m[hg]);
-            st.l[hg] += p[hg][0] + p[hg][1];
-            psum[hg] = p[hg][0] + p[hg][1];
-        }
-        // ---- V params: class scales and group minima of tokens gid, gid+8
-        float vp[2][kC], vm[2][kG];
-        {
-            const uint8_t *vpar = kTQ ? tile + 1024 + 896 : tile + 2304;
-            uint32_t pw[kG][2];
-            if constexpr (kTQ) {
-                const uint4 q4 = *reinterpret_cast<const uint4 *>(vpar + 16 * gid);
-                pw[0][0] = q4.x; pw[0][1] = q4.y; pw[kG - 1][0] = q4.z; pw[kG - 1][1] = q4.w;
-            } else {
-                const uint4 p0 = *reinterpret_cast<const uint4 *>(vpar + 32 * gid);
-                const uint4 p1 = *reinterpret_cast<const uint4 *>(vpar + 32 * gid + 16);
-                pw[0][0] = p0.x; pw[0][1] = p0.y; pw[1][0] = p0.z; pw[1][1] = p0.w;
-                pw[kG - 2][0] = p1.x; pw[kG - 2][1] = p1.y; pw[kG - 1][0] = p1.z; pw[kG - 1][1] = p1.w;
+#pragma unroll
+            for (int u = 0; u < NT; u++) {
+                p[u][hg][0] = ex2(s[u][hg][0] - st.m[hg]);
+                p[u][hg][1] = ex2(s[u][hg][1] - st.m[hg]);
+                psum[u][hg] = p[u][hg][0] + p[u][hg][1];
+                st.l[hg] += psum[u][hg];
             }
-            if (!full) {  // masked tokens contribute nothing (their slots may hold anything)
-#pragma unroll
-                for (int g = 0; g < kG; g++) {
-                    if (!ok0) pw[g][0] = 0u;
-                    if (!ok1) pw[g][1] = 0u;
-                }
-            }
-#pragma unroll
-            for (int g = 0; g < kG; g++)
-#pragma unroll
-                for (int tk = 0; tk < 2; tk++) {
-                    const float2 rm = h2x2f(pw[g][tk]);
-                    vm[tk][g] = rm.y;
-                    if constexpr (kTQ) {
-                        vp[tk][2 * g] = rm.x;
-                        vp[tk][2 * g + 1] = rm.x;
-                    } else {
-                        vp[tk][g] = rm.x;
-                    }
-                }
         }
+        // ---- V params; z = sum_t p_t * min_t
+        float vp[NT][2][kC], vm[NT][2][kG];
 #pragma unroll
-        for (int hg = 0; hg < HG; hg++)
+        for (int u = 0; u < NT; u++) vparams(tiles[u], ok0[u], ok1[u], full[u], vp[u], vm[u]);
 #pragma unroll
-            for (int g = 0; g < kG; g++) st.z[hg][g] = fmaf(p[hg][0], vm[0][g], fmaf(p[hg][1], vm[1][g], st.z[hg][g]));
+        for (int u = 0; u < NT; u++)
+#pragma unroll
+            for (int hg = 0; hg < HG; hg++)
+#pragma unroll
+                for (int g = 0; g < kG; g++)
+                    st.z[hg][g] = fmaf(p[u][hg][0], vm[u][0][g], fmaf(p[u][hg][1], vm[u][1][g], st.z[hg][g]));
         // ---- normalisers per class (shared by all heads)
         {
             float lmax[kC];
             bool need = false;
 #pragma unroll
             for (int c = 0; c < kC; c++) {
-                lmax[c] = fmaxf(vp[0][c], vp[1][c]);
+                lmax[c] = fmaxf(vp[0][0][c], vp[0][1][c]);
+#pragma unroll
+                for (int u = 1; u < NT; u++) lmax[c] = fmaxf(lmax[c], fmaxf(vp[u][0][c], vp[u][1][c]));
                 need |= lmax[c] > st.nu_lim[c];
             }
             if (__any_sync(0xffffffffu, need)) {
@@ -772,48 +878,17 @@ struct LowBitT {
                 }
             }
         }
-        // ---- P' per class as f16 hi+lo, transposed into the PV B operand
-        uint32_t bp[HG][kC][2];
+        pv<NT>(tiles, st, p, vp);
+    }
+
+    __device__ static void step(const uint8_t *tile, const Frag &f, State &st, int t_lo, int t_hi,
+                                float (&psum)[HG]) {
+        const uint8_t *const tiles[1] = {tile};
+        const int lo[1] = {t_lo}, hi[1] = {t_hi};
+        float ps[1][HG];
+        stepn<1>(tiles, f, st, lo, hi, ps);
 #pragma unroll
-        for (int hg = 0; hg < HG; hg++)
-#pragma unroll
-            for (int c = 0; c < kC; c++) {
-                const float pt0 = p[hg][0] * vp[0][c] * st.inv_nu[c];
-                const float pt1 = p[hg][1] * vp[1][c] * st.inv_nu[c];
-                const __half2 hi = __floats2half2_rn(pt0, pt1);
-                const float2 hf = __half22float2(hi);
-                const __half2 lo = __floats2half2_rn(pt0 - hf.x, pt1 - hf.y);
-                const uint32_t hu = *reinterpret_cast<const uint32_t *>(&hi);
-                const uint32_t lu = *reinterpret_cast<const uint32_t *>(&lo);
-                bp[hg][c][0] = movmatrix_trans(prmt(hu, lu, 0x5410u));
-                bp[hg][c][1] = movmatrix_trans(prmt(hu, lu, 0x7632u));
-            }
-        // ---- V code words per m-block -> exact f16 A fragments; P x V
-        uint32_t vw[8];
-        if constexpr (kTQ) {
-            const uint8_t *vh = tile + 1024;
-            const uint4 ev = *reinterpret_cast<const uint4 *>(vh + 16 * lane);
-            const uint2 od = *reinterpret_cast<const uint2 *>(vh + 512 + 8 * lane);
-            const uint32_t pl = *reinterpret_cast<const uint32_t *>(vh + 768 + 4 * lane);
-            vw[0] = ev.x; vw[1] = ev.y;                    // class 0 (group 0, even)
-            vw[2] = od.x & 0x77777777u; vw[3] = od.y & 0x77777777u;  // class 1 (group 0, odd)
-            vw[4] = ev.z; vw[5] = ev.w;                    // class 2 (group 1, even)
-            vw[6] = tq_hi_codes(od.x, pl); vw[7] = tq_hi_codes(od.y, pl >> 16);  // class 3
-        } else {
-            const uint8_t *vt = tile + 1024 + lane * 32;
-            const int sw = (lane >> 2) & 1;
-            const uint4 c0 = *reinterpret_cast<const uint4 *>(vt + ((0 ^ sw) << 4));
-            const uint4 c1 = *reinterpret_cast<const uint4 *>(vt + ((1 ^ sw) << 4));
-            vw[0] = c0.x; vw[1] = c0.y; vw[2] = c0.z; vw[3] = c0.w;
-            vw[4] = c1.x; vw[5] = c1.y; vw[6] = c1.z; vw[7] = c1.w;
-        }
-#pragma unroll
-        for (int mb = 0; mb < 8; mb++) {
-            uint32_t a[4];
-            nib8_to_h2x4(vw[mb], a);
-#pragma unroll
-            for (int hg = 0; hg < HG; hg++) mma16816(st.o[hg][mb], a, bp[hg][mb >> 1][0], bp[hg][mb >> 1][1]);
-        }
+        for (int hg = 0; hg < HG; hg++) psum[hg] = ps[0][hg];
     }
 
     __device__ static void mass(const AttnArgs &A, uint64_t unit, const State &st, float (&psum)[HG]) {
@@ -1417,21 +1492,28 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     bool counted0 = false;
     uint64_t pend_u0 = 0, pend_u1 = 0;
 
-    for (uint32_t k = 0; k < n; ++k) {
+    for (uint32_t k = 0; k < n;) {
         if (cons.tile == 0 || k == 0) OPS::begin(frag, state, A, cons.i * HK + cons.h);
-        if (pend_n && !counted0 && k == pend_k0 + 4u) {
+        // tiles this iteration: two consecutive tiles of one segment where the
+        // codec steps pairs, else one
+        const uint32_t nt = (OPS::kTilesPerStep == 2 && cons.tile + 1 < cons.geo.ntiles && k + 1 < n) ? 2u : 1u;
+        if (pend_n && !counted0 && k >= pend_k0 + 4u) {
             __syncwarp();
             if (lane == 0) tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, pend_n0, pend_u0, Tv, W, wid), 1u);
             counted0 = true;  // the ticket is read after the loop
         }
-        if (cons.tile + 4u == cons.geo.ntiles) {
+        if (cons.tile + 4u <= cons.geo.ntiles && cons.geo.ntiles < cons.tile + 4u + nt) {
             // the next segment's query rows (s_idx + 1 in batch order) into L1,
             // so that its begin() does not wait for them
             const size_t next = (size_t)(cons.i * HK + cons.h + 1) * A.group;
             if (next < (size_t)A.num_seqs * HK * A.group && (uint32_t)lane * 128u < A.group * kHeadDim * 4u)
                 asm volatile("prefetch.global.L1 [%0];" ::"l"(A.query + next * kHeadDim + lane * 32));
         }
-        if (!mbar_wait_bounded(&bars[st], par)) {
+        uint32_t st1 = st + 1u, par1 = par;
+        if (st1 == (uint32_t)S) { st1 = 0; par1 ^= 1u; }
+        bool landed = mbar_wait_bounded(&bars[st], par);
+        if (landed && nt == 2) landed = mbar_wait_bounded(&bars[st1], par1);
+        if (!landed) {
             if (lane == 0) latch(A.status, QWN_KV_STATUS_WAIT_TIMEOUT);
             // wait (bounded) for the copies still in flight into this warp's stages
             uint32_t s2 = st, p2 = par;
@@ -1442,38 +1524,55 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
             return;
         }
         const int tile_tok0 = (int)(cons.geo.tile0 + cons.tile) * 16;
-        const int t_lo = max(cons.geo.tok_lo - tile_tok0, 0);
-        const int t_hi = min(cons.geo.tok_hi - tile_tok0, 16);
-        float psum[HG];
-        OPS::step(wsm + st * B, frag, state, t_lo, t_hi, psum);
-        if (A.tile_mass) OPS::mass(A, cons.seg_base + cons.tile, state, psum);
-        __syncwarp();
-
-        // refill this stage with unit k + S
-        const uint32_t j = k + (uint32_t)S;
-        if (j < n) {
-            if (j - wbase == 16u && wbase + 32u < n)  // request the next window early
-                fill_window(A, cons, wbase + 32u - k, wbase + 32u, n, win, cw ^ 1);
-            if (j - wbase == 32u) {
-                wbase = j;
-                cw ^= 1;
-                window_ready();
-            }
-            const int32_t seg = win->app[cw][j - wbase];
-            const uint8_t *src = window_src(A, win, cw, j - wbase);
-            if (seg >= 0) fused_append<CODEC>(A.new_k, A.new_v, A.seq_ids, A.seq_lens, A.kv_heads, seg, src);
-            // every shared-memory read of this stage fed a register that was
-            // consumed before the __syncwarp above, so the copy cannot
-            // overtake them
-            if (lane == 0) {
-                mbar_expect_tx(&bars[st], B);
-                bulk_g2s(wsm + st * B, src, B, &bars[st]);
+        if constexpr (OPS::kTilesPerStep == 2) {
+            if (nt == 2) {
+                const uint8_t *const tl[2] = {wsm + st * B, wsm + st1 * B};
+                const int lo[2] = {max(cons.geo.tok_lo - tile_tok0, 0), max(cons.geo.tok_lo - tile_tok0 - 16, 0)};
+                const int hi[2] = {min(cons.geo.tok_hi - tile_tok0, 16), min(cons.geo.tok_hi - tile_tok0 - 16, 16)};
+                float ps[2][HG];
+                OPS::template stepn<2>(tl, frag, state, lo, hi, ps);
+                if (A.tile_mass) {
+                    OPS::mass(A, cons.seg_base + cons.tile, state, ps[0]);
+                    OPS::mass(A, cons.seg_base + cons.tile + 1, state, ps[1]);
+                }
             }
         }
-        if (++st == (uint32_t)S) { st = 0; par ^= 1u; }
+        if (nt == 1) {
+            const int t_lo = max(cons.geo.tok_lo - tile_tok0, 0);
+            const int t_hi = min(cons.geo.tok_hi - tile_tok0, 16);
+            float psum[HG];
+            OPS::step(wsm + st * B, frag, state, t_lo, t_hi, psum);
+            if (A.tile_mass) OPS::mass(A, cons.seg_base + cons.tile, state, psum);
+        }
+        __syncwarp();
+
+        // refill the consumed stages with units k + S (and k + 1 + S)
+        for (uint32_t e = 0; e < nt; e++) {
+            const uint32_t j = k + e + (uint32_t)S;
+            if (j < n) {
+                if (j - wbase == 16u && wbase + 32u < n)  // request the next window early
+                    fill_window(A, cons, wbase + 32u - k, wbase + 32u, n, win, cw ^ 1);  // cons is at unit k
+                if (j - wbase == 32u) {
+                    wbase = j;
+                    cw ^= 1;
+                    window_ready();
+                }
+                const int32_t seg = win->app[cw][j - wbase];
+                const uint8_t *src = window_src(A, win, cw, j - wbase);
+                if (seg >= 0) fused_append<CODEC>(A.new_k, A.new_v, A.seq_ids, A.seq_lens, A.kv_heads, seg, src);
+                // every shared-memory read of this stage fed a register that was
+                // consumed before the __syncwarp above, so the copy cannot
+                // overtake them
+                if (lane == 0) {
+                    mbar_expect_tx(&bars[st], B);
+                    bulk_g2s(wsm + st * B, src, B, &bars[st]);
+                }
+            }
+            if (++st == (uint32_t)S) { st = 0; par ^= 1u; }
+        }
 
         // end of this warp's share of the segment?
-        if (cons.tile + 1 == cons.geo.ntiles || k + 1 == n) {
+        if (cons.tile + nt == cons.geo.ntiles || k + nt == n) {
             const uint32_t s_idx = cons.i * HK + cons.h;
             const uint32_t np = finish_segment<OPS>(A, state, s_idx, cons.vbase, cons.geo.ntiles, Tv, W, wid);
             if (np) {
@@ -1483,9 +1582,11 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
             }
         }
         // next unit
-        if (k + 1 < n) {
-            if (++cons.tile == cons.geo.ntiles) walk_next_segment(A, cons);
+        if (k + nt < n) {
+            cons.tile += nt;
+            if (cons.tile == cons.geo.ntiles) walk_next_segment(A, cons);
         }
+        k += nt;
     }
     // the pipeline is drained: its stages hold the partials being merged,
     // completed on the next barrier in the ring
