@@ -432,10 +432,14 @@ def _finish_line(args, wl, world, rank, value, ms_step, attn_bytes, attn_ms, att
 
 def run_split(args, wl, world, rank, local):
     """cfg4: one long sequence.  At N GPUs every rank holds the cache and
-    attends its contiguous page-aligned KV range (qwn_kv_partial writing
-    o | m | l into one block); the blocks are all-gathered over NCCL and
-    merged on every rank (qwn_kv_merge_partials_packed).  The rank owning
-    the tail stores each new token.  Total work is fixed: strong scaling."""
+    attends its contiguous page-aligned KV range.  Default exchange "p2p":
+    qwn_kv_decode_split, whose attention kernel stores each kv head's partial
+    (m, l, o) into every rank's exchange buffer over NVLink and merges the
+    ranks' partials itself -- one launch per step, no collective.  Exchange
+    "nccl": qwn_kv_partial writing o | m | l into one block, an NCCL
+    all-gather of the blocks and qwn_kv_merge_partials_packed on every rank.
+    The rank owning the tail stores each new token.  Total work is fixed:
+    strong scaling."""
     import torch
     import qwanto_b200 as qb
     from qwanto_b200.sharding import kv_ranges
@@ -473,6 +477,11 @@ def run_split(args, wl, world, rank, local):
     # fixed page ranges of the prefilled context; the last rank owns the tail,
     # where every new token goes
     ranges = kv_ranges(c0, world, P)
+    p2p = world > 1 and args.exchange == "p2p"
+    ex = None
+    if p2p:
+        from qwanto_b200.exchange import PeerExchange
+        ex = PeerExchange(H, device=local, timeout_ns=2_000_000_000)
 
     def step(s, i=None):
         r = s % ring
@@ -482,6 +491,11 @@ def run_split(args, wl, world, rank, local):
             ev_a[i].record(stream)
         if world == 1:
             pool.decode(0, 1, H, q[r], out, key=k[r], value=v[r], stream=stream)
+        elif p2p:
+            a, b = ranges[rank]
+            tail = rank == world - 1
+            pool.decode_split(0, H, q[r], out, ex, t_begin=a, t_end=0 if tail else b,
+                              key=k[r] if tail else None, value=v[r] if tail else None, stream=stream)
         else:
             a, b = ranges[rank]
             if rank == world - 1:
@@ -527,6 +541,9 @@ def run_split(args, wl, world, rank, local):
     for _ in range(n_soak):
         if world == 1:
             pool.decode(0, 1, H, q[0], out, stream=stream)
+        elif p2p:
+            a, b = ranges[rank]
+            pool.decode_split(0, H, q[0], out, ex, t_begin=a, t_end=0 if rank == world - 1 else b, stream=stream)
         else:
             a, b = ranges[rank]
             pool.partial(0, 1, H, q[0], send[H * HD: H * HD + H], send[H * HD + H:], send[: H * HD],
@@ -537,6 +554,9 @@ def run_split(args, wl, world, rank, local):
     t_wall1 = time.perf_counter()
     sampler.stop()
     status = pool.check()
+    if ex is not None:
+        dist.barrier()  # every rank is past its last split call before the buffers go
+        ex.close()
     # this rank's algorithmic bytes per step: its KV range, the appended
     # token (tail rank), Q, the exchanged partial blocks and the output
     a, b = ranges[rank]
@@ -548,8 +568,12 @@ def run_split(args, wl, world, rank, local):
     if rank == 0:
         line = _finish_line(args, wl, world, rank, 1000.0 / ms_step, ms_step, attn_bytes, attn_ms, attn_max,
                             launches, status, sampler.summary(t_wall0 - 0.05, t_wall1 + 0.05),
-                            {"global_batch": 1, "context": c0, "parallelism": f"split-KV x{world} (NCCL all-gather "
-                             f"of (m, l, o) blocks, {blk * 4} B per rank)",
+                            {"global_batch": 1, "context": c0,
+                             "parallelism": (f"split-KV x{world}" if world == 1 else
+                                             f"split-KV x{world}, (m, l, o) exchanged in-kernel over NVLink peer "
+                                             f"stores, {blk * 4} B per rank" if p2p else
+                                             f"split-KV x{world} (NCCL all-gather of (m, l, o) blocks, "
+                                             f"{blk * 4} B per rank)"),
                              "l2": "inputs larger than L2 (272 MB of KV per layer-step)"}, "strong")
         line["unit"] = "layer-steps/s"
     pool.close()
@@ -697,6 +721,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--ring", type=int, default=8, help="distinct input step buffers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="cfg4 at N>1: partials exchanged in-kernel over NVLink (p2p) or by an NCCL all-gather")
     ap.add_argument("--layers", type=int, default=0, help="override the config's layer count (profiling)")
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling)")
     args = ap.parse_args()

@@ -62,7 +62,8 @@ enum {
     QWN_KV_STATUS_BAD_PAGE = 1u << 2,
     QWN_KV_STATUS_BAD_SEQUENCE = 1u << 3,
     QWN_KV_STATUS_WAIT_TIMEOUT = 1u << 4,
-    QWN_KV_STATUS_BAD_LENGTH = 1u << 5
+    QWN_KV_STATUS_BAD_LENGTH = 1u << 5,
+    QWN_KV_STATUS_PEER_TIMEOUT = 1u << 6  /* a rank's partial did not arrive (qwn_kv_decode_split) */
 };
 
 typedef struct {
@@ -176,6 +177,62 @@ QWN_CUDA_ABI_API int qwn_kv_merge_partials(uint32_t parts, uint32_t rows, const 
  * decoder has no split-KV path); the merge rule is qwn_kv_merge_partials'. */
 QWN_CUDA_ABI_API int qwn_kv_merge_partials_packed(uint32_t parts, uint32_t rows, const float *packed_dev,
                                                   float *out_dev, void *stream);
+
+/* ---- split-KV over the GPUs of one node, exchange fused into attention ----
+ * Each rank attends its token range of one sequence.  The warp that completes
+ * a (sequence, kv head) segment's partial state (m, l, o) stores it into every
+ * rank's exchange buffer with plain peer stores over NVLink, raises that
+ * segment's flag there, waits (bounded) for every rank's flag of the segment in
+ * its own buffer and merges the ranks' partials in rank order: every rank ends
+ * with the same output rows, and no collective or merge launch follows.  This
+ * replaces qwn_kv_partial + an all-gather + qwn_kv_merge_partials_packed; the
+ * reference's decoder has no split-KV path (its merge rule is the one of
+ * qwn_kv_merge_partials).
+ * Exchange buffer of a rank: flags [2 parities][QWN_KV_MAX_RANKS senders]
+ * [QWN_KV_EXCHANGE_SEGMENTS] u32, then blocks [2][QWN_KV_MAX_RANKS] of
+ * max_rows*130 floats (o[max_rows][128], m[max_rows], l[max_rows]).  Calls
+ * alternate parities, so a rank one call ahead never overwrites a block that
+ * a slower rank is still merging. */
+#define QWN_KV_MAX_RANKS 8u
+#define QWN_KV_EXCHANGE_SEGMENTS 64u
+
+/* bytes of one rank's exchange buffer for rows of up to max_rows query heads */
+QWN_CUDA_ABI_API int qwn_kv_exchange_bytes(uint32_t max_rows, uint64_t *bytes);
+/* allocate and zero this rank's exchange buffer on device_id; ipc_handle
+ * (64 bytes) receives the CUDA IPC handle the other ranks open */
+QWN_CUDA_ABI_API int qwn_kv_exchange_alloc(int32_t device_id, uint64_t bytes, void **buffer_dev,
+                                           void *ipc_handle);
+QWN_CUDA_ABI_API int qwn_kv_exchange_free(int32_t device_id, void *buffer_dev);
+/* map another rank's buffer (its 64-byte IPC handle) into this process on device_id */
+QWN_CUDA_ABI_API int qwn_kv_exchange_open(int32_t device_id, const void *ipc_handle, void **buffer_dev);
+QWN_CUDA_ABI_API int qwn_kv_exchange_close(int32_t device_id, void *buffer_dev);
+
+typedef struct {
+    QwnCudaAbiHeader header;
+    uint32_t rank, world;                /* world <= QWN_KV_MAX_RANKS */
+    uint32_t max_rows;                   /* row capacity the buffers were sized for */
+    uint32_t reserved;
+    void *buffers[QWN_KV_MAX_RANKS];     /* rank p's exchange buffer as mapped here; [rank] = own */
+    uint64_t timeout_ns;                 /* bound on each wait for a rank's partial; 0 = 2 s */
+} QwnKvPeerSet;
+
+typedef struct {
+    QwnCudaAbiHeader header;
+    uint32_t layer;
+    uint32_t query_heads;               /* multiple of kv_heads, at most 8 per kv head, <= max_rows */
+    const int32_t *seq_ids_dev;         /* [1]: the sequence, or NULL = sequence 0 */
+    float scale;                        /* softmax scale; 0 = 1/sqrt(128) */
+    uint32_t epoch;                     /* 1, 2, 3, ...: one per call, the same on every rank */
+    const float *query_dev;             /* [query_heads][128] */
+    const float *key_dev;               /* newest token [kv_heads][128] on the rank whose range runs to the
+                                           end of the sequence (t_end 0), stored before it is read; else NULL */
+    const float *value_dev;
+    float *output_dev;                  /* [query_heads][128]: the merged rows, the same on every rank */
+    uint32_t t_begin, t_end;            /* this rank's token range, t_end 0 = to the end; must hold tokens */
+    const QwnKvPeerSet *peers;
+    void *stream;
+} QwnKvSplitRequest;
+QWN_CUDA_ABI_API int qwn_kv_decode_split(QwnKvPoolHandle *pool, const QwnKvSplitRequest *request);
 
 /* Store tokens [first_pos, first_pos+n_tokens) of one sequence and layer
  * (already reserved with qwn_kv_seq_append): key/value [n_tokens][kv_heads][128]. */

@@ -171,6 +171,21 @@ class KvPool:
         r.t_begin, r.t_end, r.stream = t_begin, t_end, _stream(stream)
         check("qwn_kv_partial", lib().qwn_kv_partial(C.byref(self.h), C.byref(r)))
 
+    def decode_split(self, layer: int, query_heads: int, query, output, exchange, t_begin: int = 0, t_end: int = 0,
+                     key=None, value=None, seq_ids=None, scale: float = 0.0, stream=None) -> None:
+        """Split-KV decode of one sequence over the ranks of `exchange`
+        (a :class:`qwanto_b200.exchange.PeerExchange`): this rank attends
+        [t_begin, t_end) (t_end 0 = to the end, where key/value store the
+        newest token) and every rank receives the merged output rows."""
+        r = init(_lib.SplitRequest())
+        r.layer, r.query_heads, r.seq_ids_dev, r.scale = layer, query_heads, _ptr(seq_ids), scale
+        r.epoch = exchange.next_epoch()
+        r.query_dev, r.key_dev, r.value_dev, r.output_dev = _ptr(query), _ptr(key), _ptr(value), _ptr(output)
+        r.t_begin, r.t_end = t_begin, t_end
+        r.peers = C.addressof(exchange.peers)
+        r.stream = _stream(stream)
+        check("qwn_kv_decode_split", lib().qwn_kv_decode_split(C.byref(self.h), C.byref(r)))
+
     def store_tokens(self, seq: int, layer: int, first_pos: int, n_tokens: int, key, value, stream=None) -> None:
         check("qwn_kv_store_tokens", lib().qwn_kv_store_tokens(C.byref(self.h), seq, layer, first_pos, n_tokens,
                                                                 _ptr(key), _ptr(value), _stream(stream)))

@@ -35,6 +35,10 @@ ST_BAD_PAGE = 1 << 2
 ST_BAD_SEQUENCE = 1 << 3
 ST_WAIT_TIMEOUT = 1 << 4
 ST_BAD_LENGTH = 1 << 5
+ST_PEER_TIMEOUT = 1 << 6
+
+MAX_RANKS = 8
+EXCHANGE_SEGMENTS = 64
 
 
 class Header(C.Structure):
@@ -167,6 +171,18 @@ class StaticAttentionRequest(C.Structure):
                 ("output_dev", C.c_void_p), ("status_dev", C.c_void_p), ("stream", C.c_void_p)]
 
 
+
+class PeerSet(C.Structure):
+    _fields_ = [("header", Header), ("rank", C.c_uint32), ("world", C.c_uint32), ("max_rows", C.c_uint32),
+                ("reserved", C.c_uint32), ("buffers", C.c_void_p * 8), ("timeout_ns", C.c_uint64)]
+
+
+class SplitRequest(C.Structure):
+    _fields_ = [("header", Header), ("layer", C.c_uint32), ("query_heads", C.c_uint32), ("seq_ids_dev", C.c_void_p),
+                ("scale", C.c_float), ("epoch", C.c_uint32), ("query_dev", C.c_void_p), ("key_dev", C.c_void_p),
+                ("value_dev", C.c_void_p), ("output_dev", C.c_void_p), ("t_begin", C.c_uint32),
+                ("t_end", C.c_uint32), ("peers", C.c_void_p), ("stream", C.c_void_p)]
+
 _P = C.POINTER
 _SIGS = {
     "qwn_cuda_abi_query": (C.c_int, [_P(AbiInfo)]),
@@ -199,6 +215,12 @@ _SIGS = {
     "qwn_kv_merge_partials": (C.c_int, [C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_void_p]),
     "qwn_kv_merge_partials_packed": (C.c_int, [C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "qwn_kv_exchange_bytes": (C.c_int, [C.c_uint32, _P(C.c_uint64)]),
+    "qwn_kv_exchange_alloc": (C.c_int, [C.c_int32, C.c_uint64, _P(C.c_void_p), C.c_void_p]),
+    "qwn_kv_exchange_free": (C.c_int, [C.c_int32, C.c_void_p]),
+    "qwn_kv_exchange_open": (C.c_int, [C.c_int32, C.c_void_p, _P(C.c_void_p)]),
+    "qwn_kv_exchange_close": (C.c_int, [C.c_int32, C.c_void_p]),
+    "qwn_kv_decode_split": (C.c_int, [_P(Handle), _P(SplitRequest)]),
     "qwn_kv_store_tokens": (C.c_int, [_P(Handle), C.c_int32, C.c_uint32, C.c_uint32, C.c_uint32,
                                       C.c_void_p, C.c_void_p, C.c_void_p]),
     "qwn_kv_generate_rows": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64,

@@ -69,6 +69,12 @@ struct AttnArgs {
     float *part_m, *part_l, *part_o;  // non-null: export unnormalised (m, l, o)
     const float *new_k, *new_v;       // non-null: fused append of the newest token
     uint32_t *status;
+    // split-KV over ranks (xworld > 0): every segment's partial goes to each
+    // rank's exchange buffer (xbuf[p] as mapped here) and the ranks' partials
+    // of the segment merge into the output
+    uint8_t *xbuf[QWN_KV_MAX_RANKS];
+    uint32_t xrank, xworld, xepoch, xrows;
+    uint64_t xtimeout_ns;
 };
 
 __device__ __forceinline__ float pow2ceil(float x) {
@@ -1165,6 +1171,134 @@ __device__ __noinline__ void fused_append(const float *new_k, const float *new_v
 // and l[G]; one bulk copy of slot_bytes(G) moves it.
 __device__ __forceinline__ uint32_t slot_bytes(uint32_t G) { return (G * (kHeadDim + 2) * 4 + 15u) & ~15u; }
 
+// ---------------------------------------------------------------------------
+// split-KV exchange between ranks (peer memory over NVLink)
+// ---------------------------------------------------------------------------
+constexpr size_t kXFlagBytes = 2ull * QWN_KV_MAX_RANKS * QWN_KV_EXCHANGE_SEGMENTS * 4;
+__device__ __forceinline__ uint32_t *xflag(uint8_t *buf, uint32_t parity, uint32_t sender, uint32_t seg) {
+    return reinterpret_cast<uint32_t *>(buf) + (parity * QWN_KV_MAX_RANKS + sender) * QWN_KV_EXCHANGE_SEGMENTS + seg;
+}
+// block of (parity, sender): o[xrows][128], m[xrows], l[xrows]
+__device__ __forceinline__ float *xblock(uint8_t *buf, uint32_t parity, uint32_t sender, uint32_t xrows) {
+    return reinterpret_cast<float *>(buf + kXFlagBytes) +
+           (size_t)(parity * QWN_KV_MAX_RANKS + sender) * xrows * (kHeadDim + 2);
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// copy this warp's partial slot of segment s_idx (written by the warp itself)
+// into every rank's block
+__device__ __forceinline__ void publish_slot(const AttnArgs &A, uint32_t s_idx, const float *slot) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t G = A.group;
+    const size_t row0 = (size_t)s_idx * G;
+    __syncwarp();  // the lanes' slot stores are visible to the whole warp
+    for (uint32_t g = 0; g < G; g++) {
+        const float4 v = reinterpret_cast<const float4 *>(slot + g * kHeadDim)[lane];
+        const float m = slot[G * kHeadDim + g], l = slot[G * kHeadDim + G + g];
+        for (uint32_t r = 0; r < A.xworld; r++) {
+            float *blk = xblock(A.xbuf[r], A.xepoch & 1u, A.xrank, A.xrows);
+            reinterpret_cast<float4 *>(blk + (row0 + g) * kHeadDim)[lane] = v;
+            if (lane == 0) {
+                blk[(size_t)A.xrows * kHeadDim + row0 + g] = m;
+                blk[(size_t)A.xrows * (kHeadDim + 1) + row0 + g] = l;
+            }
+        }
+    }
+}
+
+// This rank's partial of segment s_idx (rows row0..row0+G) has been stored
+// into every rank's block by the calling warp: raise the segment's flag on
+// every rank (lane r releases to rank r; the warp barrier before it orders the
+// other lanes' block stores), wait -- lane r for rank r's flag in this rank's
+// buffer, bounded by xtimeout_ns -- and merge the ranks' partials in rank
+// order into the output rows: the same arithmetic, so the same rows, on
+// every rank.  Loads go through L2 (.cg): the blocks are written by peers.
+__device__ __forceinline__ void exchange_merge(const AttnArgs &A, uint32_t s_idx, size_t row0) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t par = A.xepoch & 1u, W = A.xworld, G = A.group;
+    __syncwarp();
+    if ((uint32_t)lane < W) st_release_sys(xflag(A.xbuf[lane], par, A.xrank, s_idx), A.xepoch);
+    uint8_t *own = A.xbuf[A.xrank];
+    bool ok = true;
+    if ((uint32_t)lane < W) {
+        const uint32_t *f = xflag(own, par, lane, s_idx);
+        const uint64_t t0 = globaltimer();
+        while (ld_acquire_sys(f) != A.xepoch) {
+            if (globaltimer() - t0 > A.xtimeout_ns) { ok = false; break; }
+            __nanosleep(32);
+        }
+    }
+    if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) latch(A.status, QWN_KV_STATUS_PEER_TIMEOUT);
+        return;
+    }
+    // (m, l) of pair i = g*W + r (at most 64 pairs): lane holds i = lane, lane+32
+    float mp[2], lp[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const uint32_t i = (uint32_t)lane + 32u * h;
+        mp[h] = -INFINITY;
+        lp[h] = 0.f;
+        if (i < G * W) {
+            const float *blk = xblock(own, par, i % W, A.xrows);
+            const size_t row = row0 + i / W;
+            mp[h] = __ldcg(blk + (size_t)A.xrows * kHeadDim + row);
+            lp[h] = __ldcg(blk + (size_t)A.xrows * (kHeadDim + 1) + row);
+        }
+    }
+    for (uint32_t g = 0; g < G; g += 2) {
+        // two rows per round: all ranks' o of both rows are loaded at once
+        float4 v[2][QWN_KV_MAX_RANKS];
+#pragma unroll
+        for (int e = 0; e < 2; e++)
+#pragma unroll
+            for (uint32_t r = 0; r < QWN_KV_MAX_RANKS; r++)
+                v[e][r] = (r < W && g + e < G)
+                              ? __ldcg(reinterpret_cast<const float4 *>(xblock(own, par, r, A.xrows) +
+                                                                        (row0 + g + e) * kHeadDim) + lane)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            if (g + e >= G) break;
+            float m[QWN_KV_MAX_RANKS], l[QWN_KV_MAX_RANKS];
+            float M = -INFINITY;
+#pragma unroll
+            for (uint32_t r = 0; r < QWN_KV_MAX_RANKS; r++) {
+                const uint32_t i = (g + e) * W + r;
+                const float mh = __shfl_sync(0xffffffffu, i < 32 ? mp[0] : mp[1], i & 31);
+                const float lh = __shfl_sync(0xffffffffu, i < 32 ? lp[0] : lp[1], i & 31);
+                m[r] = r < W ? mh : -INFINITY;
+                l[r] = r < W ? lh : 0.f;
+                M = fmaxf(M, m[r]);
+            }
+            float ls = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (uint32_t r = 0; r < QWN_KV_MAX_RANKS; r++) {
+                if (r >= W) break;
+                const float w = m[r] == -INFINITY ? 0.f : ex2(m[r] - M);
+                ls += l[r] * w;
+                acc.x += v[e][r].x * w; acc.y += v[e][r].y * w; acc.z += v[e][r].z * w; acc.w += v[e][r].w * w;
+            }
+            const float inv = ls > 0.f ? 1.0f / ls : 0.f;
+            reinterpret_cast<float4 *>(A.output + (row0 + g + e) * kHeadDim)[lane] =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        }
+    }
+}
+
 // Merge the nparts partial slots of segment s_idx into its output rows
 // (row0 = s_idx * G).  The slots were written by other warps, so each read is
 // an L2 round trip made while DRAM is saturated by the streaming warps; the
@@ -1172,7 +1306,7 @@ __device__ __forceinline__ uint32_t slot_bytes(uint32_t G) { return (G * (kHeadD
 // stages (buf, SB bytes) with bulk copies completed on one mbarrier -- one
 // round trip per chunk -- and combines them from shared memory.  GG >= G is
 // the compile-time row count.  Returns false when the wait gave up.
-template <int GG>
+template <int GG, bool XCHG>
 __device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, uint64_t base_w, uint32_t stride_w,
                                            uint32_t nparts, float *dst_slot, uint8_t *buf, uint32_t SB,
                                            uint64_t *bar, uint32_t &par) {
@@ -1250,7 +1384,16 @@ __device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, ui
             continue;
         }
         const size_t row = row0 + g;
-        if (A.part_o) {
+        if constexpr (XCHG) {
+            for (uint32_t r = 0; r < A.xworld; r++) {
+                float *blk = xblock(A.xbuf[r], A.xepoch & 1u, A.xrank, A.xrows);
+                reinterpret_cast<float4 *>(blk + row * kHeadDim)[lane] = acc[g];
+                if (lane == 0) {
+                    blk[(size_t)A.xrows * kHeadDim + row] = M[g];
+                    blk[(size_t)A.xrows * (kHeadDim + 1) + row] = ls[g];
+                }
+            }
+        } else if (A.part_o) {
             reinterpret_cast<float4 *>(A.part_o + row * kHeadDim)[lane] = acc[g];
             if (lane == 0) { A.part_m[row] = M[g]; A.part_l[row] = ls[g]; }
         } else {
@@ -1260,15 +1403,19 @@ __device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, ui
         }
         if (A.seg_ml && lane == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + g] = make_float2(M[g], ls[g]);
     }
+    if constexpr (XCHG) {
+        if (!dst_slot) exchange_merge(A, s_idx, row0);
+    }
     return true;
 }
 
+template <bool XCHG>
 __device__ __forceinline__ bool merge_parts(const AttnArgs &A, uint32_t s_idx, uint64_t base_w, uint32_t stride_w,
                                             uint32_t nparts, float *dst_slot, uint8_t *buf, uint32_t SB,
                                             uint64_t *bar, uint32_t &par) {
-    if (A.group <= 2) return merge_rows<2>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
-    if (A.group <= 4) return merge_rows<4>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
-    return merge_rows<8>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
+    if (A.group <= 2) return merge_rows<2, XCHG>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
+    if (A.group <= 4) return merge_rows<4, XCHG>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
+    return merge_rows<8, XCHG>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
 }
 
 // End of a warp's share of segment s_idx (first unit Us, ns units).  A warp
@@ -1278,7 +1425,7 @@ __device__ __forceinline__ bool merge_parts(const AttnArgs &A, uint32_t s_idx, u
 // streaming loop (a release there waits for the slot stores to reach L2, a
 // round trip the loop should not take mid-stream); the warp that draws
 // nparts-1 merges, also after its loop.
-template <class OPS>
+template <class OPS, bool XCHG>
 __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const typename OPS::State &st, uint32_t s_idx,
                                                    uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid) {
     // warps whose range meets the segment's tiles (virtual units Us+V ..
@@ -1287,7 +1434,9 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
     const uint64_t wa = warp_of_unit(Us + kVirtualUnits, T, W), wb = warp_of_unit(Us + kVirtualUnits + ns - 1, T, W);
     const uint32_t nparts = (uint32_t)(wb - wa + 1);
     const size_t row0 = (size_t)s_idx * A.group;
-    if (nparts == 1) {
+    // split-KV over ranks: a whole segment is a partial too (its slot is
+    // published to the ranks after the streaming loop)
+    if (nparts == 1 && !XCHG) {
         float2 *sm = A.seg_ml ? A.seg_ml + (size_t)s_idx * kMaxGroup : nullptr;
         if (A.part_o)
             OPS::store_rows(A, st, A.part_o + row0 * kHeadDim, A.part_m + row0, A.part_l + row0, false, sm);
@@ -1312,7 +1461,7 @@ __device__ __forceinline__ uint32_t *part_counter(const AttnArgs &A, uint32_t s_
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int CODEC, int HG>
+template <int CODEC, int HG, bool XCHG>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kernel(const AttnArgs A) {
     using OPS = Ops<CODEC, HG>;
     constexpr int S = OPS::kStages, B = OPS::kBytes;
@@ -1489,6 +1638,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     // segment a few tiles after it was written (its stores have landed by then,
     // so the release costs nothing), the last after the loop
     uint32_t pend_n = 0, pend_s0 = 0, pend_n0 = 0, pend_s1 = 0, pend_n1 = 0, pend_k0 = 0, tk0 = 0;
+    uint64_t xpend = 0;  // split-KV: segments this warp saw whole, to publish and merge after the loop
     bool counted0 = false;
     uint64_t pend_u0 = 0, pend_u1 = 0;
 
@@ -1574,8 +1724,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         // end of this warp's share of the segment?
         if (cons.tile + nt == cons.geo.ntiles || k + nt == n) {
             const uint32_t s_idx = cons.i * HK + cons.h;
-            const uint32_t np = finish_segment<OPS>(A, state, s_idx, cons.vbase, cons.geo.ntiles, Tv, W, wid);
-            if (np) {
+            const uint32_t np = finish_segment<OPS, XCHG>(A, state, s_idx, cons.vbase, cons.geo.ntiles, Tv, W, wid);
+            if (XCHG && np == 1) xpend |= 1ull << s_idx;
+            else if (np) {
                 const int e = pend_n++;  // at most two: the segment the range starts in and the one it ends in
                 if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.vbase; pend_k0 = k; }
                 else { pend_s1 = s_idx; pend_n1 = np; pend_u1 = cons.vbase; }
@@ -1602,6 +1753,14 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     }
     tk0 = __shfl_sync(0xffffffffu, tk0, 0);
     tk1 = __shfl_sync(0xffffffffu, tk1, 0);
+    if constexpr (XCHG) {
+        while (xpend) {
+            const uint32_t s = (uint32_t)(__ffsll((long long)xpend) - 1);
+            xpend &= xpend - 1;
+            publish_slot(A, s, A.partials + (size_t)(wid + s) * kPartialFloats);
+            exchange_merge(A, s, (size_t)s * A.group);
+        }
+    }
     for (uint32_t e = 0; e < pend_n; e++) {
         const uint32_t np = e ? pend_n1 : pend_n0, s_idx = e ? pend_s1 : pend_s0;
         const uint64_t wa = warp_of_unit((e ? pend_u1 : pend_u0) + kVirtualUnits, Tv, W);
@@ -1610,7 +1769,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         const uint32_t SB = (uint32_t)(S * B);
         if (np <= kMergeGroup) {
             if (tk != np - 1) continue;  // not the last arrival
-            if (!merge_parts(A, s_idx, wa, 1, np, nullptr, buf, SB, &bars[st], par)) return;
+            if (!merge_parts<XCHG>(A, s_idx, wa, 1, np, nullptr, buf, SB, &bars[st], par)) return;
             if (lane == 0) A.counters[s_idx] = 0u;  // ready for the next launch
             continue;
         }
@@ -1619,7 +1778,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         const uint32_t gsize = (uint32_t)min((uint64_t)kMergeGroup, wa + np - gbase);
         if (tk != gsize - 1) continue;
         float *gslot = A.partials + (size_t)(gbase + s_idx) * kPartialFloats;
-        if (!merge_parts(A, s_idx, gbase, 1, gsize, gslot, buf, SB, &bars[st], par)) return;
+        if (!merge_parts<XCHG>(A, s_idx, gbase, 1, gsize, gslot, buf, SB, &bars[st], par)) return;
         if (lane == 0) A.gcounters[gbase + s_idx] = 0u;
         // publish the group result (in its first part's slot) and count it
         __syncwarp();
@@ -1627,7 +1786,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         if (lane == 0) t2 = atom_add_acq_rel_gpu(&A.counters[s_idx], 1u);
         t2 = __shfl_sync(0xffffffffu, t2, 0);
         if (t2 != (np + kMergeGroup - 1) / kMergeGroup - 1) continue;
-        if (!merge_parts(A, s_idx, wa, kMergeGroup, (np + kMergeGroup - 1) / kMergeGroup, nullptr, buf, SB,
+        if (!merge_parts<XCHG>(A, s_idx, wa, kMergeGroup, (np + kMergeGroup - 1) / kMergeGroup, nullptr, buf, SB,
                          &bars[st], par))
             return;
         if (lane == 0) A.counters[s_idx] = 0u;
@@ -1663,10 +1822,16 @@ constexpr size_t codec_smem() {
 // kernel variants: one or two head groups of four query heads
 template <int CODEC>
 cudaError_t configure_codec() {
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<CODEC, 1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)codec_smem<CODEC, 1>());
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attn_kernel<CODEC, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(attn_kernel<CODEC, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)codec_smem<CODEC, 2>());
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_kernel<CODEC, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)codec_smem<CODEC, 1>());
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_kernel<CODEC, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)codec_smem<CODEC, 2>());
     return e;
 }
@@ -1684,14 +1849,19 @@ cudaError_t launch_variant(const uint32_t (&ctas)[2], const AttnArgs &A, cudaStr
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    // split-KV over ranks (the exchange) is its own instantiation, so the
+    // decode kernels carry none of its code
+    const bool x = A.xworld != 0;
     if (A.group > 4) {
         cfg.gridDim = dim3(ctas[1]);
         cfg.dynamicSmemBytes = codec_smem<CODEC, 2>();
-        return cudaLaunchKernelEx(&cfg, attn_kernel<CODEC, 2>, A);
+        return x ? cudaLaunchKernelEx(&cfg, attn_kernel<CODEC, 2, true>, A)
+                 : cudaLaunchKernelEx(&cfg, attn_kernel<CODEC, 2, false>, A);
     }
     cfg.gridDim = dim3(ctas[0]);
     cfg.dynamicSmemBytes = codec_smem<CODEC, 1>();
-    return cudaLaunchKernelEx(&cfg, attn_kernel<CODEC, 1>, A);
+    return x ? cudaLaunchKernelEx(&cfg, attn_kernel<CODEC, 1, true>, A)
+             : cudaLaunchKernelEx(&cfg, attn_kernel<CODEC, 1, false>, A);
 }
 
 template <int CODEC>
@@ -1727,17 +1897,17 @@ size_t attention_smem_bytes(uint32_t codec, int hg) {
 const void *attention_kernel_ptr(uint32_t codec, int hg) {
     switch (codec) {
         case QWN_KV_CODEC_Q8_HEAD_F16:
-            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16, 1>
-                           : (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16, 2>;
+            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16, 1, false>
+                           : (const void *)attn_kernel<QWN_KV_CODEC_Q8_HEAD_F16, 2, false>;
         case QWN_KV_CODEC_Q8_B64_F32:
-            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32, 1>
-                           : (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32, 2>;
+            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32, 1, false>
+                           : (const void *)attn_kernel<QWN_KV_CODEC_Q8_B64_F32, 2, false>;
         case QWN_KV_CODEC_Q4_G32:
-            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 1>
-                           : (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 2>;
+            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 1, false>
+                           : (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 2, false>;
         case QWN_KV_CODEC_TQ35_G64:
-            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 1>
-                           : (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 2>;
+            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 1, false>
+                           : (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 2, false>;
         default: return nullptr;
     }
 }
@@ -1780,6 +1950,14 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
     A.new_k = a.new_k;
     A.new_v = a.new_v;
     A.status = p->status;
+    if (a.peers) {
+        for (uint32_t r = 0; r < a.peers->world; r++) A.xbuf[r] = static_cast<uint8_t *>(a.peers->buffers[r]);
+        A.xrank = a.peers->rank;
+        A.xworld = a.peers->world;
+        A.xrows = a.peers->max_rows;
+        A.xepoch = a.epoch;
+        A.xtimeout_ns = a.peers->timeout_ns ? a.peers->timeout_ns : 2000000000ull;
+    }
     switch (p->codec) {
         case QWN_KV_CODEC_Q8_HEAD_F16: return launch_codec<QWN_KV_CODEC_Q8_HEAD_F16>(p, A, s);
         case QWN_KV_CODEC_Q8_B64_F32: return launch_codec<QWN_KV_CODEC_Q8_B64_F32>(p, A, s);

@@ -124,6 +124,9 @@ struct AttnLaunch {
     uint32_t t_begin, t_end;
     // fused quantize-on-append of the newest token ([num_seqs][kv_heads][128])
     const float *new_k, *new_v;
+    // split-KV over ranks: exchange of the segments' partials, merged in-kernel
+    const QwnKvPeerSet *peers;
+    uint32_t epoch;
 };
 cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s);
 cudaError_t launch_merge(uint32_t parts, uint32_t rows, const float *m, const float *l,

@@ -664,6 +664,98 @@ QWN_CUDA_ABI_API int qwn_kv_merge_partials_packed(uint32_t parts, uint32_t rows,
     return QWN_CUDA_STATUS_OK;
 }
 
+// ---- split-KV exchange buffers (CUDA IPC over the node's NVLink fabric) ----
+static size_t exchange_bytes(uint32_t max_rows) {
+    return 2ull * QWN_KV_MAX_RANKS * QWN_KV_EXCHANGE_SEGMENTS * 4 +
+           2ull * QWN_KV_MAX_RANKS * max_rows * (kHeadDim + 2) * sizeof(float);
+}
+
+QWN_CUDA_ABI_API int qwn_kv_exchange_bytes(uint32_t max_rows, uint64_t *bytes) {
+    if (!bytes || max_rows == 0) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    *bytes = exchange_bytes(max_rows);
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_exchange_alloc(int32_t device, uint64_t bytes, void **buf, void *ipc_handle) {
+    if (!buf || !ipc_handle || bytes == 0) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    *buf = nullptr;
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaMalloc(buf, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*buf, 0, bytes);
+    cudaIpcMemHandle_t hd{};
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&hd, *buf);
+    if (e != cudaSuccess) {
+        if (*buf) cudaFree(*buf);
+        *buf = nullptr;
+        set_cuda_error("qwn_kv_exchange_alloc", e);
+        return e == cudaErrorMemoryAllocation ? QWN_CUDA_STATUS_OUT_OF_MEMORY : QWN_CUDA_STATUS_RUNTIME_ERROR;
+    }
+    static_assert(sizeof(hd) == 64, "CUDA IPC handles are 64 bytes");
+    std::memcpy(ipc_handle, &hd, sizeof(hd));
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_exchange_free(int32_t device, void *buf) {
+    if (!buf) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(device);
+    cudaError_t e = cudaFree(buf);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_exchange_free", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_exchange_open(int32_t device, const void *ipc_handle, void **buf) {
+    if (!buf || !ipc_handle) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t hd;
+    std::memcpy(&hd, ipc_handle, sizeof(hd));
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaIpcOpenMemHandle(buf, hd, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_exchange_open", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_exchange_close(int32_t device, void *buf) {
+    if (!buf) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    cudaSetDevice(device);
+    cudaError_t e = cudaIpcCloseMemHandle(buf);
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_exchange_close", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
+QWN_CUDA_ABI_API int qwn_kv_decode_split(QwnKvPoolHandle *h, const QwnKvSplitRequest *r) {
+    Pool *p = pool_from(h);
+    if (!p || !r || !header_ok(r->header, sizeof(*r))) return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    const QwnKvPeerSet *ps = r->peers;
+    bool ok = ps && header_ok(ps->header, sizeof(*ps)) && ps->world >= 1 && ps->world <= QWN_KV_MAX_RANKS &&
+              ps->rank < ps->world && r->epoch != 0 && r->layer < p->layers && r->query_dev && r->output_dev &&
+              r->query_heads && r->query_heads % p->kv_heads == 0 && r->query_heads <= p->max_query_heads &&
+              r->query_heads <= ps->max_rows && p->kv_heads <= QWN_KV_EXCHANGE_SEGMENTS &&
+              (r->t_end == 0 || r->t_end > r->t_begin) && ((r->key_dev == nullptr) == (r->value_dev == nullptr)) &&
+              (r->key_dev == nullptr || r->t_end == 0);
+    for (uint32_t k = 0; ok && k < ps->world; k++) ok = ps->buffers[k] != nullptr;
+    if (!ok) {
+        set_error("qwn_kv_decode_split: invalid request");
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    }
+    cudaSetDevice(p->device);
+    AttnLaunch a{};
+    a.layer = r->layer;
+    a.num_seqs = 1;
+    a.query_heads = r->query_heads;
+    a.seq_ids = r->seq_ids_dev;
+    a.query = r->query_dev;
+    a.output = r->output_dev;
+    a.scale = r->scale > 0.f ? r->scale : 1.0f / std::sqrt((float)kHeadDim);
+    a.t_begin = r->t_begin;
+    a.t_end = r->t_end;
+    a.new_k = r->key_dev;
+    a.new_v = r->value_dev;
+    a.peers = ps;
+    a.epoch = r->epoch;
+    cudaError_t e = launch_attention(p, a, stream_of(p, r->stream));
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_decode_split", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    return QWN_CUDA_STATUS_OK;
+}
+
 QWN_CUDA_ABI_API int qwn_kv_store_tokens(QwnKvPoolHandle *h, int32_t seq, uint32_t layer, uint32_t first,
                                          uint32_t n, const float *key, const float *value, void *stream) {
     Pool *p = pool_from(h);
