@@ -68,7 +68,8 @@ def profiled_traffic(cfg: int):
     """DRAM bytes per attention launch (dram__bytes_read + write) from the
     committed ncu capture of the same kernel on this workload's shapes, or
     None when no capture covers the workload."""
-    path = os.path.join(ROOT, "profiles", {2: "attn_kernel_q8head_cfg2_full.md"}.get(cfg, ""))
+    path = os.path.join(ROOT, "profiles", {2: "attn_kernel_q8head_cfg2_full.md", 3: "attn_kernel_q4_cfg3_full.md",
+                                           4: "attn_kernel_q8head_hg2_cfg4_full.md"}.get(cfg, ""))
     if not os.path.isfile(path):
         return None
     with open(path) as f:
@@ -303,7 +304,7 @@ def run_ours(args, wl, world, rank, local):
     ms_total = start.elapsed_time(end)
     # keep the GPU busy (attention only, no growth) so the clock samples cover
     # at least ~1.5 s of this workload
-    while time.perf_counter() - t_wall0 < 1.5:
+    while time.perf_counter() - t_wall0 < args.soak_ms / 1000.0:
         for layer in range(L):
             pool.decode(layer, B, H, q[0, layer], out[layer], stream=stream)
         torch.cuda.synchronize(dev)
@@ -414,6 +415,8 @@ def _finish_line(args, wl, world, rank, value, ms_step, attn_bytes, attn_ms, att
                  clocks, extra_config, scaling, e2e=None):
     peak, peak_kind = peaks()
     achieved = attn_bytes / (attn_ms / 1000.0) / 1e9 if attn_ms > 0 else 0.0
+    # the committed capture covers the 1-GPU launch of this workload only
+    traffic = profiled_traffic(args.config) if world == 1 else None
     line = {
         "metric": METRIC, "value": value, "unit": "seq-steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling,
@@ -421,7 +424,8 @@ def _finish_line(args, wl, world, rank, value, ms_step, attn_bytes, attn_ms, att
         "config": dict({"workload": wl["name"], "layers": wl["layers"], "query_heads": wl["H"],
                         "kv_heads": wl["HK"], "head_dim": HD, "page_tokens": wl["P"]}, **extra_config),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": attn_bytes,
+                     "peak_kind": peak_kind, "traffic": (traffic or {}).get("bytes_per_launch"),
+                     "traffic_source": (traffic or {}).get("source"), "algorithmic_bytes_per_launch": attn_bytes,
                      "avg_launch_ms": attn_ms, "avg_launch_ms_max_rank": attn_ms_max},
         "gpu_launches": int(launches), "status_bits": status, "clocks": clocks,
     }
@@ -537,7 +541,7 @@ def run_split(args, wl, world, rank, local):
     ms_step = ms_total / K
     # keep the GPUs on this workload (no growth; the same count on every rank,
     # so the collectives match) until the clock samples cover ~1.5 s
-    n_soak = min(100000, int(1500.0 / max(ms_step, 1e-3)) + 1)
+    n_soak = min(100000, int(args.soak_ms / max(ms_step, 1e-3)) + 1) if args.soak_ms > 0 else 0
     for _ in range(n_soak):
         if world == 1:
             pool.decode(0, 1, H, q[0], out, stream=stream)
@@ -671,7 +675,7 @@ def run_churn(args, wl, world, rank, local):
     ms_total = start.elapsed_time(end)
     # keep the GPU on this workload (attention only, no growth or eviction)
     # until the clock samples cover ~1.5 s
-    while time.perf_counter() - t_wall0 < 1.5:
+    while time.perf_counter() - t_wall0 < args.soak_ms / 1000.0:
         for _ in range(20):
             pool.decode(0, B, H, q[0], out, stream=stream)
         torch.cuda.synchronize(dev)
@@ -721,6 +725,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--ring", type=int, default=8, help="distinct input step buffers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--soak-ms", type=float, default=1500.0,
+                    help="cfg4/cfg5: keep the GPU on the workload after the timed steps until the clock samples "
+                         "cover this long (0 for profiling runs)")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="cfg4 at N>1: partials exchanged in-kernel over NVLink (p2p) or by an NCCL all-gather")
     ap.add_argument("--layers", type=int, default=0, help="override the config's layer count (profiling)")
