@@ -1086,11 +1086,13 @@ __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t v) {
 // launch appends (-1: none).  The next window is requested 16 units before it
 // is needed.
 struct WarpWindow {
-    int32_t pg[2][32];
-    uint32_t off[2][32];
+    int32_t pg[2][32];    // page id (kNoUnit past the warp's last unit)
+    uint32_t off[2][32];  // tile offset in its page; after window_resolve the
+                          // tile's address in 64-byte units from the pool base
     int32_t app[2][32];
     uint32_t hv[2][32];  // h * tiles_per_page + tile in page (layer-free part of off)
 };
+constexpr int32_t kNoUnit = INT32_MIN;
 
 // the newest token's K and V rows (512 B each) of segment `app` into L1 for its store
 __device__ __forceinline__ void prefetch_new_rows(const AttnArgs &A, int32_t app) {
@@ -1128,7 +1130,7 @@ __device__ __forceinline__ void fill_window(const AttnArgs &A, const Walk &from,
             prefetch_new_rows(A, app);
         }
     }
-    if (!copied) win->pg[w][lane] = -1;
+    if (!copied) win->pg[w][lane] = base + lane < n ? -1 : kNoUnit;
     win->off[w][lane] = off;
     win->app[w][lane] = app;
     win->hv[w][lane] = hv;
@@ -1139,14 +1141,23 @@ __device__ __forceinline__ void window_ready() {
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncwarp();
 }
-// address of unit L of window w (out-of-range page ids latch BAD_PAGE)
-__device__ __forceinline__ const uint8_t *window_src(const AttnArgs &A, const WarpWindow *win, int w, uint32_t L) {
-    int32_t pg = win->pg[w][L];
-    if (pg < 0 || (uint32_t)pg >= A.total_pages) {
+// tile addresses of window w's units, one lane each, once its page ids have
+// landed (out-of-range page ids of real units latch BAD_PAGE and read page
+// 0).  Pages and tiles are multiples of 64 bytes, so the address fits 32 bits
+// in 64-byte units for pools up to 256 GB.
+__device__ __forceinline__ void window_resolve(const AttnArgs &A, WarpWindow *win, int w) {
+    const int lane = threadIdx.x & 31;
+    int32_t pg = win->pg[w][lane];
+    if (pg != kNoUnit && (pg < 0 || (uint32_t)pg >= A.total_pages)) {
         latch(A.status, QWN_KV_STATUS_BAD_PAGE);
         pg = 0;  // stay in bounds; the latched status marks the result invalid
     }
-    return A.pages + (size_t)pg * A.page_bytes + win->off[w][L];
+    if (pg == kNoUnit) pg = 0;
+    win->off[w][lane] = (uint32_t)(((uint64_t)pg * A.page_bytes + win->off[w][lane]) >> 6);
+    __syncwarp();
+}
+__device__ __forceinline__ const uint8_t *window_src(const AttnArgs &A, const WarpWindow *win, int w, uint32_t L) {
+    return A.pages + ((size_t)win->off[w][L] << 6);
 }
 
 // quantize and store the newest token of segment `seg` into `tile`
@@ -1620,6 +1631,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         if (n == 0) return;
     }
 
+    window_resolve(A, win, 0);
     const uint32_t npro = n < (uint32_t)S ? n : (uint32_t)S;
     for (uint32_t j = 0; j < npro; j++) {
         const int32_t seg = win->app[0][j];
@@ -1706,6 +1718,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
                     wbase = j;
                     cw ^= 1;
                     window_ready();
+                    window_resolve(A, win, cw);
                 }
                 const int32_t seg = win->app[cw][j - wbase];
                 const uint8_t *src = window_src(A, win, cw, j - wbase);
