@@ -92,10 +92,11 @@ __device__ __forceinline__ float2 h2x2f(uint32_t w) {
 // m16n8 product covers 16 tokens x 4 heads:
 //  * QK^T on the integer tensor cores (m16n8k32 u8 x s8 -> s32): the K codes
 //    (stored biased, 1..255) are used as they are; each query row is split
-//    into four int8 slices q = s0*c0 + s1*c1 + s2*c2 + s3*c3 (s_{j+1} =
-//    s_j/254, residual below 2^-31 of max|q|), columns (head, slice).  The
-//    sums are exact integers; 128*sum(c_j) removes the code bias, and the
-//    slices recombine in fp32 with the token's K scale.
+//    into three int8 slices q = s0*c0 + s1*c1 + s2*c2 (s_{j+1} = s_j/254,
+//    residual below 2^-23 of max|q|), columns (head, slice): 4 heads x 3
+//    slices in 2 n-blocks, 8 heads x 3 slices in 3.  The sums are exact
+//    integers; 128*sum(c_j) removes the code bias, and the slices
+//    recombine in fp32 with the token's K scale.
 //  * P x V on the f16 tensor cores with V^T as the A operand (dims x
 //    tokens) and P^T (tokens x (head, hi/lo)) as B: the probabilities of a
 //    lane's two tokens become f16 hi+lo pairs, and movmatrix transposes them
@@ -111,10 +112,21 @@ struct Int8T {
     // two head groups keep twice the state: 2 CTAs per SM, deeper pipelines
     static constexpr int kBytes = kB64 ? 4352 : 4160, kStages = HG == 1 ? 4 : 6;
     static constexpr int kTilesPerStep = 1;
+    // QK^T n-blocks: columns (head, slice), three query slices per head.
+    // C column e (0, 1) of n-block nb held by a lane belongs to head group
+    // col_hg and slice col_slice of the lane's head tig (-1: unused):
+    //   HG = 1: nb0 = slices 0, 1; nb1 = slice 2 | unused
+    //   HG = 2: nb0 = group 0 slices 0, 1; nb1 = group 1 slices 0, 1;
+    //           nb2 = slice 2 of group 0 | of group 1
+    static constexpr int kNB = HG == 1 ? 2 : 3;
+    __device__ static constexpr int col_hg(int nb, int e) { return HG == 1 ? 0 : (nb < 2 ? nb : e); }
+    __device__ static constexpr int col_slice(int nb, int e) {
+        return HG == 1 ? (nb == 0 ? e : (e == 0 ? 2 : -1)) : (nb < 2 ? e : 2);
+    }
     struct Frag {
-        uint32_t b[HG][2][4][2];   // IMMA B: [head group][n-block][k-block][reg]
-        uint32_t magic[HG][kX][4]; // per (scale group, slice) of this lane's head
-        float sc[HG][4];           // slice scale x log2(e) x softmax scale
+        uint32_t b[kNB][4][2];        // IMMA B: [n-block][k-block][reg]
+        uint32_t magic[kX][2 * kNB];  // per (scale group, C column 2nb+e of this lane)
+        float sc[2 * kNB];            // slice scale x log2(e) x softmax scale per C column
     };
     struct State {
         float o[HG][8][4];  // (dims x (head, hi/lo)) accumulators per m-block
@@ -126,6 +138,10 @@ struct Int8T {
     __device__ static void begin(Frag &f, State &st, const AttnArgs &A, uint32_t s_idx) {
         const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
         const uint32_t G = A.group;
+        uint32_t packed[HG][3][8];  // B words of the lane's head of each group, per slice
+        int colsum[HG][3][kX];      // sum of the slice codes over the head's dims, per scale group
+        float s0[HG];
+        int bad[HG];
 #pragma unroll
         for (int hg = 0; hg < HG; hg++) {
             const uint32_t hq = 4 * hg + (gid >> 1);
@@ -142,29 +158,29 @@ struct Int8T {
                 for (int i = 0; i < 32; i++) v[i] = 0.f;
             }
             float mx = 0.f;
-            int bad = 0;
+            int bd = 0;
 #pragma unroll
             for (int i = 0; i < 32; i++) {
                 if (isfinite(v[i])) mx = fmaxf(mx, fabsf(v[i]));
-                else bad = 1;
+                else bd = 1;
             }
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
-            bad |= __shfl_xor_sync(0xffffffffu, bad, 2);
+            bd |= __shfl_xor_sync(0xffffffffu, bd, 1);
+            bd |= __shfl_xor_sync(0xffffffffu, bd, 2);
+            bad[hg] = bd;
             // slice scales s_j = s_0 / 254^j (the C side repeats these steps)
             float s = mx > 0.f ? mx * (1.0f / 127.0f) : 1.0f;
             float inv = mx > 0.f ? 127.0f / mx : 1.0f;
-            const float s0 = s;
+            s0[hg] = s;
             // slice j: c = round(v / s_j) with |v / s_j| <= 127 by construction
             // (|v| <= max|q| for j = 0, |residual| <= s_{j-1}/2 = 127 s_j after);
-            // adding 1.5*2^23 rounds to an integer held in the low mantissa bits,
+            // the residual after three slices is below 2^-23 of max|q|.  Adding
+            // 1.5*2^23 rounds to an integer held in the low mantissa bits,
             // whose low byte is the two's-complement code
             constexpr float kRound = 12582912.0f;
-            int colsum[2][kX];  // this lane's column (slice 2nb + (gid&1)), per scale group
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                uint32_t packed[8];
+            for (int j = 0; j < 3; j++) {
                 float sum[kX];
 #pragma unroll
                 for (int x = 0; x < kX; x++) sum[x] = 0.f;
@@ -180,49 +196,76 @@ struct Int8T {
                         sum[kB64 ? (i >> 4) : 0] += c;
                         bits[e] = __float_as_uint(r);
                     }
-                    packed[w] = prmt(prmt(bits[0], bits[1], 0x0040u), prmt(bits[2], bits[3], 0x0040u), 0x5410u);
+                    packed[hg][j][w] = prmt(prmt(bits[0], bits[1], 0x0040u), prmt(bits[2], bits[3], 0x0040u), 0x5410u);
                 }
-                if ((j & 1) == (gid & 1)) {
 #pragma unroll
-                    for (int kb = 0; kb < 4; kb++) {
-                        const int base = 4 * (kb >> 1) + 2 * (kb & 1);  // word index of dims base..base+7
-                        f.b[hg][j >> 1][kb][0] = packed[base];
-                        f.b[hg][j >> 1][kb][1] = packed[base + 1];
-                    }
-#pragma unroll
-                    for (int x = 0; x < kX; x++) colsum[j >> 1][x] = (int)sum[x];
+                for (int x = 0; x < kX; x++) {
+                    int cs = (int)sum[x];
+                    // over the head's 128 dims (the four tig lanes)
+                    cs += __shfl_xor_sync(0xffffffffu, cs, 1);
+                    cs += __shfl_xor_sync(0xffffffffu, cs, 2);
+                    colsum[hg][j][x] = cs;
                 }
                 s = s * (1.0f / 254.0f);
                 inv = inv * 254.0f;
             }
-            // column sums over the head's 128 dims (the four tig lanes)
+        }
+        // B column gid of n-block nb = C column e' = gid & 1 of the lanes with tig = gid >> 1
+        const int ep = gid & 1;
+        int cs_b[kNB][kX];
 #pragma unroll
-            for (int nb = 0; nb < 2; nb++)
+        for (int nb = 0; nb < kNB; nb++) {
+            const int hgb = ep ? col_hg(nb, 1) : col_hg(nb, 0);
+            const int slb = ep ? col_slice(nb, 1) : col_slice(nb, 0);
 #pragma unroll
-                for (int x = 0; x < kX; x++) {
-                    colsum[nb][x] += __shfl_xor_sync(0xffffffffu, colsum[nb][x], 1);
-                    colsum[nb][x] += __shfl_xor_sync(0xffffffffu, colsum[nb][x], 2);
-                }
-            // C side: columns 2tig (slice 2nb) and 2tig+1 (slice 2nb+1) of head
-            // 4hg+tig come from the lanes with gid = 2tig + e
+            for (int kb = 0; kb < 4; kb++) {
+                const int base = 4 * (kb >> 1) + 2 * (kb & 1);  // word index of dims base..base+7
+                uint32_t w0 = 0u, w1 = 0u;
 #pragma unroll
-            for (int nb = 0; nb < 2; nb++)
+                for (int hg = 0; hg < HG; hg++)
 #pragma unroll
-                for (int e = 0; e < 2; e++)
+                    for (int j = 0; j < 3; j++)
+                        if (hg == hgb && j == slb) { w0 = packed[hg][j][base]; w1 = packed[hg][j][base + 1]; }
+                f.b[nb][kb][0] = w0;
+                f.b[nb][kb][1] = w1;
+            }
 #pragma unroll
-                    for (int x = 0; x < kX; x++) {
-                        const int cs = __shfl_sync(0xffffffffu, colsum[nb][x], 8 * tig + 4 * e);
-                        f.magic[hg][x][2 * nb + e] = 0x4B400000u - (uint32_t)(128 * cs);
-                    }
-            const float hs0 = __shfl_sync(0xffffffffu, s0, 8 * tig);
-            const int hbad = __shfl_sync(0xffffffffu, bad, 8 * tig);
-            float sj = hs0;
+            for (int x = 0; x < kX; x++) {
+                int cs = 0;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                f.sc[hg][j] = hbad ? __int_as_float(0x7fffffff) : sj * A.scale_log2;
-                sj = sj * (1.0f / 254.0f);
+                for (int hg = 0; hg < HG; hg++)
+#pragma unroll
+                    for (int j = 0; j < 3; j++)
+                        if (hg == hgb && j == slb) cs = colsum[hg][j][x];
+                cs_b[nb][x] = cs;
             }
         }
+        // C side: column 2tig+e of n-block nb comes from the lanes with gid = 2tig + e
+#pragma unroll
+        for (int nb = 0; nb < kNB; nb++)
+#pragma unroll
+            for (int e = 0; e < 2; e++)
+#pragma unroll
+                for (int x = 0; x < kX; x++) {
+                    const int cs = __shfl_sync(0xffffffffu, cs_b[nb][x], 8 * tig + 4 * e);
+                    f.magic[x][2 * nb + e] = 0x4B400000u - (uint32_t)(128 * cs);
+                }
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            const float hs0 = __shfl_sync(0xffffffffu, s0[hg], 8 * tig);
+            const int hbad = __shfl_sync(0xffffffffu, bad[hg], 8 * tig);
+#pragma unroll
+            for (int nb = 0; nb < kNB; nb++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    if (col_hg(nb, e) != hg || col_slice(nb, e) < 0) continue;
+                    const float sj = col_slice(nb, e) == 0 ? hs0
+                                     : col_slice(nb, e) == 1 ? hs0 * (1.0f / 254.0f)
+                                                             : hs0 * (1.0f / 254.0f) * (1.0f / 254.0f);
+                    f.sc[2 * nb + e] = hbad ? __int_as_float(0x7fffffff) : sj * A.scale_log2;
+                }
+        }
+        if constexpr (HG == 1) f.sc[3] = 0.f;
 #pragma unroll
         for (int hg = 0; hg < HG; hg++) {
             st.m[hg] = -INFINITY;
@@ -264,43 +307,46 @@ struct Int8T {
         const bool full = t_lo == 0 && t_hi == 16;  // warp-uniform
         const bool ok0 = full || (gid >= t_lo && gid < t_hi);
         const bool ok1 = full || (gid + 8 >= t_lo && gid + 8 < t_hi);
-        // ---- scores
+        // ---- scores: kNB x 4 integer MMAs for all head groups
+        int acc[kNB][2][4];  // [n-block][k-block pair][c]
+#pragma unroll
+        for (int kb = 0; kb < 4; kb++)
+#pragma unroll
+            for (int nb = 0; nb < kNB; nb++) {
+                if (kb & 1)
+                    imma16832(acc[nb][kb >> 1], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3], f.b[nb][kb][0],
+                              f.b[nb][kb][1]);
+                else
+                    imma16832_z(acc[nb][kb >> 1], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3], f.b[nb][kb][0],
+                                f.b[nb][kb][1]);
+            }
         float s[HG][2];
 #pragma unroll
-        for (int hg = 0; hg < HG; hg++) {
-            int acc[2][2][4];  // [n-block][k-block pair][c]
+        for (int tk = 0; tk < 2; tk++) {
+            float raw[HG][kX];
 #pragma unroll
-            for (int kb = 0; kb < 4; kb++)
+            for (int hg = 0; hg < HG; hg++)
 #pragma unroll
-                for (int nb = 0; nb < 2; nb++) {
-                    if (kb & 1)
-                        imma16832(acc[nb][kb >> 1], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3], f.b[hg][nb][kb][0],
-                                  f.b[hg][nb][kb][1]);
-                    else
-                        imma16832_z(acc[nb][kb >> 1], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3],
-                                    f.b[hg][nb][kb][0], f.b[hg][nb][kb][1]);
+                for (int x = 0; x < kX; x++) raw[hg][x] = 0.f;
+#pragma unroll
+            for (int nb = 0; nb < kNB; nb++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    if (col_slice(nb, e) < 0) continue;
+                    const int hg = col_hg(nb, e), j = 2 * nb + e, c = 2 * tk + e;
+                    if constexpr (kB64) {
+                        raw[hg][0] = fmaf(small_int_to_float(acc[nb][0][c], f.magic[0][j]), f.sc[j], raw[hg][0]);
+                        raw[hg][kX - 1] =
+                            fmaf(small_int_to_float(acc[nb][1][c], f.magic[kX - 1][j]), f.sc[j], raw[hg][kX - 1]);
+                    } else {
+                        raw[hg][0] = fmaf(small_int_to_float(acc[nb][0][c] + acc[nb][1][c], f.magic[0][j]), f.sc[j],
+                                          raw[hg][0]);
+                    }
                 }
 #pragma unroll
-            for (int tk = 0; tk < 2; tk++) {
-                float raw[kX];
-#pragma unroll
-                for (int x = 0; x < kX; x++) raw[x] = 0.f;
-#pragma unroll
-                for (int nb = 0; nb < 2; nb++)
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const int c = 2 * tk + e, j = 2 * nb + e;
-                        if constexpr (kB64) {
-                            raw[0] = fmaf(small_int_to_float(acc[nb][0][c], f.magic[hg][0][j]), f.sc[hg][j], raw[0]);
-                            raw[kX - 1] =
-                                fmaf(small_int_to_float(acc[nb][1][c], f.magic[hg][kX - 1][j]), f.sc[hg][j], raw[kX - 1]);
-                        } else {
-                            raw[0] = fmaf(small_int_to_float(acc[nb][0][c] + acc[nb][1][c], f.magic[hg][0][j]),
-                                          f.sc[hg][j], raw[0]);
-                        }
-                    }
-                float sc = raw[0] * ks[0][tk];
-                if constexpr (kB64) sc = fmaf(raw[kX - 1], ks[kX - 1][tk], sc);
+            for (int hg = 0; hg < HG; hg++) {
+                float sc = raw[hg][0] * ks[0][tk];
+                if constexpr (kB64) sc = fmaf(raw[hg][kX - 1], ks[kX - 1][tk], sc);
                 s[hg][tk] = (tk ? ok1 : ok0) ? sc : -INFINITY;
             }
         }
