@@ -160,10 +160,11 @@ def global_lengths(wl: dict, n_gpus: int) -> np.ndarray:
 # ---------------------------------------------------------------------------
 # reference arm: the reference's own CPU code (oracle/_ref), bounded sample
 # ---------------------------------------------------------------------------
-def reference_rate(wl: dict, lens: np.ndarray, steps: int, warmup: int, layers_sample: int):
+def reference_rate(wl: dict, lens: np.ndarray, steps: int, warmup: int, layers_sample: int, threads: int = 0):
     """Decode steps of the reference CPU path on `lens` over the first
-    `layers_sample` layers; returns (seq-steps/s scaled to all layers,
-    seconds per sampled step, threads, codec name)."""
+    `layers_sample` layers with `threads` OpenMP threads (0 = every host
+    core); returns (seq-steps/s scaled to all layers, seconds per sampled
+    step, threads, codec name)."""
     import ctypes as C
     from oracle import oracle as O
     R = O.ref()
@@ -173,7 +174,7 @@ def reference_rate(wl: dict, lens: np.ndarray, steps: int, warmup: int, layers_s
     # every host core: torchrun sets OMP_NUM_THREADS=1 in its workers, so the
     # thread count is set explicitly (the affinity mask bounds it)
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
-    R.qref_set_threads(cores)
+    R.qref_set_threads(threads if threads > 0 else cores)
     ids = np.ascontiguousarray(lens, dtype=np.int32)
     h = R.qref_batch_create(codec, ids.size, ids.ctypes.data_as(C.POINTER(C.c_int32)), layers_sample,
                             wl["H"], wl["HK"], HD, steps + warmup + 1, wl["seed"])
@@ -188,6 +189,18 @@ def reference_rate(wl: dict, lens: np.ndarray, steps: int, warmup: int, layers_s
     R.qref_batch_destroy(h)
     rate = ids.size / (dt * wl["layers"] / layers_sample)
     return rate, dt, int(R.qref_max_threads()), ("q8_b64_f32" if codec == 1 else "tq35_g64")
+
+
+def one_thread_row(wl, lens: np.ndarray, steps: int, unit: str, what: str):
+    """The reference CPU path on one thread (the 1-thread row next to the
+    all-cores baseline), one sampled layer."""
+    res = reference_rate(wl, lens, steps, 0, 1, threads=1)
+    if not res:
+        return None
+    rate, dt, threads, cname = res
+    return {"value": rate, "unit": unit, "cores": threads, "kind": "reference",
+            "sample": f"{what}, first 1 of {wl['layers']} layers, {steps} timed step(s) on one thread, "
+                      f"scaled x{wl['layers']:g}; reference codec {cname}"}
 
 
 def run_reference(args, wl, world, rank):
@@ -406,6 +419,8 @@ def run_ours(args, wl, world, rank, local):
                                     "sample": f"{len(lens)} sequences (same lengths), first {ls} of {L} layers, "
                                               f"{2 if L > 1 else 20} timed steps, scaled x{L / ls:g}; "
                                               f"reference codec {cname}"}
+            line["cpu_baseline"]["one_thread"] = one_thread_row(wl, lens, 1 if L > 1 else 20, "seq-steps/s",
+                                                                f"{len(lens)} sequences")
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
@@ -588,6 +603,8 @@ def run_split(args, wl, world, rank, local):
                 rate, dt, threads, cname = res
                 line["cpu_baseline"] = {"value": rate, "unit": "layer-steps/s", "cores": threads, "kind": "reference",
                                         "sample": f"1 sequence of {c0} tokens, 3 timed steps; reference codec {cname}"}
+                line["cpu_baseline"]["one_thread"] = one_thread_row(wl, np.array([c0], np.int32), 1, "layer-steps/s",
+                                                                    f"1 sequence of {c0} tokens")
         print(json.dumps(line), flush=True)
     return 0
 
@@ -711,6 +728,8 @@ def run_churn(args, wl, world, rank, local):
                 line["cpu_baseline"] = {"value": rate, "unit": "seq-steps/s", "cores": threads, "kind": "reference",
                                         "sample": f"{B} sequences (same lengths), append + attend, 2 timed steps, "
                                                   f"no eviction; reference codec {cname}"}
+                line["cpu_baseline"]["one_thread"] = one_thread_row(wl, lens.astype(np.int32), 1, "seq-steps/s",
+                                                                    f"{B} sequences, append + attend, no eviction")
         print(json.dumps(line), flush=True)
     return 0
 
