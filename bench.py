@@ -61,7 +61,26 @@ def workload(cfg: int) -> dict:
 
 
 def kv_bytes(codec: int) -> int:
-    return {1: 272, 2: 260, 3: 128, 4: 160}[codec]
+    return {1: 272, 2: 260, 3: 128, 4: 160, 5: 512}[codec]
+
+
+def dtype_of(codec: int) -> str:
+    return {1: "int8", 2: "int8", 3: "u4", 4: "u4", 5: "f16"}[codec]
+
+
+CODEC_LABEL = {1: "int8 per 64 channels + fp32 scale", 2: "int8 per-token-head KV + fp16 scale",
+               3: "TurboQuant 3.5-bit groups of 64", 4: "4-bit KV groups of 32 (fp16 range+min)",
+               5: "fp16 KV (the reference's paged pool format)"}
+
+
+def with_codec(wl: dict, codec: int) -> dict:
+    """The workload with another KV codec (--codec): same shapes and inputs."""
+    if not codec or codec == wl["codec"]:
+        return wl
+    wl = dict(wl)
+    wl["name"] = wl["name"].split(",")[0] + f", {CODEC_LABEL[codec]} (codec override)"
+    wl["codec"] = codec
+    return wl
 
 
 def profiled_traffic(cfg: int):
@@ -170,7 +189,9 @@ def reference_rate(wl: dict, lens: np.ndarray, steps: int, warmup: int, layers_s
     R = O.ref()
     if R is None:
         return None
-    codec = 1 if wl["codec"] in (1, 2) else 3  # the reference CPU has only its own codecs
+    # the reference CPU has only its own codecs: its Q8 for the int8 codecs,
+    # TurboQuant for the low-bit ones, its fp16 paged pool for fp16
+    codec = {1: 1, 2: 1, 3: 3, 4: 3, 5: 5}[wl["codec"]]
     # every host core: torchrun sets OMP_NUM_THREADS=1 in its workers, so the
     # thread count is set explicitly (the affinity mask bounds it)
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
@@ -188,7 +209,7 @@ def reference_rate(wl: dict, lens: np.ndarray, steps: int, warmup: int, layers_s
     dt = (time.perf_counter() - t0) / steps
     R.qref_batch_destroy(h)
     rate = ids.size / (dt * wl["layers"] / layers_sample)
-    return rate, dt, int(R.qref_max_threads()), ("q8_b64_f32" if codec == 1 else "tq35_g64")
+    return rate, dt, int(R.qref_max_threads()), {1: "q8_b64_f32", 3: "tq35_g64", 5: "f16_paged"}[codec]
 
 
 def one_thread_row(wl, lens: np.ndarray, steps: int, unit: str, what: str):
@@ -218,7 +239,7 @@ def run_reference(args, wl, world, rank):
               f"(time scaled x{wl['layers'] / layers_sample:g}), reference codec {cname}")
     line = {"metric": METRIC, "value": rate, "unit": "seq-steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * dt * wl["layers"] / layers_sample,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_of(wl["codec"]),
             "data": "synthetic", "impl": "reference",
             "config": {"workload": wl["name"], "global_batch": int(lens.size), "layers": wl["layers"],
                        "query_heads": wl["H"], "kv_heads": wl["HK"], "head_dim": HD, "page_tokens": wl["P"],
@@ -380,11 +401,11 @@ def run_ours(args, wl, world, rank, local):
     if rank == 0:
         clocks = sampler.summary(t_wall0 - 0.05, t_wall1 + 0.05)
         # the capture covers one GPU's full cfg batch; other shapes report none
-        traffic = profiled_traffic(args.config) if world == 1 and not args.batch else None
+        traffic = profiled_traffic(args.config) if world == 1 and not args.batch and not args.codec else None
         line = {
             "metric": METRIC, "value": value, "unit": "seq-steps/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8" if wl["codec"] in (1, 2) else "u4", "data": "synthetic",
+            "dtype": dtype_of(wl["codec"]), "data": "synthetic",
             "config": {"workload": wl["name"], "global_batch": int(B * world), "per_gpu_batch": int(B),
                        "layers": L, "query_heads": H, "kv_heads": HK, "head_dim": HD, "page_tokens": P,
                        "context": f"U[{wl['lo']},{wl['hi']}] (+{W} warmup tokens)",
@@ -431,11 +452,11 @@ def _finish_line(args, wl, world, rank, value, ms_step, attn_bytes, attn_ms, att
     peak, peak_kind = peaks()
     achieved = attn_bytes / (attn_ms / 1000.0) / 1e9 if attn_ms > 0 else 0.0
     # the committed capture covers the 1-GPU launch of this workload only
-    traffic = profiled_traffic(args.config) if world == 1 else None
+    traffic = profiled_traffic(args.config) if world == 1 and not args.codec else None
     line = {
         "metric": METRIC, "value": value, "unit": "seq-steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling,
-        "vs_baseline": None, "dtype": "int8" if wl["codec"] in (1, 2) else "u4", "data": "synthetic",
+        "vs_baseline": None, "dtype": dtype_of(wl["codec"]), "data": "synthetic",
         "config": dict({"workload": wl["name"], "layers": wl["layers"], "query_heads": wl["H"],
                         "kv_heads": wl["HK"], "head_dim": HD, "page_tokens": wl["P"]}, **extra_config),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -744,6 +765,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--ring", type=int, default=8, help="distinct input step buffers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--codec", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
+                    help="run the config's shapes with another KV codec (5 = fp16, the reference's paged pool)")
     ap.add_argument("--soak-ms", type=float, default=1500.0,
                     help="cfg4/cfg5: keep the GPU on the workload after the timed steps until the clock samples "
                          "cover this long (0 for profiling runs)")
@@ -754,7 +777,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3  # the timing rules want >= 3 warm-up steps
-    wl = workload(args.config)
+    wl = with_codec(workload(args.config), args.codec)
     if not args.steps:
         args.steps = wl.get("steps", 20)
     if args.layers:

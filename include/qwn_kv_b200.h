@@ -52,7 +52,9 @@ typedef enum {
     QWN_KV_CODEC_Q8_B64_F32 = 1,  /* reference Q8: fp32 scale per 64 channels */
     QWN_KV_CODEC_Q8_HEAD_F16 = 2, /* int8 per token-head, fp16 absmax scale */
     QWN_KV_CODEC_TQ35_G64 = 3,    /* reference TurboQuant 4/3-bit, groups of 64 */
-    QWN_KV_CODEC_Q4_G32 = 4       /* 4-bit, groups of 32, fp16 range + fp16 min */
+    QWN_KV_CODEC_Q4_G32 = 4,      /* 4-bit, groups of 32, fp16 range + fp16 min */
+    QWN_KV_CODEC_F16 = 5          /* fp16 K and V, round to nearest even: the reference's paged
+                                     pool (qwn_paged_kv_write, c/qwn_paged_kv.c:151-198) */
 } QwnKvCodec;
 
 /* device status bits latched by kernels */

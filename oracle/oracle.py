@@ -24,8 +24,9 @@ CODEC_Q8_B64_F32 = 1
 CODEC_Q8_HEAD_F16 = 2
 CODEC_TQ35_G64 = 3
 CODEC_Q4_G32 = 4
-CODEC_NAMES = {1: "q8_b64_f32", 2: "q8_head_f16", 3: "tq35_g64", 4: "q4_g32"}
-TILE_BYTES = {1: 4352, 2: 4160, 3: 2048, 4: 2560}
+CODEC_F16 = 5
+CODEC_NAMES = {1: "q8_b64_f32", 2: "q8_head_f16", 3: "tq35_g64", 4: "q4_g32", 5: "f16"}
+TILE_BYTES = {1: 4352, 2: 4160, 3: 2048, 4: 2560, 5: 8192}
 
 _lib = None
 _ref = None
@@ -142,6 +143,7 @@ def lib():
         _decl(L, "qor_q4g32_quantize", None, f32p, C.c_int, u8p, u16p, u16p)
         _decl(L, "qor_tile_bytes", C.c_size_t, C.c_int)
         _decl(L, "qor_tile_store", None, C.c_int, u8p, C.c_int, f32p, f32p)
+        _decl(L, "qor_tile_dequant", C.c_float, C.c_int, u8p, C.c_int, C.c_int, C.c_int)
         _decl(L, "qor_tile_load", None, C.c_int, u8p, C.c_int, C.c_int, i16p, f32p)
         _decl(L, "qor_pool_init", C.c_int, C.POINTER(QorPool), C.c_int, C.c_int, C.c_int,
               C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64)
@@ -211,6 +213,8 @@ def ref():
             _decl(R, "qref_batch_destroy", None, C.c_void_p)
             _decl(R, "qref_max_threads", C.c_int)
             _decl(R, "qref_set_threads", None, C.c_int)
+            _decl(R, "qref_f16_write", C.c_int, f32p, f32p, C.c_int, C.c_int, C.POINTER(C.c_uint16),
+                  C.POINTER(C.c_uint16))
             _ref = R
     return _ref
 

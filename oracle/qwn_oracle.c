@@ -79,13 +79,15 @@ void qor_outlier_channels(uint64_t seed, uint32_t layer, int channels, int count
 static uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 static float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
 
-/* IEEE binary32 -> binary16, round to nearest even, with subnormals. */
+/* IEEE binary32 -> binary16, round to nearest even, with subnormals; a NaN
+ * stays a quiet NaN with the top ten payload bits, as the F16C conversion
+ * the reference's fp16 pool write uses (_mm256_cvtps_ph). */
 uint16_t qor_f32_to_f16_rne(float f) {
     uint32_t x = f2u(f);
     uint32_t sign = (x >> 16) & 0x8000u;
     uint32_t absx = x & 0x7FFFFFFFu;
     if (absx >= 0x7F800000u) /* inf or nan */
-        return (uint16_t)(sign | 0x7C00u | (absx > 0x7F800000u ? 0x200u : 0u));
+        return (uint16_t)(sign | 0x7C00u | (absx > 0x7F800000u ? (0x200u | ((absx >> 13) & 0x3FFu)) : 0u));
     if (absx >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u); /* >= 65520 */
     if (absx < 0x33000001u) return (uint16_t)sign;              /* <= 2^-25 */
     int e = (int)(absx >> 23) - 127;
@@ -323,6 +325,10 @@ void qor_q4g32_quantize(const float *src, int n, uint8_t *codes, uint16_t *range
  *    4*group, odd word at 512 + 16t + 4tig, plane u16 at 768 + 8t + 2tig.
  *    V: even word e = 2*group + (mb&1) at 16*lane + 4e, odd word k = mb&1 at
  *    512 + 8*lane + 4k, plane u16 at 768 + 4*lane + 2k.
+ *  - fp16 (codec 5, 8192 B): K [0,4096), V [4096,8192), each row t of 256
+ *    bytes holds dims 0..127 as fp16 (RNE), 16-byte chunk c = d>>3 stored
+ *    at position c xor (t&7), so that ldmatrix reads eight rows without bank
+ *    conflicts.
  */
 
 size_t qor_tile_bytes(int codec) {
@@ -331,6 +337,7 @@ size_t qor_tile_bytes(int codec) {
         case QOR_CODEC_Q8_HEAD_F16: return 4160;
         case QOR_CODEC_TQ35_G64: return 2048;
         case QOR_CODEC_Q4_G32: return 2560;
+        case QOR_CODEC_F16: return 8192;
         default: return 0;
     }
 }
@@ -344,6 +351,11 @@ static size_t v8_off(int t, int d) {
     int chunk = (mb >> 1) ^ ((lane >> 1) & 3);
     int e = 4 * (t >> 3) + 2 * (r >> 3) + (t & 1);
     return 2048 + (size_t)lane * 64 + (size_t)chunk * 16 + (size_t)(8 * (mb & 1) + e);
+}
+
+/* fp16 element (t, d) of the K (is_value 0) or V half */
+static size_t f16_off(int is_value, int t, int d) {
+    return (size_t)is_value * 4096 + (size_t)t * 256 + (size_t)((((d >> 3) ^ (t & 7))) << 4) + (size_t)(d & 7) * 2;
 }
 
 /* int8 scale positions (see the layout notes above) */
@@ -451,6 +463,13 @@ static uint8_t tq_load_code(const uint8_t *half, int is_value, int t, int d) {
 
 void qor_tile_store(int codec, uint8_t *tile, int t, const float *k, const float *v) {
     const int HD = QOR_HEAD_DIM;
+    if (codec == QOR_CODEC_F16) { /* c/qwn_paged_kv.c:151-198: fp32 -> fp16 RNE */
+        for (int d = 0; d < HD; d++) {
+            put_u16(tile + f16_off(0, t, d), qor_f32_to_f16_rne(k[d]));
+            put_u16(tile + f16_off(1, t, d), qor_f32_to_f16_rne(v[d]));
+        }
+        return;
+    }
     if (codec == QOR_CODEC_Q8_B64_F32 || codec == QOR_CODEC_Q8_HEAD_F16) {
         int8_t ck[HD], cv[HD];
         if (codec == QOR_CODEC_Q8_B64_F32) {
@@ -543,6 +562,7 @@ void qor_tile_load(int codec, const uint8_t *tile, int t, int is_value, int16_t 
 }
 
 float qor_tile_dequant(int codec, const uint8_t *tile, int t, int is_value, int d) {
+    if (codec == QOR_CODEC_F16) return qor_f16_to_f32(get_u16(tile + f16_off(is_value, t, d)));
     int16_t codes[128];
     float params[8];
     qor_tile_load(codec, tile, t, is_value, codes, params);
@@ -654,6 +674,11 @@ static const uint8_t *ctile(const QorPool *p, int seq, int layer, int kv, int po
  *  Q8 (c/qwanto_turboquant.c:648-662): total += q[i] * (code * scale)
  *  TurboQuant scalar (:218-252): per group block_dot += q*(code*s+zp); total += block_dot */
 static float token_dot(const QorPool *p, const uint8_t *tile, int t, const float *q) {
+    if (p->codec == QOR_CODEC_F16) { /* c/qwn_paged_kv.c:338-355: dot of q with the fp16 row */
+        float total = 0.0f;
+        for (int i = 0; i < 128; i++) total += q[i] * qor_f16_to_f32(get_u16(tile + f16_off(0, t, i)));
+        return total;
+    }
     int16_t c[128];
     float par[8];
     qor_tile_load(p->codec, tile, t, 0, c, par);
@@ -680,6 +705,10 @@ static float token_dot(const QorPool *p, const uint8_t *tile, int t, const float
 }
 
 static void token_value(const QorPool *p, const uint8_t *tile, int t, float *v) {
+    if (p->codec == QOR_CODEC_F16) {
+        for (int i = 0; i < 128; i++) v[i] = qor_f16_to_f32(get_u16(tile + f16_off(1, t, i)));
+        return;
+    }
     int16_t c[128];
     float par[8];
     qor_tile_load(p->codec, tile, t, 1, c, par);

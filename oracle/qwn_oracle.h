@@ -34,7 +34,8 @@ enum {
     QOR_CODEC_Q8_B64_F32 = 1,  /* reference Q8: int8, fp32 scale per 64 channels */
     QOR_CODEC_Q8_HEAD_F16 = 2, /* int8 per token-head, fp16 absmax scale */
     QOR_CODEC_TQ35_G64 = 3,    /* reference TurboQuant: 4/3-bit alternating, groups of 64 */
-    QOR_CODEC_Q4_G32 = 4       /* 4-bit, groups of 32, fp16 range + fp16 min */
+    QOR_CODEC_Q4_G32 = 4,      /* 4-bit, groups of 32, fp16 range + fp16 min */
+    QOR_CODEC_F16 = 5          /* fp16 K and V, the reference's paged pool format */
 };
 
 #define QOR_HEAD_DIM 128   /* the paged layout is defined for head_dim 128 */

@@ -20,9 +20,10 @@
 
 #include "qwanto_turboquant.h"
 #include "qwn_oracle.h"
+#include "qwn_paged_kv.h"
 
 typedef struct {
-    int codec; /* 1 = reference Q8, 3 = reference TurboQuant */
+    int codec; /* 1 = reference Q8, 3 = reference TurboQuant, 5 = reference fp16 paged pool */
     int nseq, layers, heads, kv_heads, head_dim;
     uint64_t seed;
     int32_t *lens;            /* current tokens per sequence */
@@ -31,7 +32,16 @@ typedef struct {
     float *q, *k, *v, *ctx;   /* per-sequence scratch rows */
     float *scores;            /* [nseq*heads][max_ctx] */
     int max_ctx;
+    /* codec 5: the decoder's fp16 paged path (c/qwanto_decode.c:1600-1604,
+     * :1807-1835): one block pool, a block table per sequence, per-thread
+     * gather scratch */
+    QwnKVBlockPool fpool;
+    QwnBlockTable *bt;
+    uint16_t *kg, *vg;
+    int nthreads;
 } QrefBatch;
+
+void qref_batch_destroy(void *handle);
 
 static void gen_row(uint64_t seed, uint32_t kind, int seq, int layer, int pos, int width,
                     float *out) {
@@ -41,6 +51,7 @@ static void gen_row(uint64_t seed, uint32_t kind, int seq, int layer, int pos, i
 
 static int append_token(QrefBatch *b, int s, int l, int pos, const float *k, const float *v) {
     int KV = b->kv_heads * b->head_dim;
+    if (b->codec == 5) return qwn_paged_kv_write(&b->fpool, &b->bt[s], l, pos, k, v);
     if (b->codec == 1) return qwn_q8_cache_append(&b->q8[(size_t)s * b->layers + l], k, v, KV);
     TurboQuantCache *c = &b->tq[(size_t)s * b->layers + l];
     int bph = (b->head_dim + TURBOQUANT_GROUP_SIZE - 1) / TURBOQUANT_GROUP_SIZE;
@@ -67,7 +78,7 @@ void *qref_batch_create(int codec, int nseq, const int32_t *lens, int layers, in
     b->max_ctx = maxlen + max_new;
     size_t nc = (size_t)nseq * (size_t)layers;
     if (codec == 1) b->q8 = (QwnQ8Cache *)calloc(nc, sizeof(QwnQ8Cache));
-    else b->tq = (TurboQuantCache *)calloc(nc, sizeof(TurboQuantCache));
+    else if (codec == 3) b->tq = (TurboQuantCache *)calloc(nc, sizeof(TurboQuantCache));
     int KV = kv_heads * head_dim;
     b->q = (float *)malloc(sizeof(float) * (size_t)nseq * heads * head_dim);
     b->k = (float *)malloc(sizeof(float) * (size_t)nseq * KV);
@@ -75,13 +86,29 @@ void *qref_batch_create(int codec, int nseq, const int32_t *lens, int layers, in
     b->ctx = (float *)malloc(sizeof(float) * (size_t)nseq * heads * head_dim);
     b->scores = (float *)malloc(sizeof(float) * (size_t)nseq * heads * (size_t)b->max_ctx);
     int fail = 0;
-    for (int s = 0; s < nseq && !fail; s++)
+    if (codec == 5) {
+        int blocks = 0;
+        for (int s = 0; s < nseq; s++) blocks += (lens[s] + max_new + QWN_PAGE_BLOCK_SIZE - 1) / QWN_PAGE_BLOCK_SIZE;
+        b->bt = (QwnBlockTable *)calloc((size_t)nseq, sizeof(QwnBlockTable));
+        fail = !b->bt || qwn_kv_pool_init(&b->fpool, blocks + nseq, layers, kv_heads, head_dim) != 0;
+        /* the blocks of every prefill token, in sequence order (the pool's
+         * LIFO free stack is not thread-safe) */
+        for (int s = 0; s < nseq && !fail; s++) {
+            fail = qwn_block_table_init(&b->bt[s], s, (b->lens[s] + max_new) / QWN_PAGE_BLOCK_SIZE + 1) != 0;
+            for (int t = 0; t < lens[s] && !fail; t++) fail = qwn_block_table_append_token(&b->fpool, &b->bt[s]) != 0;
+        }
+        b->nthreads = omp_get_max_threads();
+        b->kg = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)b->nthreads * b->max_ctx * head_dim);
+        b->vg = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)b->nthreads * b->max_ctx * head_dim);
+        fail = fail || !b->kg || !b->vg;
+    }
+    for (int s = 0; s < nseq && !fail && codec != 5; s++)
         for (int l = 0; l < layers && !fail; l++) {
             int cap = lens[s] + max_new;
             if (codec == 1) fail = qwn_q8_cache_init(&b->q8[(size_t)s * layers + l], cap, kv_heads, head_dim) != 0;
             else fail = qwn_turboquant_init(&b->tq[(size_t)s * layers + l], cap, kv_heads, head_dim) != 0;
         }
-    if (fail) return NULL;
+    if (fail) { qref_batch_destroy(b); return NULL; }
     /* prefill: tokens [0, len) of every (sequence, layer), parallel over caches */
     #pragma omp parallel
     {
@@ -108,6 +135,9 @@ int qref_batch_step(void *handle, int layers_run) {
     int H = b->heads, HK = b->kv_heads, HD = b->head_dim, KV = HK * HD;
     float ratio = (float)H / (float)HK;
     float scale = 1.0f / sqrtf((float)HD);
+    if (b->codec == 5) /* one block-table append per token, before the layers */
+        for (int s = 0; s < b->nseq; s++)
+            if (qwn_block_table_append_token(&b->fpool, &b->bt[s]) != 0) return -1;
     for (int l = 0; l < layers_run && l < b->layers; l++) {
         /* inputs of this step (position = current length) */
         #pragma omp parallel for schedule(static)
@@ -126,7 +156,11 @@ int qref_batch_step(void *handle, int layers_run) {
             float *sc = b->scores + (size_t)w * b->max_ctx;
             const float *qh = b->q + ((size_t)s * H + h) * HD;
             float *out = b->ctx + ((size_t)s * H + h) * HD;
-            if (b->codec == 1)
+            if (b->codec == 5) {
+                size_t g = (size_t)omp_get_thread_num() * b->max_ctx * HD;
+                qwn_paged_attention_gather_head(&b->fpool, &b->bt[s], l, h, (h * HK) / H, qh, b->kg + g,
+                                                b->vg + g, sc, out);
+            } else if (b->codec == 1)
                 qwn_q8_cache_attention_head(qh, &b->q8[(size_t)s * b->layers + l], kh, pos, scale, sc, out);
             else
                 qwn_turboquant_attention_head(qh, &b->tq[(size_t)s * b->layers + l], l, h, kh, pos,
@@ -147,8 +181,38 @@ void qref_batch_destroy(void *handle) {
         if (b->q8) qwn_q8_cache_free(&b->q8[c]);
         if (b->tq) qwn_turboquant_free(&b->tq[c]);
     }
+    if (b->bt) {
+        for (int s = 0; s < b->nseq; s++) qwn_block_table_free(&b->fpool, &b->bt[s]);
+        free(b->bt);
+    }
+    if (b->codec == 5) qwn_kv_pool_free(&b->fpool);
+    free(b->kg); free(b->vg);
     free(b->q8); free(b->tq); free(b->lens); free(b->q); free(b->k); free(b->v);
     free(b->ctx); free(b->scores); free(b);
+}
+
+/* The reference's fp16 pool write (c/qwn_paged_kv.c:151-198) of n token-head
+ * rows of head_dim values: k/v [n][head_dim] fp32 -> k16/v16 [n][head_dim]
+ * fp16 bits, read back from a one-block pool (n <= 16).  Pins the oracle's
+ * fp32 -> fp16 rounding. */
+int qref_f16_write(const float *k, const float *v, int n, int head_dim, uint16_t *k16, uint16_t *v16) {
+    if (n <= 0 || n > QWN_PAGE_BLOCK_SIZE) return -1;
+    QwnKVBlockPool pool;
+    QwnBlockTable bt;
+    if (qwn_kv_pool_init(&pool, 1, 1, 1, head_dim) != 0) return -1;
+    int rc = qwn_block_table_init(&bt, 0, 1);
+    for (int t = 0; t < n && rc == 0; t++) rc = qwn_block_table_append_token(&pool, &bt);
+    for (int t = 0; t < n && rc == 0; t++)
+        rc = qwn_paged_kv_write(&pool, &bt, 0, t, k + (size_t)t * head_dim, v + (size_t)t * head_dim);
+    if (rc == 0) {
+        int blk = bt.block_ids[0];
+        size_t base = (size_t)blk * QWN_PAGE_BLOCK_SIZE * head_dim;
+        memcpy(k16, pool.key_data + base, sizeof(uint16_t) * (size_t)n * head_dim);
+        memcpy(v16, pool.val_data + base, sizeof(uint16_t) * (size_t)n * head_dim);
+    }
+    qwn_block_table_free(&pool, &bt);
+    qwn_kv_pool_free(&pool);
+    return rc;
 }
 
 int qref_max_threads(void) { return omp_get_max_threads(); }

@@ -22,16 +22,17 @@ import ctypes as C
 import numpy as np
 
 from . import _lib
-from ._lib import (CODEC_Q4_G32, CODEC_Q8_B64_F32, CODEC_Q8_HEAD_F16, CODEC_TQ35_G64, QwnCudaError, check,
+from ._lib import (CODEC_F16, CODEC_Q4_G32, CODEC_Q8_B64_F32, CODEC_Q8_HEAD_F16, CODEC_TQ35_G64, QwnCudaError, check,
                    init, lib)
 
 __all__ = ["CudaContext", "KvPool", "lib", "QwnCudaError", "generate_rows", "merge_partials",
-           "CODEC_Q8_B64_F32", "CODEC_Q8_HEAD_F16", "CODEC_TQ35_G64", "CODEC_Q4_G32", "launch_count", "merge_partials_packed"]
+           "CODEC_Q8_B64_F32", "CODEC_Q8_HEAD_F16", "CODEC_TQ35_G64", "CODEC_Q4_G32", "CODEC_F16", "launch_count", "merge_partials_packed"]
 
-TILE_BYTES = {CODEC_Q8_B64_F32: 4352, CODEC_Q8_HEAD_F16: 4160, CODEC_TQ35_G64: 2048, CODEC_Q4_G32: 2560}
+TILE_BYTES = {CODEC_Q8_B64_F32: 4352, CODEC_Q8_HEAD_F16: 4160, CODEC_TQ35_G64: 2048, CODEC_Q4_G32: 2560,
+              CODEC_F16: 8192}
 # per token-head K+V bytes at head_dim 128 (the roofline's algorithmic bytes)
 KV_BYTES_PER_TOKEN_HEAD = {CODEC_Q8_B64_F32: 272, CODEC_Q8_HEAD_F16: 260, CODEC_TQ35_G64: 128,
-                           CODEC_Q4_G32: 160}
+                           CODEC_Q4_G32: 160, CODEC_F16: 512}
 
 
 def _ptr(x) -> int | None:

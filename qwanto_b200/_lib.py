@@ -20,6 +20,7 @@ CODEC_Q8_B64_F32 = 1
 CODEC_Q8_HEAD_F16 = 2
 CODEC_TQ35_G64 = 3
 CODEC_Q4_G32 = 4
+CODEC_F16 = 5
 
 CAP_HYPERVSQ2_GEMV = 1 << 0
 CAP_Q8_KV = 1 << 5

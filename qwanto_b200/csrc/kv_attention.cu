@@ -995,6 +995,212 @@ struct LowBitT {
 };
 
 // ---------------------------------------------------------------------------
+// fp16 codec (F16, the reference's paged pool format): the int8 structure
+// without quantisation.  QK^T on the f16 tensor cores (m16n8k16) with the K
+// rows as A, loaded by ldmatrix from the swizzled tile, and the query as B in
+// two f16 parts per head (hi + lo of the query pre-scaled by log2(e) x the
+// softmax scale and by a power of two that keeps it within [-1, 1]):
+// columns (head, part), products exact in fp32, 8 MMAs per tile and head
+// group.  P x V as in Int8T with V^T loaded by ldmatrix.trans and P^T as
+// f16 hi/lo pairs through movmatrix; V needs no scale.
+// ---------------------------------------------------------------------------
+template <int HG>
+struct F16T {
+    static constexpr int kBytes = 8192, kStages = HG == 1 ? 2 : 3;
+    static constexpr int kTilesPerStep = 1;
+    struct Frag {
+        uint32_t b[HG][8][2];  // B: [head group][k-block of 16 dims][reg]
+        float sq[HG];          // the power of two of the lane's head (C side)
+    };
+    struct State {
+        float o[HG][8][4];  // (dims x (head, hi/lo)) accumulators per m-block
+        float m[HG], l[HG];
+    };
+
+    __device__ static void begin(Frag &f, State &st, const AttnArgs &A, uint32_t s_idx) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        const uint32_t G = A.group;
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            const uint32_t hq = 4 * hg + (gid >> 1);
+            // dims 16kb + 2tig + {0, 1, 8, 9} of the lane's head
+            float v[32];
+            if (hq < G) {
+                const float *q = A.query + ((size_t)s_idx * G + hq) * kHeadDim;
+#pragma unroll
+                for (int kb = 0; kb < 8; kb++) {
+                    const float2 x0 = *reinterpret_cast<const float2 *>(q + 16 * kb + 2 * tig);
+                    const float2 x1 = *reinterpret_cast<const float2 *>(q + 16 * kb + 8 + 2 * tig);
+                    v[4 * kb] = x0.x; v[4 * kb + 1] = x0.y; v[4 * kb + 2] = x1.x; v[4 * kb + 3] = x1.y;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) v[i] = 0.f;
+            }
+            float mx = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                v[i] *= A.scale_log2;
+                if (isfinite(v[i])) mx = fmaxf(mx, fabsf(v[i]));
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float sq = mx > 0.f ? pow2ceil(mx) : 1.0f;
+            const float inv = 1.0f / sq;  // a power of two: exact
+            const bool lo = gid & 1;      // B column gid = (head gid>>1, part gid&1)
+#pragma unroll
+            for (int kb = 0; kb < 8; kb++) {
+                uint32_t w[2];
+#pragma unroll
+                for (int r = 0; r < 2; r++) {
+                    const float y0 = v[4 * kb + 2 * r] * inv, y1 = v[4 * kb + 2 * r + 1] * inv;
+                    const __half2 h = __floats2half2_rn(y0, y1);
+                    const float2 hf = __half22float2(h);
+                    const __half2 l2 = __floats2half2_rn(y0 - hf.x, y1 - hf.y);
+                    w[r] = lo ? *reinterpret_cast<const uint32_t *>(&l2) : *reinterpret_cast<const uint32_t *>(&h);
+                }
+                f.b[hg][kb][0] = w[0];
+                f.b[hg][kb][1] = w[1];
+            }
+            // C side: this lane's head 4hg + tig is held by the lanes gid = 2tig
+            f.sq[hg] = __shfl_sync(0xffffffffu, sq, 8 * tig);
+            st.m[hg] = -INFINITY;
+            st.l[hg] = 0.f;
+#pragma unroll
+            for (int mb = 0; mb < 8; mb++) st.o[hg][mb][0] = st.o[hg][mb][1] = st.o[hg][mb][2] = st.o[hg][mb][3] = 0.f;
+        }
+    }
+
+    __device__ static void step(const uint8_t *tile, const Frag &f, State &st, int t_lo, int t_hi,
+                                float (&psum)[HG]) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        // ---- scores: A = K rows; ldmatrix lane l gives row (l&7) of matrix
+        // l>>3 = (tokens 8*(m&1).., dims 8*(2kb + (m>>1))..)
+        const int krow = (lane & 7) + 8 * ((lane >> 3) & 1), kch = lane >> 4;
+        float acc[HG][4];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) acc[hg][0] = acc[hg][1] = acc[hg][2] = acc[hg][3] = 0.f;
+#pragma unroll
+        for (int kb = 0; kb < 8; kb++) {
+            uint32_t a[4];
+            ldmatrix_x4(a, tile + krow * 256 + ((((2 * kb + kch) ^ (krow & 7))) << 4));
+#pragma unroll
+            for (int hg = 0; hg < HG; hg++) mma16816(acc[hg], a, f.b[hg][kb][0], f.b[hg][kb][1]);
+        }
+        const bool full = t_lo == 0 && t_hi == 16;  // warp-uniform
+        const bool ok0 = full || (gid >= t_lo && gid < t_hi);
+        const bool ok1 = full || (gid + 8 >= t_lo && gid + 8 < t_hi);
+        float s[HG][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            // columns 2tig (hi part) and 2tig+1 (lo part) of head 4hg + tig
+            s[hg][0] = ok0 ? (acc[hg][0] + acc[hg][1]) * f.sq[hg] : -INFINITY;
+            s[hg][1] = ok1 ? (acc[hg][2] + acc[hg][3]) * f.sq[hg] : -INFINITY;
+        }
+        // ---- online softmax per head (reduction over the 8 token lanes gid)
+        float p[HG][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float tmax = fmaxf(s[hg][0], s[hg][1]);
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+            const float m_new = fmaxf(st.m[hg], tmax);
+            if (__any_sync(0xffffffffu, m_new > st.m[hg])) {
+                const float alpha = ex2(st.m[hg] - m_new);
+                st.l[hg] *= alpha;
+#pragma unroll
+                for (int mb = 0; mb < 8; mb++) {
+                    st.o[hg][mb][0] *= alpha; st.o[hg][mb][1] *= alpha;
+                    st.o[hg][mb][2] *= alpha; st.o[hg][mb][3] *= alpha;
+                }
+                st.m[hg] = m_new;
+            }
+            p[hg][0] = ex2(s[hg][0] - st.m[hg]);
+            p[hg][1] = ex2(s[hg][1] - st.m[hg]);
+            st.l[hg] += p[hg][0] + p[hg][1];
+            psum[hg] = p[hg][0] + p[hg][1];
+        }
+        // ---- P as f16 hi+lo, transposed into the PV B operand
+        uint32_t bp[HG][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            const __half2 hi = __floats2half2_rn(p[hg][0], p[hg][1]);
+            const float2 hf = __half22float2(hi);
+            const __half2 lo = __floats2half2_rn(p[hg][0] - hf.x, p[hg][1] - hf.y);
+            const uint32_t hu = *reinterpret_cast<const uint32_t *>(&hi);
+            const uint32_t lu = *reinterpret_cast<const uint32_t *>(&lo);
+            bp[hg][0] = movmatrix_trans(prmt(hu, lu, 0x5410u));  // (hi, lo) of token gid
+            bp[hg][1] = movmatrix_trans(prmt(hu, lu, 0x7632u));  // (hi, lo) of token gid+8
+        }
+        // ---- P x V: A = V^T; ldmatrix.trans lane l gives row (l&7) of matrix
+        // l>>3 = (tokens 8*(m>>1).., dims 8*(2mb + (m&1))..)
+        const int vrow = (lane & 7) + 8 * (lane >> 4), vch = (lane >> 3) & 1;
+        const uint8_t *vt = tile + 4096 + vrow * 256;
+        // a partial tile's masked slots may hold anything (even non-finite
+        // values): zero their V entries, tokens 2tig, 2tig+1 (+8) of this lane
+        uint32_t vmask[2] = {0xFFFFFFFFu, 0xFFFFFFFFu};
+        if (!full) {
+#pragma unroll
+            for (int hk = 0; hk < 2; hk++) {
+                const int t0 = 2 * tig + 8 * hk;
+                vmask[hk] = (t0 >= t_lo && t0 < t_hi ? 0x0000FFFFu : 0u) |
+                            (t0 + 1 >= t_lo && t0 + 1 < t_hi ? 0xFFFF0000u : 0u);
+            }
+        }
+#pragma unroll
+        for (int mb = 0; mb < 8; mb++) {
+            uint32_t a[4];
+            ldmatrix_x4_trans(a, vt + ((((2 * mb + vch) ^ (vrow & 7))) << 4));
+            a[0] &= vmask[0]; a[1] &= vmask[0]; a[2] &= vmask[1]; a[3] &= vmask[1];
+#pragma unroll
+            for (int hg = 0; hg < HG; hg++) mma16816(st.o[hg][mb], a, bp[hg][0], bp[hg][1]);
+        }
+    }
+
+    // tile probability mass and running max per head (eviction scores)
+    __device__ static void mass(const AttnArgs &A, uint64_t unit, const State &st, float (&psum)[HG]) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float u = psum[hg];
+            u += __shfl_xor_sync(0xffffffffu, u, 4);
+            u += __shfl_xor_sync(0xffffffffu, u, 8);
+            u += __shfl_xor_sync(0xffffffffu, u, 16);
+            const uint32_t h = 4 * hg + tig;
+            if (gid == 0 && h < A.group) A.tile_mass[unit * kMaxGroup + h] = make_float2(u, st.m[hg]);
+        }
+    }
+
+    // rows of the G query heads at o_base (stride 128), optionally normalised;
+    // m_out / l_out / seg_ml per head when non-null
+    __device__ static void store_rows(const AttnArgs &A, const State &st, float *o_base, float *m_out, float *l_out,
+                                      bool normalize, float2 *seg_ml) {
+        const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float lt = st.l[hg];
+            lt += __shfl_xor_sync(0xffffffffu, lt, 4);
+            lt += __shfl_xor_sync(0xffffffffu, lt, 8);
+            lt += __shfl_xor_sync(0xffffffffu, lt, 16);
+            const uint32_t h = 4 * hg + tig;
+            if (h >= A.group) continue;
+            const float inv = normalize ? (lt > 0.f ? 1.0f / lt : 0.f) : 1.0f;
+            float *row = o_base + (size_t)h * kHeadDim;
+#pragma unroll
+            for (int mb = 0; mb < 8; mb++) {
+                row[16 * mb + gid] = (st.o[hg][mb][0] + st.o[hg][mb][1]) * inv;
+                row[16 * mb + gid + 8] = (st.o[hg][mb][2] + st.o[hg][mb][3]) * inv;
+            }
+            if (gid == 0) {
+                if (m_out) { m_out[h] = st.m[hg]; l_out[h] = lt; }
+                if (seg_ml) seg_ml[h] = make_float2(st.m[hg], lt);
+            }
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------
 // per-codec operations used by the kernel: begin (load the query rows of a
 // segment, reset the state), step (one tile), mass (eviction scores of the
 // tile), store_rows (the segment's G output rows, or a partial)
@@ -1006,6 +1212,8 @@ template <int HG>
 struct Ops<QWN_KV_CODEC_Q4_G32, HG> : LowBitT<QWN_KV_CODEC_Q4_G32, HG> {};
 template <int HG>
 struct Ops<QWN_KV_CODEC_TQ35_G64, HG> : LowBitT<QWN_KV_CODEC_TQ35_G64, HG> {};
+template <int HG>
+struct Ops<QWN_KV_CODEC_F16, HG> : F16T<HG> {};
 
 // ---------------------------------------------------------------------------
 // batch geometry
@@ -1947,6 +2155,8 @@ size_t attention_smem_bytes(uint32_t codec, int hg) {
             return hg == 1 ? codec_smem<QWN_KV_CODEC_Q8_B64_F32, 1>() : codec_smem<QWN_KV_CODEC_Q8_B64_F32, 2>();
         case QWN_KV_CODEC_Q4_G32:
             return hg == 1 ? codec_smem<QWN_KV_CODEC_Q4_G32, 1>() : codec_smem<QWN_KV_CODEC_Q4_G32, 2>();
+        case QWN_KV_CODEC_F16:
+            return hg == 1 ? codec_smem<QWN_KV_CODEC_F16, 1>() : codec_smem<QWN_KV_CODEC_F16, 2>();
         case QWN_KV_CODEC_TQ35_G64:
             return hg == 1 ? codec_smem<QWN_KV_CODEC_TQ35_G64, 1>() : codec_smem<QWN_KV_CODEC_TQ35_G64, 2>();
         default: return 0;
@@ -1964,6 +2174,9 @@ const void *attention_kernel_ptr(uint32_t codec, int hg) {
         case QWN_KV_CODEC_Q4_G32:
             return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 1, false>
                            : (const void *)attn_kernel<QWN_KV_CODEC_Q4_G32, 2, false>;
+        case QWN_KV_CODEC_F16:
+            return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_F16, 1, false>
+                           : (const void *)attn_kernel<QWN_KV_CODEC_F16, 2, false>;
         case QWN_KV_CODEC_TQ35_G64:
             return hg == 1 ? (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 1, false>
                            : (const void *)attn_kernel<QWN_KV_CODEC_TQ35_G64, 2, false>;
@@ -2021,6 +2234,7 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
         case QWN_KV_CODEC_Q8_HEAD_F16: return launch_codec<QWN_KV_CODEC_Q8_HEAD_F16>(p, A, s);
         case QWN_KV_CODEC_Q8_B64_F32: return launch_codec<QWN_KV_CODEC_Q8_B64_F32>(p, A, s);
         case QWN_KV_CODEC_Q4_G32: return launch_codec<QWN_KV_CODEC_Q4_G32>(p, A, s);
+        case QWN_KV_CODEC_F16: return launch_codec<QWN_KV_CODEC_F16>(p, A, s);
         case QWN_KV_CODEC_TQ35_G64: return launch_codec<QWN_KV_CODEC_TQ35_G64>(p, A, s);
         default: return cudaErrorNotSupported;
     }
@@ -2068,7 +2282,7 @@ static __device__ __align__(256) float g_static_scratch[kStaticFloats];
 constexpr int kStaticMaxDevices = 64;
 std::mutex g_static_mu;
 float *g_static_addr[kStaticMaxDevices] = {};
-uint32_t g_static_ctas[kStaticMaxDevices][5][2] = {};
+uint32_t g_static_ctas[kStaticMaxDevices][6][2] = {};
 
 template <int CODEC>
 cudaError_t static_setup(int dev) {
@@ -2124,7 +2338,8 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
             if ((e = static_setup<QWN_KV_CODEC_Q8_B64_F32>(dev)) != cudaSuccess ||
                 (e = static_setup<QWN_KV_CODEC_Q8_HEAD_F16>(dev)) != cudaSuccess ||
                 (e = static_setup<QWN_KV_CODEC_Q4_G32>(dev)) != cudaSuccess ||
-                (e = static_setup<QWN_KV_CODEC_TQ35_G64>(dev)) != cudaSuccess) {
+                (e = static_setup<QWN_KV_CODEC_TQ35_G64>(dev)) != cudaSuccess ||
+                (e = static_setup<QWN_KV_CODEC_F16>(dev)) != cudaSuccess) {
                 set_cuda_error("qwn_kv_attention_static: kernel set-up", e);
                 return QWN_CUDA_STATUS_RUNTIME_ERROR;
             }
@@ -2171,6 +2386,7 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
         case QWN_KV_CODEC_Q8_HEAD_F16: e = launch_variant<QWN_KV_CODEC_Q8_HEAD_F16>(ctas, A, s); break;
         case QWN_KV_CODEC_Q8_B64_F32: e = launch_variant<QWN_KV_CODEC_Q8_B64_F32>(ctas, A, s); break;
         case QWN_KV_CODEC_Q4_G32: e = launch_variant<QWN_KV_CODEC_Q4_G32>(ctas, A, s); break;
+        case QWN_KV_CODEC_F16: e = launch_variant<QWN_KV_CODEC_F16>(ctas, A, s); break;
         default: e = launch_variant<QWN_KV_CODEC_TQ35_G64>(ctas, A, s); break;
     }
     count_launch();

@@ -39,6 +39,7 @@ inline size_t tile_bytes_of(uint32_t codec) {
         case QWN_KV_CODEC_Q8_HEAD_F16: return 4160;
         case QWN_KV_CODEC_TQ35_G64: return 2048;
         case QWN_KV_CODEC_Q4_G32: return 2560;
+        case QWN_KV_CODEC_F16: return 8192;
         default: return 0;
     }
 }
@@ -289,6 +290,23 @@ __device__ __forceinline__ void imma16832_z(int (&d)[4], uint32_t a0, uint32_t a
         "{%10,%10,%10,%10};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+// four 8x8 matrices of 16-bit values from shared memory (lane l gives the
+// address of row l&7 of matrix l>>3); .trans delivers them transposed
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *row) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(row)));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *row) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(row)));
+}
+// fp16 tile element (t, d) of the K (is_value 0) or V half: rows of 256
+// bytes, 16-byte chunk d>>3 at position (d>>3) xor (t&7)
+__device__ __forceinline__ uint32_t f16_off(int is_value, int t, int d) {
+    return (uint32_t)(is_value * 4096 + t * 256 + ((((d >> 3) ^ (t & 7))) << 4) + (d & 7) * 2);
 }
 // transpose of an 8x8 matrix of 16-bit values held one row pair per lane
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {

@@ -243,6 +243,7 @@ cudaError_t dispatch_store(uint32_t codec, dim3 grid, dim3 block, cudaStream_t s
         case QWN_KV_CODEC_Q8_B64_F32: K<QWN_KV_CODEC_Q8_B64_F32>::launch(grid, block, s, args...); break;
         case QWN_KV_CODEC_TQ35_G64: K<QWN_KV_CODEC_TQ35_G64>::launch(grid, block, s, args...); break;
         case QWN_KV_CODEC_Q4_G32: K<QWN_KV_CODEC_Q4_G32>::launch(grid, block, s, args...); break;
+        case QWN_KV_CODEC_F16: K<QWN_KV_CODEC_F16>::launch(grid, block, s, args...); break;
         default: return cudaErrorNotSupported;
     }
     count_launch();

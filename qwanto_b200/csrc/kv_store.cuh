@@ -100,6 +100,21 @@ __device__ __forceinline__ void put_bits(uint8_t *tile, uint32_t byte, uint32_t 
 template <int CODEC>
 __device__ void store_token(uint8_t *tile, int t, float4 k, float4 v, int lane);
 
+// fp32 -> fp16 round to nearest even (c/qwn_paged_kv.c:151-198, F16C); a NaN
+// stays a quiet NaN with the top ten payload bits, as F16C keeps them
+__device__ __forceinline__ uint32_t f16_bits(float x) {
+    const uint32_t u = __float_as_uint(x);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return ((u >> 16) & 0x8000u) | 0x7E00u | ((u >> 13) & 0x3FFu);
+    return __half_as_ushort(__float2half_rn(x));
+}
+template <>
+__device__ void store_token<QWN_KV_CODEC_F16>(uint8_t *tile, int t, float4 k, float4 v, int lane) {
+    // the lane's dims 4*lane..4*lane+3: half of one 16-byte chunk
+    const uint2 kk = make_uint2(f16_bits(k.x) | (f16_bits(k.y) << 16), f16_bits(k.z) | (f16_bits(k.w) << 16));
+    const uint2 vv = make_uint2(f16_bits(v.x) | (f16_bits(v.y) << 16), f16_bits(v.z) | (f16_bits(v.w) << 16));
+    *reinterpret_cast<uint2 *>(tile + f16_off(0, t, 4 * lane)) = kk;
+    *reinterpret_cast<uint2 *>(tile + f16_off(1, t, 4 * lane)) = vv;
+}
 template <>
 __device__ void store_token<QWN_KV_CODEC_Q8_HEAD_F16>(uint8_t *tile, int t, float4 k, float4 v, int lane) {
     const uint16_t sk = head_scale16(warp_max(absmax4(k)));

@@ -12,7 +12,7 @@ from kvharness import Twin, assert_close
 
 pytestmark = pytest.mark.gpu
 
-CODECS = [1, 2, 3, 4]
+CODECS = [1, 2, 3, 4, 5]
 
 
 def test_generator_bit_exact(cuda, oracle_mod):
@@ -31,7 +31,7 @@ def test_generator_bit_exact(cuda, oracle_mod):
         assert np.array_equal(got[r].view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("codec", [1, 2, 3, 4])
+@pytest.mark.parametrize("codec", [1, 2, 3, 4, 5])
 @pytest.mark.parametrize("page_tokens", [16, 64])
 def test_prefill_pages_bit_exact(cuda, codec, page_tokens):
     """Quantize-on-append into pages: every byte of every used page, the page
@@ -83,7 +83,7 @@ def test_long_context_and_subset_batch(cuda, codec):
         tw.close()
 
 
-@pytest.mark.parametrize("codec", [2, 3])
+@pytest.mark.parametrize("codec", [2, 3, 5])
 def test_single_long_sequence_two_level_merge(cuda, codec):
     """One 24k-token sequence: every (sequence, kv head) segment is split over
     ~220 warps, so the partials merge in two levels (groups of 16, then the
@@ -100,7 +100,7 @@ def test_single_long_sequence_two_level_merge(cuda, codec):
         tw.close()
 
 
-@pytest.mark.parametrize("codec", [2, 4])
+@pytest.mark.parametrize("codec", [2, 4, 5])
 @pytest.mark.parametrize("heads", [(32, 8), (12, 2)])
 def test_identity_batch_cached_plans(cuda, codec, heads):
     """Calls without a sequence-id array cache the launch setup across the

@@ -24,7 +24,7 @@ def _query(torch, qb, seed, pos):
     return q
 
 
-@pytest.mark.parametrize("codec", [2, 4])
+@pytest.mark.parametrize("codec", [2, 4, 5])
 def test_split_one_rank_matches_decode_and_oracle(cuda, codec):
     import qwanto_b200 as qb
     from qwanto_b200._lib import ST_PEER_TIMEOUT

@@ -246,6 +246,56 @@ def test_tq35_attention_oracle_vs_reference_live(oracle_mod, ref_lib):
     ref_lib.qwn_turboquant_free(C.byref(tq))
 
 
+def _f16_specials():
+    rng = np.random.default_rng(12)
+    xs = [rng.standard_normal(1024).astype(np.float32) * s for s in (1e-9, 6e-8, 3e-5, 1.0, 1e3, 6.5e4)]
+    edge = np.array([0.0, -0.0, 65504.0, 65519.0, 65520.0, -65520.0, 1e6, np.inf, -np.inf,
+                     2.0 ** -24, 2.0 ** -25, 1.5 * 2.0 ** -25, 2.0 ** -14, 2.0 ** -14 * (1 - 2.0 ** -11)],
+                    np.float32)
+    nans = np.array([0x7FC00000, 0x7F800001, 0xFFC12345, 0x7FBFFFFF], np.uint32).view(np.float32)
+    x = np.concatenate(xs + [edge, nans]).astype(np.float32)
+    return np.concatenate([x, np.zeros((-len(x)) % (16 * 128), np.float32)])
+
+
+def test_f16_store_matches_reference_pool_write_live(oracle_mod, ref_lib):
+    """The fp16 codec's rounding against the reference's own pool write
+    (qwn_paged_kv_write, c/qwn_paged_kv.c:151-198, F16C round to nearest
+    even): bit-exact on random, subnormal, overflow, infinite and NaN inputs."""
+    x = _f16_specials().reshape(-1, 16, 128)
+    for blk in x:
+        k16 = np.zeros((16, 128), np.uint16)
+        v16 = np.zeros((16, 128), np.uint16)
+        v = -blk[::-1].copy()
+        assert ref_lib.qref_f16_write(oracle_mod._ptr(blk, oracle_mod.f32p), oracle_mod._ptr(v, oracle_mod.f32p),
+                                      16, 128, oracle_mod._ptr(k16, oracle_mod.u16p),
+                                      oracle_mod._ptr(v16, oracle_mod.u16p)) == 0
+        mine_k = np.array([oracle_mod.f16_rne(float(e)) for e in blk.ravel()], np.uint16).reshape(16, 128)
+        mine_v = np.array([oracle_mod.f16_rne(float(e)) for e in v.ravel()], np.uint16).reshape(16, 128)
+        assert np.array_equal(mine_k, k16) and np.array_equal(mine_v, v16)
+
+
+def test_f16_attention_oracle_vs_reference_live(oracle_mod, ref_lib):
+    """The decoder's fp16 paged path (block table appends, qwn_paged_kv_write,
+    qwn_paged_attention_gather_head; c/qwanto_decode.c:1600-1604, :1807-1835)
+    run by the reference shim, against the oracle's fp16 codec on the same
+    generated rows: equal within reassociation noise."""
+    HK, HD, H, seed = 2, 128, 12, 33
+    for ntok in (1, 17, 300):
+        lens = np.array([ntok - 1], np.int32)
+        b = ref_lib.qref_batch_create(5, 1, oracle_mod._ptr(lens, oracle_mod.i32p), 1, H, HK, HD, 1, seed)
+        assert b
+        assert ref_lib.qref_batch_step(b, 1) == 1
+        ctx = np.ctypeslib.as_array(ref_lib.qref_batch_ctx(b), shape=(H * HD,)).copy().reshape(H, HD)
+        ref_lib.qref_batch_destroy(b)
+        p = oracle_mod.Pool(oracle_mod.CODEC_F16, 1, HK, 16, 64, 1, 64)
+        assert p.append([0], [ntok]) == 0
+        for t in range(ntok):
+            assert p.write(0, 0, t, oracle_mod.gen_row(seed, 2, 0, 0, t, HK * HD),
+                           oracle_mod.gen_row(seed, 3, 0, 0, t, HK * HD)) == 0
+        ours = p.attention(0, 0, ntok, oracle_mod.gen_row(seed, 1, 0, 0, ntok - 1, H * HD), H, 1.0 / np.sqrt(HD))
+        np.testing.assert_allclose(ours, ctx, rtol=1e-5, atol=1e-6)
+
+
 # ------------------------------------------------------- oracle internals ---
 
 def test_f16_rne_matches_numpy(oracle_mod):
@@ -255,6 +305,23 @@ def test_f16_rne_matches_numpy(oracle_mod):
     mine = np.array([oracle_mod.f16_rne(float(v)) for v in xs], np.uint16)
     with np.errstate(over="ignore"):
         assert np.array_equal(mine, xs.astype(np.float16).view(np.uint16))
+
+
+def test_f16_tile_round_trip(oracle_mod):
+    """The fp16 codec's tile reads back fp16(x) at every (token, dim) slot."""
+    rng = np.random.default_rng(5)
+    tile = np.zeros(oracle_mod.TILE_BYTES[5], np.uint8)
+    ks = rng.standard_normal((16, 128)).astype(np.float32) * 3
+    vs = rng.standard_normal((16, 128)).astype(np.float32)
+    L = oracle_mod.lib()
+    for t in rng.permutation(16):
+        L.qor_tile_store(5, oracle_mod._ptr(tile, oracle_mod.u8p), int(t),
+                         oracle_mod._ptr(ks[t], oracle_mod.f32p), oracle_mod._ptr(vs[t], oracle_mod.f32p))
+    for t in range(16):
+        for isv, x in ((0, ks[t]), (1, vs[t])):
+            got = np.array([L.qor_tile_dequant(5, oracle_mod._ptr(tile, oracle_mod.u8p), t, isv, d) for d in range(128)],
+                           np.float32)
+            assert np.array_equal(got, x.astype(np.float16).astype(np.float32))
 
 
 @pytest.mark.parametrize("codec", [1, 2, 3, 4])
