@@ -755,6 +755,84 @@ def run_churn(args, wl, world, rank, local):
     return 0
 
 
+def run_gemv(args) -> int:
+    """HyperVSQ-2 GEMV / batched GEMM (74-byte blocks of 256 2-bit weights
+    times int8 activations), through ABI v1 exactly as qwnrun calls it: this
+    library against the reference's own GPU library (oracle/_ref, compiled
+    from c/cuda/qwn_hypervsq2_cuda_abi.cu) on the same weights and inputs.
+    Times are each library's own kernel events (telemetry gpu_kernel_ms per
+    call); outputs are cross-checked.  One JSON line per shape."""
+    import ctypes as C
+    from qwanto_b200 import _lib
+    libs = {"ours": os.path.join(ROOT, "qwanto_b200", "qwn_cuda.so"),
+            "reference": os.path.join(ROOT, "oracle", "_ref", "qwn_cuda_ref.so")}
+    P = C.POINTER
+    loaded = {}
+    for name, path in libs.items():
+        if not os.path.exists(path):
+            continue
+        L = C.CDLL(path, mode=os.RTLD_LOCAL)
+        for fn, res, argt in (("qwn_cuda_abi_context_create", C.c_int, [P(_lib.ContextOptions), P(_lib.Handle)]),
+                              ("qwn_cuda_abi_context_destroy", C.c_int, [P(_lib.Handle)]),
+                              ("qwn_cuda_abi_upload_tensor", C.c_int, [P(_lib.Handle), P(_lib.TensorUpload), P(_lib.Handle)]),
+                              ("qwn_cuda_abi_release_tensor", C.c_int, [P(_lib.Handle), P(_lib.Handle)]),
+                              ("qwn_cuda_abi_hypervsq2_gemm", C.c_int, [P(_lib.Handle), P(_lib.GemmRequest), P(_lib.Telemetry)])):
+            getattr(L, fn).restype = res
+            getattr(L, fn).argtypes = argt
+        loaded[name] = L
+    rng = np.random.default_rng(7)
+    shapes = [(4096, 4096, 1), (14336, 4096, 1), (4096, 14336, 1), (151936, 4096, 1), (4096, 4096, 8), (14336, 4096, 8)]
+    for rows, cols, batch in shapes:
+        nblk = (cols + 255) // 256
+        w = rng.integers(0, 256, size=(rows, nblk, 74), dtype=np.uint8)
+        base = (rng.random((rows, nblk)) * 0.01 + 0.001).astype(np.float16)
+        offs = (rng.random((rows, nblk)) * 0.002 - 0.001).astype(np.float16)
+        w[:, :, 0:2] = base.view(np.uint8).reshape(rows, nblk, 2)
+        w[:, :, 2:4] = offs.view(np.uint8).reshape(rows, nblk, 2)
+        wb = np.ascontiguousarray(w.reshape(-1))
+        act = rng.integers(-127, 128, size=(batch, cols), dtype=np.int8)
+        scales = (rng.random(batch) + 0.5).astype(np.float32)
+        line = {"gemv": {"rows": rows, "cols": cols, "batch": batch}, "weight_bytes": int(wb.size)}
+        outs = {}
+        for name, L in loaded.items():
+            o = _lib.init(_lib.ContextOptions())
+            o.device_id = 0
+            ctx = _lib.init(_lib.Handle())
+            if L.qwn_cuda_abi_context_create(C.byref(o), C.byref(ctx)) != 0:
+                line[name] = "context_create failed"
+                continue
+            up = _lib.init(_lib.TensorUpload())
+            up.host_data, up.data_bytes, up.dtype, up.rows, up.cols, up.block_bytes = wb.ctypes.data, wb.size, 1, rows, cols, 74
+            th = _lib.init(_lib.Handle())
+            assert L.qwn_cuda_abi_upload_tensor(C.byref(ctx), C.byref(up), C.byref(th)) == 0
+            out = np.zeros((batch, rows), np.float32)
+            rq = _lib.init(_lib.GemmRequest())
+            rq.tensor, rq.input_q8 = th, act.ctypes.data
+            rq.input_scales = scales.ctypes.data_as(C.POINTER(C.c_float))
+            rq.output = out.ctypes.data_as(C.POINTER(C.c_float))
+            rq.batch, rq.rows, rq.cols, rq.input_mode = batch, rows, cols, 1
+            tel = _lib.init(_lib.Telemetry())
+            per = []
+            n = 10 if wb.size > 50e6 else 60
+            for i in range(n + 3):
+                before = tel.gpu_kernel_ms
+                assert L.qwn_cuda_abi_hypervsq2_gemm(C.byref(ctx), C.byref(rq), C.byref(tel)) == 0
+                if i >= 3:
+                    per.append(tel.gpu_kernel_ms - before)
+            us = 1000.0 * float(np.median(per))
+            moved = wb.size + act.size + 4 * out.size
+            line[name] = {"kernel_us": us, "gbs": moved / (us * 1e-6) / 1e9}
+            outs[name] = out.copy()
+            L.qwn_cuda_abi_release_tensor(C.byref(ctx), C.byref(th))
+            L.qwn_cuda_abi_context_destroy(C.byref(ctx))
+        if "ours" in outs and "reference" in outs:
+            ref = outs["reference"]
+            line["max_rel_diff"] = float(np.max(np.abs(outs["ours"] - ref) / (1e-3 + np.abs(ref))))
+            line["speedup"] = line["reference"]["kernel_us"] / line["ours"]["kernel_us"]
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -765,6 +843,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--ring", type=int, default=8, help="distinct input step buffers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemv", action="store_true",
+                    help="time the HyperVSQ-2 GEMV against the reference GPU library instead (one line per shape)")
     ap.add_argument("--codec", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
                     help="run the config's shapes with another KV codec (5 = fp16, the reference's paged pool)")
     ap.add_argument("--soak-ms", type=float, default=1500.0,
@@ -775,6 +855,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="override the config's layer count (profiling)")
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling)")
     args = ap.parse_args()
+    if args.gemv:
+        return run_gemv(args)
     if args.warmup < 3:
         args.warmup = 3  # the timing rules want >= 3 warm-up steps
     wl = with_codec(workload(args.config), args.codec)

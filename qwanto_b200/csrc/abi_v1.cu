@@ -25,10 +25,16 @@ namespace {
 
 std::mutex g_abi_mu;
 
+// A HyperVSQ-2 tensor, repacked at upload: the 64 code bytes of every block
+// in [rows][blocks][64] (16-byte aligned for vector loads), then the block
+// headers (fp16 base, fp16 offset, four sub-scale bytes; the two reserved
+// bytes dropped) in [rows][blocks][8]: 72 bytes per block instead of 74.
 struct Tensor {
     void *dev = nullptr;
     uint64_t bytes = 0;
-    uint32_t rows = 0, cols = 0;
+    uint32_t rows = 0, cols = 0, nblk = 0;
+    const uint8_t *codes() const { return static_cast<const uint8_t *>(dev); }
+    const uint8_t *hdr() const { return codes() + (uint64_t)rows * nblk * 64; }
 };
 
 struct KvCache {
@@ -225,41 +231,107 @@ __device__ __forceinline__ float half_ftz(const uint8_t *b) {
     return __uint_as_float(bits);
 }
 
-__global__ void hypervsq2_gemv_kernel(const uint8_t *w, const int8_t *in, float in_scale, const float *in_scales,
-                                      float *out, uint32_t batch, uint32_t rows, uint32_t cols,
-                                      uint32_t in_stride, uint32_t out_stride, uint64_t row_bytes) {
-    const uint32_t row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const uint32_t tok = blockIdx.y;
-    const int lane = threadIdx.x & 31;
-    if (row >= rows || tok >= batch) return;
-    const uint8_t *rp = w + (uint64_t)row * row_bytes;
-    const int8_t *ip = in + (uint64_t)tok * in_stride;
-    const uint32_t nblk = (cols + 255) / 256;
-    const int oct = lane >> 2;
-    float acc = 0.f;
-    for (uint32_t b = 0; b < nblk; b++) {
-        const uint8_t *blk = rp + (uint64_t)b * QWN_CUDA_HYPERVSQ2_BLOCK_BYTES;
-        const uint32_t e0 = b * 256 + (uint32_t)lane * 8;
-        if (e0 >= cols) continue;
-        const float base = half_ftz(blk), offs = half_ftz(blk + 2);
-        const uint8_t sb = blk[4 + (oct >> 1)];
-        const int sub = (oct & 1) ? (sb >> 4) : (sb & 15);
-        const float eff = base * ((float)sub * (1.0f / 8.0f));
-        const uint8_t *pv = blk + 10 + oct * 8 + (lane & 3) * 2;
-        const uint32_t codes = (uint32_t)pv[0] | ((uint32_t)pv[1] << 8);
-        int dot = 0, asum = 0;
-        const uint32_t n = min(8u, cols - e0);
-        for (uint32_t k = 0; k < n; k++) {
-            const int a = ip[e0 + k];
-            const int q = (int)((codes >> (2 * k)) & 3u);
-            dot += (q - 1) * a;
-            asum += a;
-        }
-        acc += (float)dot * eff + (float)asum * offs;
-    }
+// Activations of up to kGemvTokens tokens are staged per CTA in shared
+// memory: block b of token t at t*nblk*320 + b*320, its quarter qd (weights
+// 64qd..64qd+63) at +80qd (the padding keeps the quarters of eight blocks on
+// distinct banks), and inside a quarter each group of 16 weights permuted so
+// that word i holds weights i, 4+i, 8+i, 12+i -- the order in which one
+// masked shift of a code word yields them.  Past cols the activations are 0.
+// osum[t][8b+o] is the sum of octant o's activations (the offset term and
+// the -1 of the codes).  A lane takes one quarter block (two octants), loads
+// its 16 code bytes once and applies them to every staged token with dp4a:
+// sum (q-1)*a = dp4a(q, a) - sum a, exact in integers, then the octant's
+// scale base*sub/8 and the block offset in fp32.
+constexpr int kGemvWarps = 8, kGemvTokens = 8, kGemvBlockSmem = 320 + 8 * 4;
+
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    hypervsq2_gemv_kernel(const uint8_t *codes, const uint8_t *hdr, const int8_t *in, float in_scale,
+                          const float *in_scales, float *out, uint32_t batch, uint32_t rows, uint32_t cols,
+                          uint32_t nblk, uint32_t in_stride, uint32_t out_stride, uint32_t tokens_per_pass) {
+    extern __shared__ __align__(16) uint8_t gsm[];
+    const uint32_t tok_bytes = nblk * 320u;
+    int8_t *act = reinterpret_cast<int8_t *>(gsm);
+    int *osum = reinterpret_cast<int *>(gsm + (size_t)tokens_per_pass * tok_bytes);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t wglob = blockIdx.x * kGemvWarps + warp, wtot = gridDim.x * kGemvWarps;
+    const int qd = lane & 3;
+    for (uint32_t t0 = 0; t0 < batch; t0 += tokens_per_pass) {
+        const uint32_t nt = min(tokens_per_pass, batch - t0);
+        __syncthreads();  // the previous pass is done with the staged tokens
+        // stage the permuted activation words: word w of token t = quarter
+        // (b, qd), group g = (w>>2)&3, lane-word i = w&3
+        const uint32_t words = nblk * 64u;  // 4-byte words of one token's padded row
+        for (uint32_t idx = threadIdx.x; idx < nt * words; idx += blockDim.x) {
+            const uint32_t tt = idx / words, w = idx % words;
+            const uint32_t b = w >> 6, q = (w >> 4) & 3, g = (w >> 2) & 3, i = w & 3;
+            const uint32_t c0 = b * 256u + q * 64u + g * 16u + i;
+            const int8_t *ip = in + (uint64_t)(t0 + tt) * in_stride;
+            uint32_t v = 0;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) out[(uint64_t)tok * out_stride + row] = acc * (in_scales ? in_scales[tok] : in_scale);
+            for (int k = 0; k < 4; k++) {
+                const uint32_t c = c0 + 4u * k;
+                v |= (uint32_t)(uint8_t)(c < cols ? ip[c] : 0) << (8 * k);
+            }
+            *reinterpret_cast<uint32_t *>(act + (size_t)tt * tok_bytes + b * 320u + q * 80u + g * 16u + i * 4u) = v;
+        }
+        for (uint32_t idx = threadIdx.x; idx < nt * nblk * 8u; idx += blockDim.x) {
+            const uint32_t tt = idx / (nblk * 8u), o = idx % (nblk * 8u);
+            const int8_t *ip = in + (uint64_t)(t0 + tt) * in_stride;
+            int s = 0;
+            for (uint32_t c = o * 32u; c < o * 32u + 32u && c < cols; c++) s += ip[c];
+            osum[tt * nblk * 8u + o] = s;
+        }
+        __syncthreads();
+        for (uint32_t row = wglob; row < rows; row += wtot) {
+            float acc[kGemvTokens];
+#pragma unroll
+            for (int k = 0; k < kGemvTokens; k++) acc[k] = 0.f;
+            const uint8_t *rc = codes + (uint64_t)row * nblk * 64u;
+            const uint8_t *rh = hdr + (uint64_t)row * nblk * 8u;
+#pragma unroll 2
+            for (uint32_t b = lane >> 2; b < nblk; b += 8) {
+                const uint4 cw = *reinterpret_cast<const uint4 *>(rc + b * 64u + qd * 16u);
+                const uint2 h = *reinterpret_cast<const uint2 *>(rh + b * 8u);
+                const float base = half_ftz(reinterpret_cast<const uint8_t *>(&h));
+                const float offs = half_ftz(reinterpret_cast<const uint8_t *>(&h) + 2);
+                const uint32_t sb = (h.y >> (8 * qd)) & 0xFFu;  // octants 2qd (low nibble), 2qd+1 (high)
+                const float eff0 = base * ((float)(sb & 15u) * (1.0f / 8.0f));
+                const float eff1 = base * ((float)(sb >> 4) * (1.0f / 8.0f));
+                const uint32_t cwa[4] = {cw.x, cw.y, cw.z, cw.w};
+                int e[4][4];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) e[j][i] = (int)((cwa[j] >> (2 * i)) & 0x03030303u);
+#pragma unroll
+                for (int k = 0; k < kGemvTokens; k++) {
+                    if ((uint32_t)k >= nt) break;
+                    const int8_t *ta = act + (size_t)k * tok_bytes + b * 320u + qd * 80u;
+                    int d[2] = {0, 0};
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int4 a = *reinterpret_cast<const int4 *>(ta + 16 * j);
+                        d[j >> 1] = __dp4a(e[j][0], a.x, d[j >> 1]);
+                        d[j >> 1] = __dp4a(e[j][1], a.y, d[j >> 1]);
+                        d[j >> 1] = __dp4a(e[j][2], a.z, d[j >> 1]);
+                        d[j >> 1] = __dp4a(e[j][3], a.w, d[j >> 1]);
+                    }
+                    const int *os = osum + k * nblk * 8u + b * 8u + 2 * qd;
+                    const int s0 = os[0], s1 = os[1];
+                    acc[k] += eff0 * (float)(d[0] - s0) + eff1 * (float)(d[1] - s1) + offs * (float)(s0 + s1);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kGemvTokens; k++) {
+                if ((uint32_t)k >= nt) break;
+                float v = acc[k];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0)
+                    out[(uint64_t)(t0 + k) * out_stride + row] = v * (in_scales ? in_scales[t0 + k] : in_scale);
+            }
+        }
+    }
 }
 
 int gemv_execute(Context *c, const QwnCudaGemmRequest *r, QwnCudaTelemetry *tel) {
@@ -289,11 +361,25 @@ int gemv_execute(Context *c, const QwnCudaGemmRequest *r, QwnCudaTelemetry *tel)
                             c->stream);
     auto t1 = std::chrono::steady_clock::now();
     if (e == cudaSuccess) e = cudaEventRecord(c->ev0, c->stream);
-    const uint64_t row_bytes = (uint64_t)((r->cols + 255) / 256) * QWN_CUDA_HYPERVSQ2_BLOCK_BYTES;
+    // tokens staged per pass: as many as ~96 KB of shared memory holds (two
+    // CTAs per SM), at least one (up to the opt-in limit set below)
+    const uint64_t per_tok = (uint64_t)t->nblk * kGemvBlockSmem;
+    uint32_t tpp = (uint32_t)std::min<uint64_t>(kGemvTokens, std::max<uint64_t>(1, (96u << 10) / per_tok));
+    tpp = std::min<uint32_t>(tpp, r->batch);
+    const size_t smem = (size_t)tpp * per_tok;
+    if (smem > (200u << 10)) {
+        set_error("HyperVSQ-2 GEMV: cols too large for one token's activations in shared memory");
+        return QWN_CUDA_STATUS_UNSUPPORTED;
+    }
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(hypervsq2_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   200 << 10);
     if (e == cudaSuccess) {
-        hypervsq2_gemv_kernel<<<dim3((r->rows + 3) / 4, r->batch), 128, 0, c->stream>>>(
-            (const uint8_t *)t->dev, c->d_in, r->input_scale, r->input_scales ? c->d_scales : nullptr, c->d_out,
-            r->batch, r->rows, r->cols, ist, ost, row_bytes);
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device);
+        const uint32_t grid = std::min<uint32_t>((r->rows + kGemvWarps - 1) / kGemvWarps, (uint32_t)std::max(1, sms) * 4u);
+        hypervsq2_gemv_kernel<<<grid, kGemvWarps * 32, smem, c->stream>>>(
+            t->codes(), t->hdr(), c->d_in, r->input_scale, r->input_scales ? c->d_scales : nullptr, c->d_out,
+            r->batch, r->rows, r->cols, t->nblk, ist, ost, tpp);
         count_launch();
         e = cudaGetLastError();
     }
@@ -434,11 +520,12 @@ QWN_CUDA_ABI_API int qwn_cuda_abi_upload_tensor(QwnCudaContextHandle *h, const Q
         set_error("invalid HyperVSQ-2 tensor upload request");
         return QWN_CUDA_STATUS_INVALID_ARGUMENT;
     }
-    const uint64_t need = (uint64_t)u->rows * ((u->cols + 255u) / 256u) * u->block_bytes;
-    if (u->data_bytes < need) {
+    const uint32_t nblk = (u->cols + 255u) / 256u;
+    if (u->data_bytes < (uint64_t)u->rows * nblk * u->block_bytes) {
         set_error("HyperVSQ-2 tensor upload is shorter than its validated shape");
         return QWN_CUDA_STATUS_INVALID_ARGUMENT;
     }
+    const uint64_t need = (uint64_t)u->rows * nblk * 72u;  // the repacked layout (struct Tensor)
     std::lock_guard<std::mutex> lk(g_abi_mu);
     cudaSetDevice(c->device);
     size_t fb = 0, tb = 0;
@@ -451,8 +538,25 @@ QWN_CUDA_ABI_API int qwn_cuda_abi_upload_tensor(QwnCudaContextHandle *h, const Q
     t->bytes = need;
     t->rows = u->rows;
     t->cols = u->cols;
+    t->nblk = nblk;
+    // repack on the host: codes [rows][blocks][64], then headers [rows][blocks][8]
+    std::vector<uint8_t> packed;
+    try {
+        packed.resize(need);
+    } catch (...) {
+        delete t;
+        set_error("HyperVSQ-2 tensor upload: host staging allocation failed");
+        return QWN_CUDA_STATUS_OUT_OF_MEMORY;
+    }
+    const uint8_t *src = static_cast<const uint8_t *>(u->host_data);
+    const uint64_t nb = (uint64_t)u->rows * nblk;
+    for (uint64_t i = 0; i < nb; i++) {
+        const uint8_t *blk = src + i * QWN_CUDA_HYPERVSQ2_BLOCK_BYTES;
+        std::memcpy(packed.data() + i * 64, blk + 10, 64);
+        std::memcpy(packed.data() + nb * 64 + i * 8, blk, 8);
+    }
     if (cudaMalloc(&t->dev, need) != cudaSuccess ||
-        cudaMemcpy(t->dev, u->host_data, need, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaMemcpy(t->dev, packed.data(), need, cudaMemcpyHostToDevice) != cudaSuccess) {
         cudaFree(t->dev);
         delete t;
         set_cuda_error("HyperVSQ-2 tensor upload", cudaGetLastError());

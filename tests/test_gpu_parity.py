@@ -381,6 +381,64 @@ def test_abi_v1_decoder_sequence(cuda, oracle_mod):
         ctx.close()
 
 
+def _hvsq2_numpy(w, act, scales, cols):
+    """The 74-byte HyperVSQ-2 block arithmetic (c/cuda/qwn_hypervsq2_cuda_abi.cu:225-289)
+    in float64: per weight (q-1)*a*base*sub/8 + a*offset, times the token scale."""
+    rows, nblk, _ = w.shape
+    # the reference decodes the fp16 base and offset with subnormals flushed
+    # to zero (half_to_float, c/cuda/qwn_hypervsq2_cuda_abi.cu:111-126)
+    ftz = lambda x: np.where(np.abs(x) < 2.0 ** -14, 0.0, x)
+    base = ftz(w[:, :, 0:2].copy().view(np.float16)[:, :, 0].astype(np.float64))
+    offs = ftz(w[:, :, 2:4].copy().view(np.float16)[:, :, 0].astype(np.float64))
+    sub = np.zeros((rows, nblk, 8), np.float64)
+    for o in range(8):
+        sb = w[:, :, 4 + o // 2]
+        sub[:, :, o] = (sb >> 4) if o & 1 else (sb & 15)
+    codes = np.zeros((rows, nblk, 256), np.float64)
+    for e in range(256):
+        codes[:, :, e] = (w[:, :, 10 + e // 4] >> (2 * (e % 4))) & 3
+    eff = base[:, :, None] * np.repeat(sub, 32, axis=2) / 8.0          # [rows][nblk][256]
+    wt = (codes - 1.0) * eff + offs[:, :, None]
+    wt = wt.reshape(rows, nblk * 256)[:, :cols]
+    return (act.astype(np.float64) @ wt.T) * scales[:, None].astype(np.float64)
+
+
+@pytest.mark.parametrize("rows,cols,batch", [(300, 1000, 11), (64, 4096, 1), (129, 256, 9)])
+def test_hypervsq2_gemm_shapes(cuda, rows, cols, batch):
+    """The GEMV/GEMM over ragged column counts, batches larger than one pass of
+    staged tokens and a single full block, against the format in numpy."""
+    import qwanto_b200 as qb
+    from qwanto_b200 import _lib
+    rng = np.random.default_rng(rows + cols + batch)
+    nblk = (cols + 255) // 256
+    w = rng.integers(0, 256, size=(rows, nblk, 74), dtype=np.uint8)
+    w[:, :, 0:2] = (rng.random((rows, nblk)) * 0.01 + 0.001).astype(np.float16).view(np.uint8).reshape(rows, nblk, 2)
+    w[:, :, 2:4] = (rng.random((rows, nblk)) * 0.002 - 0.001).astype(np.float16).view(np.uint8).reshape(rows, nblk, 2)
+    act = rng.integers(-127, 128, size=(batch, cols), dtype=np.int8)
+    scales = (rng.random(batch) + 0.5).astype(np.float32)
+    ref = _hvsq2_numpy(w, act, scales, cols)
+    ctx = qb.CudaContext(0)
+    try:
+        up = _lib.init(_lib.TensorUpload())
+        wb = np.ascontiguousarray(w.reshape(-1))
+        up.host_data, up.data_bytes, up.dtype, up.rows, up.cols, up.block_bytes = wb.ctypes.data, wb.size, 1, rows, cols, 74
+        th = _lib.init(_lib.Handle())
+        _lib.check("upload", qb.lib().qwn_cuda_abi_upload_tensor(C.byref(ctx.h), C.byref(up), C.byref(th)))
+        for _ in range(2):
+            out = np.zeros((batch, rows), np.float32)
+            rq = _lib.init(_lib.GemmRequest())
+            rq.tensor, rq.input_q8 = th, act.ctypes.data
+            rq.input_scales = scales.ctypes.data_as(C.POINTER(C.c_float))
+            rq.output = out.ctypes.data_as(C.POINTER(C.c_float))
+            rq.batch, rq.rows, rq.cols, rq.input_mode = batch, rows, cols, 1
+            tel = _lib.init(_lib.Telemetry())
+            _lib.check("gemm", qb.lib().qwn_cuda_abi_hypervsq2_gemm(C.byref(ctx.h), C.byref(rq), C.byref(tel)))
+            np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-3)
+        _lib.check("release", qb.lib().qwn_cuda_abi_release_tensor(C.byref(ctx.h), C.byref(th)))
+    finally:
+        ctx.close()
+
+
 def test_hypervsq2_gemv_matches_reference_cpu(cuda, oracle_mod):
     """HyperVSQ-2 74-byte GEMV (required for qwnrun to load the library)
     against the format's arithmetic restated in numpy."""
