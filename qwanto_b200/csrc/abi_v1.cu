@@ -244,6 +244,7 @@ __device__ __forceinline__ float half_ftz(const uint8_t *b) {
 // scale base*sub/8 and the block offset in fp32.
 constexpr int kGemvWarps = 8, kGemvTokens = 8, kGemvBlockSmem = 320 + 8 * 4;
 
+template <int TOKS, int ROWS>
 __global__ void __launch_bounds__(kGemvWarps * 32)
     hypervsq2_gemv_kernel(const uint8_t *codes, const uint8_t *hdr, const int8_t *in, float in_scale,
                           const float *in_scales, float *out, uint32_t batch, uint32_t rows, uint32_t cols,
@@ -282,53 +283,73 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
             osum[tt * nblk * 8u + o] = s;
         }
         __syncthreads();
-        for (uint32_t row = wglob; row < rows; row += wtot) {
-            float acc[kGemvTokens];
+        // ROWS rows per iteration (rows row, row + wtot, ...): all their code
+        // and header loads are in flight before any is used
+        for (uint32_t row = wglob; row < rows; row += ROWS * wtot) {
+            uint32_t rr[ROWS];
+            float acc[ROWS][TOKS];
+            const uint8_t *rc[ROWS], *rh[ROWS];
 #pragma unroll
-            for (int k = 0; k < kGemvTokens; k++) acc[k] = 0.f;
-            const uint8_t *rc = codes + (uint64_t)row * nblk * 64u;
-            const uint8_t *rh = hdr + (uint64_t)row * nblk * 8u;
-#pragma unroll 2
+            for (int r = 0; r < ROWS; r++) {
+                rr[r] = row + r * wtot < rows ? row + r * wtot : row;
+                rc[r] = codes + (uint64_t)rr[r] * nblk * 64u;
+                rh[r] = hdr + (uint64_t)rr[r] * nblk * 8u;
+#pragma unroll
+                for (int k = 0; k < TOKS; k++) acc[r][k] = 0.f;
+            }
             for (uint32_t b = lane >> 2; b < nblk; b += 8) {
-                const uint4 cw = *reinterpret_cast<const uint4 *>(rc + b * 64u + qd * 16u);
-                const uint2 h = *reinterpret_cast<const uint2 *>(rh + b * 8u);
-                const float base = half_ftz(reinterpret_cast<const uint8_t *>(&h));
-                const float offs = half_ftz(reinterpret_cast<const uint8_t *>(&h) + 2);
-                const uint32_t sb = (h.y >> (8 * qd)) & 0xFFu;  // octants 2qd (low nibble), 2qd+1 (high)
-                const float eff0 = base * ((float)(sb & 15u) * (1.0f / 8.0f));
-                const float eff1 = base * ((float)(sb >> 4) * (1.0f / 8.0f));
-                const uint32_t cwa[4] = {cw.x, cw.y, cw.z, cw.w};
-                int e[4][4];
+                uint4 cw[ROWS];
+                uint2 h[ROWS];
 #pragma unroll
-                for (int j = 0; j < 4; j++)
+                for (int r = 0; r < ROWS; r++) {
+                    cw[r] = *reinterpret_cast<const uint4 *>(rc[r] + b * 64u + qd * 16u);
+                    h[r] = *reinterpret_cast<const uint2 *>(rh[r] + b * 8u);
+                }
 #pragma unroll
-                    for (int i = 0; i < 4; i++) e[j][i] = (int)((cwa[j] >> (2 * i)) & 0x03030303u);
+                for (int r = 0; r < ROWS; r++) {
+                    const float base = half_ftz(reinterpret_cast<const uint8_t *>(&h[r]));
+                    const float offs = half_ftz(reinterpret_cast<const uint8_t *>(&h[r]) + 2);
+                    const uint32_t sb = (h[r].y >> (8 * qd)) & 0xFFu;  // octants 2qd (low nibble), 2qd+1 (high)
+                    const float eff0 = base * ((float)(sb & 15u) * (1.0f / 8.0f));
+                    const float eff1 = base * ((float)(sb >> 4) * (1.0f / 8.0f));
+                    const uint32_t cwa[4] = {cw[r].x, cw[r].y, cw[r].z, cw[r].w};
+                    int e[4][4];
 #pragma unroll
-                for (int k = 0; k < kGemvTokens; k++) {
-                    if ((uint32_t)k >= nt) break;
-                    const int8_t *ta = act + (size_t)k * tok_bytes + b * 320u + qd * 80u;
-                    int d[2] = {0, 0};
+                    for (int j = 0; j < 4; j++)
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const int4 a = *reinterpret_cast<const int4 *>(ta + 16 * j);
-                        d[j >> 1] = __dp4a(e[j][0], a.x, d[j >> 1]);
-                        d[j >> 1] = __dp4a(e[j][1], a.y, d[j >> 1]);
-                        d[j >> 1] = __dp4a(e[j][2], a.z, d[j >> 1]);
-                        d[j >> 1] = __dp4a(e[j][3], a.w, d[j >> 1]);
+                        for (int i = 0; i < 4; i++) e[j][i] = (int)((cwa[j] >> (2 * i)) & 0x03030303u);
+#pragma unroll
+                    for (int k = 0; k < TOKS; k++) {
+                        if ((uint32_t)k >= nt) break;
+                        const int8_t *ta = act + (size_t)k * tok_bytes + b * 320u + qd * 80u;
+                        int d[2] = {0, 0};
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const int4 a = *reinterpret_cast<const int4 *>(ta + 16 * j);
+                            d[j >> 1] = __dp4a(e[j][0], a.x, d[j >> 1]);
+                            d[j >> 1] = __dp4a(e[j][1], a.y, d[j >> 1]);
+                            d[j >> 1] = __dp4a(e[j][2], a.z, d[j >> 1]);
+                            d[j >> 1] = __dp4a(e[j][3], a.w, d[j >> 1]);
+                        }
+                        const int *os = osum + k * nblk * 8u + b * 8u + 2 * qd;
+                        const int s0 = os[0], s1 = os[1];
+                        acc[r][k] += eff0 * (float)(d[0] - s0) + eff1 * (float)(d[1] - s1) + offs * (float)(s0 + s1);
                     }
-                    const int *os = osum + k * nblk * 8u + b * 8u + 2 * qd;
-                    const int s0 = os[0], s1 = os[1];
-                    acc[k] += eff0 * (float)(d[0] - s0) + eff1 * (float)(d[1] - s1) + offs * (float)(s0 + s1);
                 }
             }
 #pragma unroll
-            for (int k = 0; k < kGemvTokens; k++) {
-                if ((uint32_t)k >= nt) break;
-                float v = acc[k];
+            for (int r = 0; r < ROWS; r++) {
+                if (r > 0 && rr[r] == row) break;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0)
-                    out[(uint64_t)(t0 + k) * out_stride + row] = v * (in_scales ? in_scales[t0 + k] : in_scale);
+                for (int k = 0; k < TOKS; k++) {
+                    if ((uint32_t)k >= nt) break;
+                    float v = acc[r][k];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (lane == 0)
+                        out[(uint64_t)(t0 + k) * out_stride + rr[r]] =
+                            v * (in_scales ? in_scales[t0 + k] : in_scale);
+                }
             }
         }
     }
@@ -371,15 +392,27 @@ int gemv_execute(Context *c, const QwnCudaGemmRequest *r, QwnCudaTelemetry *tel)
         set_error("HyperVSQ-2 GEMV: cols too large for one token's activations in shared memory");
         return QWN_CUDA_STATUS_UNSUPPORTED;
     }
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(hypervsq2_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   200 << 10);
+    // one token (decode): four rows per warp iteration; more tokens: two
+    const bool single = r->batch == 1;
+    const void *kern = single ? (const void *)hypervsq2_gemv_kernel<1, 4> : (const void *)hypervsq2_gemv_kernel<kGemvTokens, 2>;
+    const uint32_t rows_per = single ? 4u : 2u;
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 << 10);
     if (e == cudaSuccess) {
-        int sms = 0;
+        int sms = 0, per_sm = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device);
-        const uint32_t grid = std::min<uint32_t>((r->rows + kGemvWarps - 1) / kGemvWarps, (uint32_t)std::max(1, sms) * 4u);
-        hypervsq2_gemv_kernel<<<grid, kGemvWarps * 32, smem, c->stream>>>(
-            t->codes(), t->hdr(), c->d_in, r->input_scale, r->input_scales ? c->d_scales : nullptr, c->d_out,
-            r->batch, r->rows, r->cols, t->nblk, ist, ost, tpp);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGemvWarps * 32, smem);
+        // every resident warp streams rows: the GEMV is bound by the loads in flight
+        const uint32_t grid = std::min<uint32_t>((r->rows + rows_per * kGemvWarps - 1) / (rows_per * kGemvWarps),
+                                                 (uint32_t)std::max(1, sms) * (uint32_t)std::max(1, per_sm));
+        const float *isc = r->input_scales ? c->d_scales : nullptr;
+        if (single)
+            hypervsq2_gemv_kernel<1, 4><<<grid, kGemvWarps * 32, smem, c->stream>>>(
+                t->codes(), t->hdr(), c->d_in, r->input_scale, isc, c->d_out, r->batch, r->rows, r->cols, t->nblk,
+                ist, ost, tpp);
+        else
+            hypervsq2_gemv_kernel<kGemvTokens, 2><<<grid, kGemvWarps * 32, smem, c->stream>>>(
+                t->codes(), t->hdr(), c->d_in, r->input_scale, isc, c->d_out, r->batch, r->rows, r->cols, t->nblk,
+                ist, ost, tpp);
         count_launch();
         e = cudaGetLastError();
     }
