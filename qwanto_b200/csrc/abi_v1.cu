@@ -259,28 +259,46 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     for (uint32_t t0 = 0; t0 < batch; t0 += tokens_per_pass) {
         const uint32_t nt = min(tokens_per_pass, batch - t0);
         __syncthreads();  // the previous pass is done with the staged tokens
-        // stage the permuted activation words: word w of token t = quarter
-        // (b, qd), group g = (w>>2)&3, lane-word i = w&3
-        const uint32_t words = nblk * 64u;  // 4-byte words of one token's padded row
-        for (uint32_t idx = threadIdx.x; idx < nt * words; idx += blockDim.x) {
-            const uint32_t tt = idx / words, w = idx % words;
-            const uint32_t b = w >> 6, q = (w >> 4) & 3, g = (w >> 2) & 3, i = w & 3;
-            const uint32_t c0 = b * 256u + q * 64u + g * 16u + i;
-            const int8_t *ip = in + (uint64_t)(t0 + tt) * in_stride;
-            uint32_t v = 0;
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const uint32_t c = c0 + 4u * k;
-                v |= (uint32_t)(uint8_t)(c < cols ? ip[c] : 0) << (8 * k);
-            }
-            *reinterpret_cast<uint32_t *>(act + (size_t)tt * tok_bytes + b * 320u + q * 80u + g * 16u + i * 4u) = v;
-        }
+        // stage one octant (32 activations) per thread: its two groups of 16
+        // permuted (a 4x4 byte transpose) and its sum; zero past cols
+        const bool vec = (in_stride & 15u) == 0;
         for (uint32_t idx = threadIdx.x; idx < nt * nblk * 8u; idx += blockDim.x) {
-            const uint32_t tt = idx / (nblk * 8u), o = idx % (nblk * 8u);
-            const int8_t *ip = in + (uint64_t)(t0 + tt) * in_stride;
+            const uint32_t tt = idx / (nblk * 8u), og = idx % (nblk * 8u);
+            const uint32_t c0 = og * 32u;
+            const int8_t *ip = in + (uint64_t)(t0 + tt) * in_stride + c0;
+            uint32_t wv[8];
+            if (vec && c0 + 32u <= cols) {
+                const uint4 x0 = *reinterpret_cast<const uint4 *>(ip);
+                const uint4 x1 = *reinterpret_cast<const uint4 *>(ip + 16);
+                wv[0] = x0.x; wv[1] = x0.y; wv[2] = x0.z; wv[3] = x0.w;
+                wv[4] = x1.x; wv[5] = x1.y; wv[6] = x1.z; wv[7] = x1.w;
+            } else {
+#pragma unroll
+                for (int m = 0; m < 8; m++) {
+                    uint32_t v = 0;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const uint32_t c = c0 + 4u * m + k;
+                        v |= (uint32_t)(uint8_t)(c < cols ? ip[4 * m + k] : 0) << (8 * k);
+                    }
+                    wv[m] = v;
+                }
+            }
             int s = 0;
-            for (uint32_t c = o * 32u; c < o * 32u + 32u && c < cols; c++) s += ip[c];
-            osum[tt * nblk * 8u + o] = s;
+#pragma unroll
+            for (int m = 0; m < 8; m++) s = __dp4a((int)wv[m], 0x01010101, s);
+            osum[tt * nblk * 8u + og] = s;
+            const uint32_t blk = og >> 3, ol = og & 7u;
+            int8_t *dst = act + (size_t)tt * tok_bytes + blk * 320u + (ol >> 1) * 80u + (ol & 1u) * 32u;
+#pragma unroll
+            for (int gg = 0; gg < 2; gg++) {
+                const uint32_t *W = wv + 4 * gg;
+                const uint32_t p0 = __byte_perm(W[0], W[1], 0x5140), p1 = __byte_perm(W[2], W[3], 0x5140);
+                const uint32_t p2 = __byte_perm(W[0], W[1], 0x7362), p3 = __byte_perm(W[2], W[3], 0x7362);
+                *reinterpret_cast<uint4 *>(dst + 16 * gg) =
+                    make_uint4(__byte_perm(p0, p1, 0x5410), __byte_perm(p0, p1, 0x7632), __byte_perm(p2, p3, 0x5410),
+                               __byte_perm(p2, p3, 0x7632));
+            }
         }
         __syncthreads();
         // ROWS rows per iteration (rows row, row + wtot, ...): all their code
