@@ -101,6 +101,10 @@ class RefTQCache(C.Structure):
                 ("token_stride_v", C.c_size_t), ("total_bytes", C.c_size_t)]
 
 
+class RefLinearState(C.Structure):  # QwantoLinearAttentionState, c/qwanto_attention.h:11-15
+    _fields_ = [("n_heads", C.c_int), ("head_dim", C.c_int), ("state", C.POINTER(C.c_float))]
+
+
 class RefBlockPool(C.Structure):
     """c/qwn_paged_kv.h:15-25"""
     _fields_ = [("key_data", u16p), ("val_data", u16p), ("free_stack", i32p),
@@ -144,6 +148,7 @@ def lib():
         _decl(L, "qor_tile_bytes", C.c_size_t, C.c_int)
         _decl(L, "qor_tile_store", None, C.c_int, u8p, C.c_int, f32p, f32p)
         _decl(L, "qor_tile_dequant", C.c_float, C.c_int, u8p, C.c_int, C.c_int, C.c_int)
+        _decl(L, "qor_linear_attention_decode", None, f32p, C.c_int, C.c_int, f32p, f32p, f32p, C.c_float, f32p)
         _decl(L, "qor_tile_load", None, C.c_int, u8p, C.c_int, C.c_int, i16p, f32p)
         _decl(L, "qor_pool_init", C.c_int, C.POINTER(QorPool), C.c_int, C.c_int, C.c_int,
               C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64)
@@ -213,6 +218,12 @@ def ref():
             _decl(R, "qref_batch_destroy", None, C.c_void_p)
             _decl(R, "qref_max_threads", C.c_int)
             _decl(R, "qref_set_threads", None, C.c_int)
+            _decl(R, "qwanto_linear_attention_init", C.c_int, C.POINTER(RefLinearState), C.c_int, C.c_int)
+            _decl(R, "qwanto_linear_attention_destroy", None, C.POINTER(RefLinearState))
+            _decl(R, "qwanto_linear_attention_decode", None, C.POINTER(RefLinearState), f32p, f32p, f32p,
+                  C.c_float, f32p)
+            _decl(R, "qwanto_linear_attention_prefill", None, C.POINTER(RefLinearState), f32p, f32p, f32p,
+                  C.c_float, C.c_int, f32p)
             _decl(R, "qref_f16_write", C.c_int, f32p, f32p, C.c_int, C.c_int, C.POINTER(C.c_uint16),
                   C.POINTER(C.c_uint16))
             _ref = R

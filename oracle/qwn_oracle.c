@@ -934,3 +934,24 @@ int qor_pool_evict(QorPool *p, int nseqs, const int32_t *seq_ids, const float *m
     free(dead);
     return total;
 }
+
+/* ======================================================================== */
+/* linear attention (c/qwanto_attention.c:34-156)                            */
+/* ======================================================================== */
+void qor_linear_attention_decode(float *state, int n_heads, int head_dim, const float *q,
+                                 const float *k, const float *v, float decay, float *o) {
+    const int d = head_dim;
+    for (int h = 0; h < n_heads; h++) {
+        float *s = state + (size_t)h * d * d;
+        const float *qh = q + (size_t)h * d, *kh = k + (size_t)h * d, *vh = v + (size_t)h * d;
+        float *oh = o + (size_t)h * d;
+        for (int i = 0; i < d; i++)
+            for (int j = 0; j < d; j++) {
+                volatile float kv = kh[i] * vh[j]; /* rounded product, as _mm256_mul_ps */
+                s[(size_t)i * d + j] = fmaf(decay, s[(size_t)i * d + j], kv);
+            }
+        for (int j = 0; j < d; j++) oh[j] = 0.0f;
+        for (int i = 0; i < d; i++)
+            for (int j = 0; j < d; j++) oh[j] = fmaf(qh[i], s[(size_t)i * d + j], oh[j]);
+    }
+}

@@ -176,6 +176,14 @@ int qor_pool_evict(QorPool *p, int nseqs, const int32_t *seq_ids, const float *m
 /* seeded Bernoulli(prob) eviction trigger for (seed, step, seq) */
 int qor_evict_trigger(uint64_t seed, uint32_t step, uint32_t seq, double prob);
 
+/* ---- linear attention (c/qwanto_attention.c:34-156) -------------------- */
+/* One decode step over n_heads states of head_dim x head_dim (row i = key
+ * dim, column j = value dim): S[i][j] = fma(decay, S[i][j], RN(k_i * v_j)),
+ * then O[j] = fma chain over i ascending of q_i * S[i][j] starting from 0 --
+ * the order and roundings of the reference's AVX2/AVX-512 paths. */
+void qor_linear_attention_decode(float *state, int n_heads, int head_dim, const float *q,
+                                 const float *k, const float *v, float decay, float *o);
+
 #ifdef __cplusplus
 }
 #endif

@@ -296,6 +296,36 @@ def test_f16_attention_oracle_vs_reference_live(oracle_mod, ref_lib):
         np.testing.assert_allclose(ours, ctx, rtol=1e-5, atol=1e-6)
 
 
+def test_linear_attention_matches_reference_live(oracle_mod, ref_lib):
+    """Linear-attention decode and prefill (c/qwanto_attention.c:34-156, the
+    AVX2 path the reference is built with) against the oracle's restatement:
+    states and outputs bit-exact over several steps."""
+    rng = np.random.default_rng(21)
+    H, D, T = 3, 128, 6
+    st = oracle_mod.RefLinearState()
+    assert ref_lib.qwanto_linear_attention_init(C.byref(st), H, D) == 0
+    mine = np.zeros((H, D, D), np.float32)
+    q = rng.standard_normal((T, H, D)).astype(np.float32)
+    k = rng.standard_normal((T, H, D)).astype(np.float32)
+    v = rng.standard_normal((T, H, D)).astype(np.float32)
+    decay = np.float32(0.93)
+    ref_o = np.zeros((T, H, D), np.float32)
+    ref_lib.qwanto_linear_attention_prefill(C.byref(st), oracle_mod._ptr(q, oracle_mod.f32p),
+                                            oracle_mod._ptr(k, oracle_mod.f32p), oracle_mod._ptr(v, oracle_mod.f32p),
+                                            C.c_float(decay), T, oracle_mod._ptr(ref_o, oracle_mod.f32p))
+    for s in range(T):
+        o = np.zeros((H, D), np.float32)
+        oracle_mod.lib().qor_linear_attention_decode(oracle_mod._ptr(mine, oracle_mod.f32p), H, D,
+                                                     oracle_mod._ptr(q[s], oracle_mod.f32p),
+                                                     oracle_mod._ptr(k[s], oracle_mod.f32p),
+                                                     oracle_mod._ptr(v[s], oracle_mod.f32p), C.c_float(decay),
+                                                     oracle_mod._ptr(o, oracle_mod.f32p))
+        assert np.array_equal(o, ref_o[s])
+    ref_state = np.ctypeslib.as_array(st.state, shape=(H, D, D))
+    assert np.array_equal(mine, ref_state)
+    ref_lib.qwanto_linear_attention_destroy(C.byref(st))
+
+
 # ------------------------------------------------------- oracle internals ---
 
 def test_f16_rne_matches_numpy(oracle_mod):
