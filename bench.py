@@ -833,6 +833,98 @@ def run_gemv(args) -> int:
     return 0
 
 
+def run_linear(args) -> int:
+    """Linear attention (qwn_linear_attention_*): decode over a batch of
+    sequences' states and prefill of one long sequence, each timed with CUDA
+    events on device buffers, end to end through the host-buffer call, and
+    against the reference's own qwanto_linear_attention_decode/prefill
+    (oracle/_ref, built from c/qwanto_attention.c) on the host cores.  The
+    decode state is larger than L2, so every timed step streams it from HBM.
+    One JSON line per workload."""
+    import ctypes as C
+    import torch
+    from qwanto_b200.linear_attention import LinearAttentionState
+    peak, peak_kind = peaks()
+    ref = None
+    try:
+        sys.path.insert(0, ROOT)
+        from oracle import oracle as _ora
+        ref = _ora.ref()
+    except Exception:
+        ref = None
+    fp = lambda a: a.ctypes.data_as(C.POINTER(C.c_float))
+    rng = np.random.default_rng(3)
+    decay = 0.97
+    steps = args.steps or 20
+    for name, H, D, T in (("decode: 96 sequences x 32 heads, head_dim 128", 3072, 128, 1),
+                          ("decode: 8 sequences x 32 heads, head_dim 64", 256, 64, 1),
+                          ("prefill: 1 sequence x 32 heads, head_dim 128, 4096 tokens", 32, 128, 4096),
+                          ("prefill: 16 sequences x 32 heads, head_dim 128, 512 tokens", 512, 128, 512)):
+        st = LinearAttentionState(H, D)
+        ring = 4 if T == 1 else 1
+        q, k, v = (torch.randn((ring, T, H, D), device="cuda") * 0.1 for _ in range(3))
+        o = torch.empty((ring, T, H, D), device="cuda")
+        for i in range(args.warmup):
+            st.prefill(q[i % ring], k[i % ring], v[i % ring], decay, T, o[i % ring])
+        torch.cuda.synchronize()
+        n = steps if T == 1 else max(3, steps // 4)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        clocks = ClockSampler(0)
+        clocks.start()
+        time.sleep(0.3)
+        w0 = time.perf_counter()
+        ev[0].record()
+        for i in range(n):
+            st.prefill(q[i % ring], k[i % ring], v[i % ring], decay, T, o[i % ring])
+        ev[1].record()
+        torch.cuda.synchronize()
+        w1 = time.perf_counter()
+        clocks.stop()
+        us = ev[0].elapsed_time(ev[1]) * 1000.0 / n
+        state_bytes = 4 * H * D * D
+        moved = 2 * state_bytes + 16 * T * H * D  # state read+write once, q/k/v in, o out
+        line = {"linear_attention": name, "n_heads": H, "head_dim": D, "tokens": T, "steps": n,
+                "kernel_us": us, "tokens_per_s": T / (us * 1e-6),
+                "roofline": {"bound": "hbm", "achieved": moved / (us * 1e-6) / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": moved / (us * 1e-6) / 1e9 / peak, "peak_kind": peak_kind,
+                             "algorithmic_bytes": moved},
+                "clocks": clocks.summary(w0, w1)}
+        # end to end through the host-buffer call (pinned host inputs, output read back)
+        hq, hk, hv = (x[0].cpu().pin_memory() for x in (q, k, v))
+        ho = torch.empty((T, H, D)).pin_memory()
+        e2e_n = 5 if T == 1 else 2
+        st.prefill_host(hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), decay, T, ho.data_ptr())
+        t0 = time.perf_counter()
+        for _ in range(e2e_n):
+            st.prefill_host(hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), decay, T, ho.data_ptr())
+        e2e_s = (time.perf_counter() - t0) / e2e_n
+        line["e2e"] = {"tokens_per_s": T / e2e_s, "ms": e2e_s * 1e3, "h2d_bytes": 12 * T * H * D,
+                       "d2h_bytes": 4 * T * H * D}
+        st.close()
+        if ref is not None and not args.no_cpu_baseline:
+            # the reference on the host cores: a bounded sample of the same workload
+            rs = _ora.RefLinearState()
+            assert ref.qwanto_linear_attention_init(C.byref(rs), H, D) == 0
+            nt = 2 if T == 1 else max(4, min(T, int(5e8 / (2 * H * D * D))))
+            cq, ck, cv = ((rng.standard_normal((nt, H, D)) * 0.1).astype(np.float32) for _ in range(3))
+            co = np.empty((nt, H, D), np.float32)
+            t0 = time.perf_counter()
+            reps = 0
+            while True:
+                ref.qwanto_linear_attention_prefill(C.byref(rs), fp(cq), fp(ck), fp(cv), C.c_float(decay), nt, fp(co))
+                reps += 1
+                if time.perf_counter() - t0 > 3.0:
+                    break
+            cpu_s = (time.perf_counter() - t0) / (reps * nt)
+            ref.qwanto_linear_attention_destroy(C.byref(rs))
+            line["cpu_reference"] = {"tokens_per_s": 1.0 / cpu_s, "cores": 1, "kind": "reference",
+                                     "sample": f"{reps * nt} token steps of the same shape"}
+            line["speedup_kernel"] = line["tokens_per_s"] / line["cpu_reference"]["tokens_per_s"]
+            line["speedup_e2e"] = line["e2e"]["tokens_per_s"] / line["cpu_reference"]["tokens_per_s"]
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -854,9 +946,13 @@ def main():
                     help="cfg4 at N>1: partials exchanged in-kernel over NVLink (p2p) or by an NCCL all-gather")
     ap.add_argument("--layers", type=int, default=0, help="override the config's layer count (profiling)")
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling)")
+    ap.add_argument("--linear", action="store_true",
+                    help="time linear-attention decode/prefill against the reference CPU code (one line per shape)")
     args = ap.parse_args()
     if args.gemv:
         return run_gemv(args)
+    if args.linear:
+        return run_linear(args)
     if args.warmup < 3:
         args.warmup = 3  # the timing rules want >= 3 warm-up steps
     wl = with_codec(workload(args.config), args.codec)

@@ -45,7 +45,8 @@ enum {
     QWN_CUDA_CAP_TQ_KV = 1ull << 7,           /* 4-bit and 3.5-bit codecs */
     QWN_CUDA_CAP_BATCHED_DEVICE = 1ull << 8,  /* device-pointer batched decode */
     QWN_CUDA_CAP_SPLIT_KV_MERGE = 1ull << 9,  /* partial (m,l,o) export + merge */
-    QWN_CUDA_CAP_PAGE_EVICTION = 1ull << 10   /* page scores, eviction, compaction */
+    QWN_CUDA_CAP_PAGE_EVICTION = 1ull << 10,  /* page scores, eviction, compaction */
+    QWN_CUDA_CAP_LINEAR_ATTENTION = 1ull << 11 /* qwn_linear_attention_* */
 };
 
 typedef enum {
@@ -333,6 +334,51 @@ QWN_CUDA_ABI_API int qwn_kv_memcpy_d2h(void *host, const void *dev, uint64_t byt
 QWN_CUDA_ABI_API int qwn_kv_memcpy_h2d(void *dev, const void *host, uint64_t bytes);
 /* kernel launches issued by this library since load (for evidence in runs) */
 QWN_CUDA_ABI_API uint64_t qwn_kv_launch_count(void);
+
+/* ---- linear attention on a device-resident state ------------------------
+ * Mirrors QwantoLinearAttentionState and qwanto_linear_attention_init/reset/
+ * destroy/decode/prefill (c/qwanto_attention.h:11-72, c/qwanto_attention.c:
+ * 11-156); the first three fields keep the reference struct's order, with
+ * `state` a DEVICE pointer to [n_heads][head_dim][head_dim] fp32 (row = key
+ * dim, column = value dim).  Per token and head:
+ *     S[i][j] = fma(decay, S[i][j], RN(k_i * v_j)),
+ *     O[j]    = fma chain over i = 0..head_dim-1 of q_i * S[i][j] from 0,
+ * the reference's AVX2/AVX-512 order and rounding, so states and outputs are
+ * bit-identical to the reference built with -mavx2 -mfma for head_dim % 8 ==
+ * 0 (its SIMD paths).  Batched sequences are more heads: n_heads = sequences
+ * x heads with q/k/v/o laid out [seq_len][n_heads][head_dim].
+ * head_dim 1..512.  The *_host call copies host buffers in and out and
+ * synchronises, like the reference call it replaces; the others enqueue on
+ * `stream` (NULL = default stream) and return. */
+typedef struct {
+    int32_t n_heads;
+    int32_t head_dim;
+    float *state;          /* device [n_heads][head_dim][head_dim] fp32 */
+    int32_t device_id;
+    uint32_t reserved;
+    void *staging;         /* library-owned device scratch of the *_host call */
+    uint64_t staging_bytes;
+} QwnLinearAttentionState;
+
+/* <- qwanto_linear_attention_init (c/qwanto_attention.c:11-19): allocates and zeroes */
+QWN_CUDA_ABI_API int qwn_linear_attention_init(QwnLinearAttentionState *state, int32_t device_id,
+                                               int32_t n_heads, int32_t head_dim);
+/* <- qwanto_linear_attention_reset (c/qwanto_attention.c:21-25) */
+QWN_CUDA_ABI_API int qwn_linear_attention_reset(QwnLinearAttentionState *state, void *stream);
+/* <- qwanto_linear_attention_destroy (c/qwanto_attention.c:27-32) */
+QWN_CUDA_ABI_API int qwn_linear_attention_destroy(QwnLinearAttentionState *state);
+/* <- qwanto_linear_attention_decode (c/qwanto_attention.c:34-142); q/k/v/o [n_heads][head_dim] */
+QWN_CUDA_ABI_API int qwn_linear_attention_decode(QwnLinearAttentionState *state, const float *q_dev,
+                                                 const float *k_dev, const float *v_dev, float decay,
+                                                 float *o_dev, void *stream);
+/* <- qwanto_linear_attention_prefill (c/qwanto_attention.c:144-156); [seq_len][n_heads][head_dim] */
+QWN_CUDA_ABI_API int qwn_linear_attention_prefill(QwnLinearAttentionState *state, const float *q_dev,
+                                                  const float *k_dev, const float *v_dev, float decay,
+                                                  int32_t seq_len, float *o_dev, void *stream);
+/* the same prefill on HOST buffers (copies in, runs, copies out, synchronises) */
+QWN_CUDA_ABI_API int qwn_linear_attention_prefill_host(QwnLinearAttentionState *state, const float *q,
+                                                       const float *k, const float *v, float decay,
+                                                       int32_t seq_len, float *o);
 
 #ifdef __cplusplus
 }

@@ -184,6 +184,11 @@ class SplitRequest(C.Structure):
                 ("value_dev", C.c_void_p), ("output_dev", C.c_void_p), ("t_begin", C.c_uint32),
                 ("t_end", C.c_uint32), ("peers", C.c_void_p), ("stream", C.c_void_p)]
 
+class LinearAttentionState(C.Structure):
+    _fields_ = [("n_heads", C.c_int32), ("head_dim", C.c_int32), ("state", C.c_void_p), ("device_id", C.c_int32),
+                ("reserved", C.c_uint32), ("staging", C.c_void_p), ("staging_bytes", C.c_uint64)]
+
+
 _P = C.POINTER
 _SIGS = {
     "qwn_cuda_abi_query": (C.c_int, [_P(AbiInfo)]),
@@ -234,6 +239,15 @@ _SIGS = {
     "qwn_kv_memcpy_d2h": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64]),
     "qwn_kv_memcpy_h2d": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64]),
     "qwn_kv_launch_count": (C.c_uint64, []),
+    "qwn_linear_attention_init": (C.c_int, [_P(LinearAttentionState), C.c_int32, C.c_int32, C.c_int32]),
+    "qwn_linear_attention_reset": (C.c_int, [_P(LinearAttentionState), C.c_void_p]),
+    "qwn_linear_attention_destroy": (C.c_int, [_P(LinearAttentionState)]),
+    "qwn_linear_attention_decode": (C.c_int, [_P(LinearAttentionState), C.c_void_p, C.c_void_p, C.c_void_p,
+                                              C.c_float, C.c_void_p, C.c_void_p]),
+    "qwn_linear_attention_prefill": (C.c_int, [_P(LinearAttentionState), C.c_void_p, C.c_void_p, C.c_void_p,
+                                               C.c_float, C.c_int32, C.c_void_p, C.c_void_p]),
+    "qwn_linear_attention_prefill_host": (C.c_int, [_P(LinearAttentionState), C.c_void_p, C.c_void_p,
+                                                    C.c_void_p, C.c_float, C.c_int32, C.c_void_p]),
 }
 
 _lib = None

@@ -18,7 +18,7 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "qwn_cuda.so")
 
-SOURCES = ["kv_pool.cu", "kv_attention.cu", "kv_evict.cu", "abi_v1.cu"]
+SOURCES = ["kv_pool.cu", "kv_attention.cu", "kv_evict.cu", "abi_v1.cu", "linear_attention.cu"]
 HEADERS = [os.path.join(CSRC, "kv_internal.cuh"), os.path.join(CSRC, "kv_store.cuh"), os.path.join(INCLUDE, "qwn_cuda_abi.h"),
            os.path.join(INCLUDE, "qwn_kv_b200.h")]
 

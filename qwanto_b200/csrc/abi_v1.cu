@@ -468,7 +468,7 @@ QWN_CUDA_ABI_API int qwn_cuda_abi_query(QwnCudaAbiInfo *info) {
                             QWN_CUDA_CAP_RESIDENT_WEIGHTS | QWN_CUDA_CAP_TELEMETRY |
                             QWN_CUDA_CAP_DEVICE_ENUMERATION | QWN_CUDA_CAP_Q8_KV | QWN_CUDA_CAP_PAGED_KV |
                             QWN_CUDA_CAP_TQ_KV | QWN_CUDA_CAP_BATCHED_DEVICE | QWN_CUDA_CAP_SPLIT_KV_MERGE |
-                            QWN_CUDA_CAP_PAGE_EVICTION;
+                            QWN_CUDA_CAP_PAGE_EVICTION | QWN_CUDA_CAP_LINEAR_ATTENTION;
     info->max_devices = 16;
     info->max_resident_tensors = QWN_CUDA_MAX_RESIDENT_TENSORS;
     info->hypervsq2_block_bytes = QWN_CUDA_HYPERVSQ2_BLOCK_BYTES;

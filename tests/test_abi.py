@@ -87,6 +87,38 @@ def test_struct_layouts_match_ctypes_mirror():
             assert int(ours[f"{name}.{f}"]) == getattr(cls, f).offset, f"{name}.{f}"
 
 
+def test_linear_attention_state_layout():
+    """QwnLinearAttentionState: the ctypes mirror matches the header, and the
+    first three fields sit where QwantoLinearAttentionState keeps them
+    (c/qwanto_attention.h:11-15: int, int, float *)."""
+    from qwanto_b200 import _lib
+    fields = ["n_heads", "head_dim", "state", "device_id", "reserved", "staging", "staging_bytes"]
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "qwn_kv_b200.h"', "int main(void){",
+             'printf("size %zu\\n", sizeof(QwnLinearAttentionState));']
+    lines += [f'printf("{f} %zu\\n", offsetof(QwnLinearAttentionState, {f}));' for f in fields]
+    lines.append("return 0;}")
+    with tempfile.TemporaryDirectory() as d:
+        src, exe = os.path.join(d, "p.c"), os.path.join(d, "p")
+        open(src, "w").write("\n".join(lines))
+        subprocess.run(["gcc", "-I", INCLUDE, src, "-o", exe], check=True)
+        out = dict(l.split() for l in subprocess.run([exe], check=True, capture_output=True,
+                                                     text=True).stdout.strip().splitlines())
+    assert int(out["size"]) == C.sizeof(_lib.LinearAttentionState)
+    for f in fields:
+        assert int(out[f]) == getattr(_lib.LinearAttentionState, f).offset, f
+    assert (int(out["n_heads"]), int(out["head_dim"]), int(out["state"])) == (0, 4, 8)
+
+
+def test_linear_attention_rejects_bad_arguments_without_gpu():
+    from qwanto_b200 import _lib
+    L = _lib.lib()
+    st = _lib.LinearAttentionState()
+    assert L.qwn_linear_attention_init(C.byref(st), 0, 0, 128) == -1
+    assert L.qwn_linear_attention_init(C.byref(st), 0, 4, 0) == -1
+    assert L.qwn_linear_attention_init(C.byref(st), 0, 4, 1024) == -5
+    assert L.qwn_linear_attention_decode(C.byref(st), None, None, None, C.c_float(1.0), None, None) == -1
+
+
 @pytest.mark.skipif(not os.path.exists(REF_ABI), reason="reference header not present")
 def test_struct_layouts_identical_to_reference_header():
     ours = layout_probe(INCLUDE, "qwn_cuda_abi.h")
