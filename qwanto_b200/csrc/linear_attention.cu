@@ -10,37 +10,37 @@
 // roundings (__fmul_rn / __fmaf_rn, nothing left for the compiler to
 // contract), so states and outputs are bit-identical to the reference.
 //
-// Layout: CTA = (head, 32-column block); lane = column, warp w = rows
-// w, w+8, w+16, ...  A warp's row access is one 128-byte line, so the state
-// streams through HBM fully coalesced.  The output chain is serial in the
-// rows, so the updated 32-column slice goes to shared memory and one warp
-// (decode) or one warp per buffered token (prefill) runs the chain from there.
+// Work unit: (head, 32-column block); lane = column, so a warp's access to
+// one state row is one 128-byte line and the state streams through HBM fully
+// coalesced.
 //
 //   decode : HBM-bound -- the state is read and written once per token
-//            (8 d^2 bytes per head); loads are issued 16 rows per thread at a
-//            time so each CTA has 16 KB in flight.
+//            (8 d^2 bytes per head).  Persistent CTAs; eight producer warps
+//            stream units through registers while a ninth warp runs the
+//            serial output chain of the previous unit from shared memory.
 //   prefill: the state slice stays in registers for the whole sequence (read
-//            and written once), tokens are processed in chunks of up to 8:
-//            every warp updates its rows for all chunk tokens, then each warp
-//            runs the output chain of one token of the chunk.
+//            and written once); eight warps form a systolic pipeline over the
+//            rows, each handing a token's partial output sum to the next
+//            warp, so several tokens are in flight and the chain order is
+//            unchanged.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "kv_internal.cuh"
 
 namespace qkv {
 namespace {
 
-constexpr int kLaCols = 32;   // columns per CTA
-constexpr int kLaWarps = 8;   // row stripes per CTA
+constexpr int kLaCols = 32;   // columns per work unit (one per lane)
+constexpr int kLaWarps = 8;   // row stripes (decode producers, prefill stages)
 constexpr int kLaThreads = kLaCols * kLaWarps;
 constexpr int kLaMaxDim = 512;
-constexpr int kLaDecodeUnroll = 16;
-constexpr int kLaMaxChunk = 8;
-constexpr size_t kLaSmemBudget = 200 * 1024;
 
 struct DeviceScope {
     int prev = -1;
@@ -54,117 +54,299 @@ struct DeviceScope {
     }
 };
 
-__global__ void __launch_bounds__(kLaThreads) la_decode_kernel(float *__restrict__ state, int d, int col_blocks,
-                                                               const float *__restrict__ q,
-                                                               const float *__restrict__ k,
-                                                               const float *__restrict__ v, float decay,
-                                                               float *__restrict__ o) {
-    extern __shared__ float sm[];
-    float *sk = sm, *sq = sm + d, *slice = sm + 2 * d;  // slice: [d][32]
-    const int h = blockIdx.x / col_blocks, cb = blockIdx.x - h * col_blocks;
+// ---------------------------------------------------------------------------
+// Decode.  A persistent CTA walks units (head, 32-column block) with a stride
+// of the grid.  Warps 0..7 produce: for their rows i = w, w+8, ... they load
+// the state (kLaDecodeUnroll rows per thread per batch of loads), k_i and q_i
+// (warp-uniform), write the updated state back to HBM and into the unit's
+// shared slice, and publish q into the slice's q vector.  Warp 8 consumes: it
+// runs the output chain over the slice.  Two slices alternate, handed over
+// with named barriers (FULL: producers arrive, consumer syncs; EMPTY: the
+// reverse), so the producers stream the next unit while the consumer finishes
+// the last one.
+// ---------------------------------------------------------------------------
+constexpr int kLaDecodeUnroll = 8;
+constexpr int kLaDecodeThreads = kLaThreads + 32;
+constexpr int kBarFull = 1, kBarEmpty = 3;  // ids kBarFull + b, kBarEmpty + b for b in {0, 1}
+
+template <int ID>
+__device__ __forceinline__ void named_sync() {
+    asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(kLaDecodeThreads) : "memory");
+}
+template <int ID>
+__device__ __forceinline__ void named_arrive() {
+    asm volatile("bar.arrive %0, %1;" ::"n"(ID), "n"(kLaDecodeThreads) : "memory");
+}
+__device__ __forceinline__ void sync_empty(int b) {
+    if (b) named_sync<kBarEmpty + 1>();
+    else named_sync<kBarEmpty>();
+}
+
+// FAST = head_dim a multiple of 8 x kLaDecodeUnroll: every row and column of a batch of loads exists.
+template <bool FAST>
+__global__ void __launch_bounds__(kLaDecodeThreads, 4) la_decode_kernel(float *__restrict__ state, int d,
+                                                                        int col_blocks, int units,
+                                                                        const float *__restrict__ q,
+                                                                        const float *__restrict__ k,
+                                                                        const float *__restrict__ v, float decay,
+                                                                        float *__restrict__ o) {
+    extern __shared__ __align__(16) float sm[];
+    // buffer b: slice [d][32] then q [d]
+    const int buf_floats = d * kLaCols + d;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int j = cb * kLaCols + lane;
-    const bool col = j < d;
-    const size_t hd = (size_t)h * d;
-    for (int i = threadIdx.x; i < d; i += kLaThreads) {
-        sk[i] = k[hd + i];
-        sq[i] = q[hd + i];
-    }
-    const float vj = col ? v[hd + j] : 0.f;
-    __syncthreads();
-    float *S = state + hd * d;
-    for (int i0 = w; i0 < d; i0 += kLaWarps * kLaDecodeUnroll) {
-        float s[kLaDecodeUnroll];
+    int n = 0;
+    if (w < kLaWarps) {
+        for (int unit = blockIdx.x; unit < units; unit += gridDim.x, n++) {
+            const int b = n & 1;
+            float *slice = sm + b * buf_floats, *sq = slice + d * kLaCols;
+            const int h = unit / col_blocks, cb = unit - h * col_blocks;
+            const int j = cb * kLaCols + lane;
+            const bool col = j < d;
+            const size_t hd = (size_t)h * d;
+            float *S = state + hd * d;
+            const float *kh = k + hd;
+            const float vj = col ? v[hd + j] : 0.f;
+            bool free = n < 2;  // slice b was released by the consumer (unit n - 2)
+            for (int i0 = w; i0 < d; i0 += kLaWarps * kLaDecodeUnroll) {
+                float s[kLaDecodeUnroll], kk[kLaDecodeUnroll];
+                float *Si = S + (i0 * d + j);  // row i0, column j; rows u apart are 8d floats apart
+                const int rs = kLaWarps * d;
 #pragma unroll
-        for (int u = 0; u < kLaDecodeUnroll; u++) {
-            const int i = i0 + u * kLaWarps;
-            s[u] = (col && i < d) ? S[(size_t)i * d + j] : 0.f;
-        }
+                for (int u = 0; u < kLaDecodeUnroll; u++) {
+                    const int i = i0 + u * kLaWarps;
+                    if (FAST) {
+                        s[u] = Si[u * rs];
+                        kk[u] = kh[i];
+                    } else {
+                        s[u] = (col && i < d) ? Si[u * rs] : 0.f;
+                        kk[u] = i < d ? kh[i] : 0.f;
+                    }
+                }
+                const int iq = i0 + lane * kLaWarps;
+                const bool qlane = lane < kLaDecodeUnroll && (FAST || iq < d);
+                const float qv = qlane ? q[hd + iq] : 0.f;
+                if (!free) {  // wait only once the loads are in flight
+                    sync_empty(b);
+                    free = true;
+                }
+                if (qlane) sq[iq] = qv;
 #pragma unroll
-        for (int u = 0; u < kLaDecodeUnroll; u++) {
-            const int i = i0 + u * kLaWarps;
-            if (i < d) {
-                const float ns = __fmaf_rn(decay, s[u], __fmul_rn(sk[i], vj));
-                if (col) S[(size_t)i * d + j] = ns;
-                slice[i * kLaCols + lane] = ns;
+                for (int u = 0; u < kLaDecodeUnroll; u++) {
+                    const int i = i0 + u * kLaWarps;
+                    if (FAST || i < d) {
+                        const float ns = __fmaf_rn(decay, s[u], __fmul_rn(kk[u], vj));
+                        if (FAST || col) Si[u * rs] = ns;
+                        slice[i * kLaCols + lane] = ns;
+                    }
+                }
             }
+            if (!free) sync_empty(b);  // a warp without rows (head_dim < 8) still takes its turn
+            if (b) named_arrive<kBarFull + 1>();
+            else named_arrive<kBarFull>();
         }
-    }
-    __syncthreads();
-    if (w == 0 && col) {
-        float acc = 0.f;
+        // take the consumer's last two EMPTY arrivals so both barriers end balanced
+        for (int m = max(n - 2, 0); m < n; m++) sync_empty(m & 1);
+    } else {
+        for (int unit = blockIdx.x; unit < units; unit += gridDim.x, n++) {
+            const int b = n & 1;
+            const float *slice = sm + b * buf_floats, *sq = slice + d * kLaCols;
+            const int h = unit / col_blocks, cb = unit - h * col_blocks;
+            const int j = cb * kLaCols + lane;
+            if (b) named_sync<kBarFull + 1>();
+            else named_sync<kBarFull>();
+            float acc = 0.f;
+            if (FAST) {
+#pragma unroll 4
+                for (int i = 0; i < d; i += 4) {
+                    const float4 qq = *reinterpret_cast<const float4 *>(sq + i);
+                    acc = __fmaf_rn(qq.x, slice[(i + 0) * kLaCols + lane], acc);
+                    acc = __fmaf_rn(qq.y, slice[(i + 1) * kLaCols + lane], acc);
+                    acc = __fmaf_rn(qq.z, slice[(i + 2) * kLaCols + lane], acc);
+                    acc = __fmaf_rn(qq.w, slice[(i + 3) * kLaCols + lane], acc);
+                }
+            } else {
 #pragma unroll 8
-        for (int i = 0; i < d; i++) acc = __fmaf_rn(sq[i], slice[i * kLaCols + lane], acc);
-        o[hd + j] = acc;
+                for (int i = 0; i < d; i++) acc = __fmaf_rn(sq[i], slice[i * kLaCols + lane], acc);
+            }
+            if (j < d) o[(size_t)h * d + j] = acc;
+            if (b) named_arrive<kBarEmpty + 1>();
+            else named_arrive<kBarEmpty>();
+        }
     }
 }
 
-// R = rows held per thread (>= ceil(d / 8)); chunk = tokens buffered per pass.
+// ---------------------------------------------------------------------------
+// Prefill: a systolic pipeline over the CTA's 8 warps.  Warp b holds rows
+// [b*rpw, b*rpw + rpw) of the 32-column slice in registers for the whole
+// sequence (rpw = ceil(d / 8) <= R).  Tokens go in groups of P; at step s warp
+// b works on group g = s - b: for each token of the group it updates its rows
+// with k_t and v_t and continues token t's output chain over its rows from the
+// partial sum warp b-1 produced for the same token at step s-1 (0 for warp 0),
+// then hands the P sums on (the last warp stores them).  The chain still
+// visits rows 0..d-1 in ascending order, as in the reference, while 8 groups
+// are in flight; the P chains of a group are independent, which hides the fma
+// latency; no state slice passes through shared memory.  One barrier ends
+// each step.
+//
+// k, q and the 32-column v slice arrive in chunks of 8 groups (8P tokens) by
+// cp.async into three rotating buffers: chunk m is fetched at step
+// 8(m-2) + 7 (when chunk m-3 has left the pipeline) and waited for at step 8m,
+// so its global latency overlaps ~9 steps of arithmetic.
+// ---------------------------------------------------------------------------
+constexpr int kLaGroupsPerChunk = kLaWarps;  // >= the stage count (see the wait accounting above)
+constexpr int kLaBuffers = 3;
+
+// tokens per group: 4 while three chunks fit shared memory comfortably (head_dim <= 128)
 template <int R>
-__global__ void __launch_bounds__(kLaThreads) la_prefill_kernel(float *__restrict__ state, int n_heads, int d,
-                                                                int col_blocks, int seq_len, int chunk,
-                                                                const float *__restrict__ q,
-                                                                const float *__restrict__ k,
-                                                                const float *__restrict__ v, float decay,
-                                                                float *__restrict__ o) {
-    extern __shared__ float sm[];
-    // per buffered token c: k[d], q[d], v[32], then the slices [chunk][d][32]
-    const int tok_stride = 2 * d + kLaCols;
-    float *stage = sm, *slices = sm + (size_t)chunk * tok_stride;
-    const int h = blockIdx.x / col_blocks, cb = blockIdx.x - h * col_blocks;
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int j = cb * kLaCols + lane;
-    const bool col = j < d;
-    const size_t hd = (size_t)h * d, row_stride = (size_t)n_heads * d;  // token stride of q/k/v/o
-    float *S = state + hd * d;
-    float s[R];
+__host__ __device__ constexpr int group_tokens() { return R <= 16 ? 4 : (R <= 32 ? 2 : 1); }
+
+__device__ __forceinline__ void cp_async4(float *dst, const float *src) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(a), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(float *dst, const float *src) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(a), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// One group of P tokens for one warp of the prefill pipeline: update the
+// warp's rows with each token's k and v, then continue each token's output
+// chain over them.  FULL = all P tokens exist (no guards, so the P independent
+// chains interleave).
+template <int R, bool EXACT, int P, bool FULL>
+__device__ __forceinline__ void la_group(float (&s)[R], float (&acc)[P], const float *gb, int np, int tok_floats,
+                                         int d, int r0, int rpw, int lane, float decay) {
 #pragma unroll
-    for (int u = 0; u < R; u++) {
-        const int i = w + u * kLaWarps;
-        s[u] = (col && i < d) ? S[(size_t)i * d + j] : 0.f;
-    }
-    for (int t0 = 0; t0 < seq_len; t0 += chunk) {
-        const int n = min(chunk, seq_len - t0);
-        for (int c = 0; c < n; c++) {
-            const size_t base = (size_t)(t0 + c) * row_stride + hd;
-            float *st = stage + c * tok_stride;
-            for (int i = threadIdx.x; i < d; i += kLaThreads) {
-                st[i] = k[base + i];
-                st[d + i] = q[base + i];
-            }
-            if (threadIdx.x < kLaCols) st[2 * d + threadIdx.x] = col ? v[base + j] : 0.f;
-        }
-        __syncthreads();
-        for (int c = 0; c < n; c++) {
-            const float *st = stage + c * tok_stride;
-            const float vj = st[2 * d + lane];
-            float *sl = slices + (size_t)c * d * kLaCols;
+    for (int p = 0; p < P; p++) {
+        if (FULL || p < np) {
+            const float *tb = gb + p * tok_floats;
+            const float vj = tb[2 * d + lane];
+            if (EXACT) {
 #pragma unroll
-            for (int u = 0; u < R; u++) {
-                const int i = w + u * kLaWarps;
-                if (i < d) {
-                    s[u] = __fmaf_rn(decay, s[u], __fmul_rn(st[i], vj));
-                    sl[i * kLaCols + lane] = s[u];
+                for (int u = 0; u < R; u += 4) {
+                    const float4 kk = *reinterpret_cast<const float4 *>(tb + r0 + u);
+                    const float4 qq = *reinterpret_cast<const float4 *>(tb + d + r0 + u);
+                    s[u + 0] = __fmaf_rn(decay, s[u + 0], __fmul_rn(kk.x, vj));
+                    s[u + 1] = __fmaf_rn(decay, s[u + 1], __fmul_rn(kk.y, vj));
+                    s[u + 2] = __fmaf_rn(decay, s[u + 2], __fmul_rn(kk.z, vj));
+                    s[u + 3] = __fmaf_rn(decay, s[u + 3], __fmul_rn(kk.w, vj));
+                    acc[p] = __fmaf_rn(qq.x, s[u + 0], acc[p]);
+                    acc[p] = __fmaf_rn(qq.y, s[u + 1], acc[p]);
+                    acc[p] = __fmaf_rn(qq.z, s[u + 2], acc[p]);
+                    acc[p] = __fmaf_rn(qq.w, s[u + 3], acc[p]);
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < R; u++) {
+                    const int i = r0 + u;
+                    if (u < rpw && i < d) {
+                        s[u] = __fmaf_rn(decay, s[u], __fmul_rn(tb[i], vj));
+                        acc[p] = __fmaf_rn(tb[d + i], s[u], acc[p]);
+                    }
                 }
             }
         }
-        __syncthreads();
-        for (int c = w; c < n; c += kLaWarps) {
-            if (col) {
-                const float *qc = stage + c * tok_stride + d;
-                const float *sl = slices + (size_t)c * d * kLaCols;
-                float acc = 0.f;
-#pragma unroll 8
-                for (int i = 0; i < d; i++) acc = __fmaf_rn(qc[i], sl[i * kLaCols + lane], acc);
-                o[(size_t)(t0 + c) * row_stride + hd + j] = acc;
+    }
+}
+
+// EXACT = (head_dim == 8R with R a multiple of 4) and q/k/v 16-byte aligned:
+// whole rows per warp, float4 shared reads and 16-byte cp.async; otherwise
+// every row is bounds-checked and staged with 4-byte copies.
+template <int R, bool EXACT>
+__global__ void __launch_bounds__(kLaThreads, (R <= 16 ? 2 : 1)) la_prefill_kernel(
+    float *__restrict__ state, int n_heads, int d_arg, int col_blocks, int seq_len, const float *__restrict__ q,
+    const float *__restrict__ k, const float *__restrict__ v, float decay, float *__restrict__ o) {
+    constexpr int P = group_tokens<R>();
+    constexpr int C = kLaGroupsPerChunk * P;  // tokens per chunk
+    const int d = EXACT ? kLaWarps * R : d_arg;
+    extern __shared__ __align__(16) float sm[];
+    // buffer x: [C tokens][k d | q d | v 32]; then the hand-off sums [2][8][P][32]
+    const int tok_floats = 2 * d + kLaCols, buf_floats = C * tok_floats;
+    float *hand = sm + kLaBuffers * buf_floats;
+    const int h = blockIdx.x / col_blocks, cb = blockIdx.x - h * col_blocks;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int j0 = cb * kLaCols, j = j0 + lane;
+    const bool col = j < d;
+    const int rpw = EXACT ? R : (d + kLaWarps - 1) / kLaWarps;
+    const int r0 = w * rpw;
+    const size_t hd = (size_t)h * d, row_stride = (size_t)n_heads * d;  // token stride of q/k/v/o
+    const int n_chunks = (seq_len + C - 1) / C, n_groups = (seq_len + P - 1) / P;
+
+    auto fetch = [&](int m) {  // every thread issues its share of chunk m, then commits (possibly empty)
+        if (m < n_chunks) {
+            float *buf = sm + (m % kLaBuffers) * buf_floats;
+            const int t0 = m * C, n = min(C, seq_len - t0);
+            if (EXACT) {
+                constexpr int KU = kLaWarps * R / 4;     // 16-byte units of a k (or q) row
+                constexpr int U = 2 * KU + kLaCols / 4;  // per token: k, q, v slice
+                for (int x = threadIdx.x; x < n * U; x += kLaThreads) {
+                    const int c = x / U, r = x - c * U;
+                    const size_t base = (size_t)(t0 + c) * row_stride + hd;
+                    const float *src = r < KU ? k + base + 4 * r
+                                     : r < 2 * KU ? q + base + 4 * (r - KU)
+                                                  : v + base + j0 + 4 * (r - 2 * KU);
+                    cp_async16(buf + c * tok_floats + 4 * r, src);
+                }
+            } else {
+                for (int c = 0; c < n; c++) {
+                    const size_t base = (size_t)(t0 + c) * row_stride + hd;
+                    float *dst = buf + c * tok_floats;
+                    for (int x = threadIdx.x; x < tok_floats; x += kLaThreads) {
+                        if (x < d) cp_async4(dst + x, k + base + x);
+                        else if (x < 2 * d) cp_async4(dst + x, q + base + (x - d));
+                        else if (j0 + x - 2 * d < d) cp_async4(dst + x, v + base + j0 + (x - 2 * d));
+                    }
+                }
+            }
+        }
+        cp_async_commit();
+    };
+
+    float *S = state + hd * d;
+    float s[R];  // this warp's rows of the slice, for the whole sequence
+#pragma unroll
+    for (int u = 0; u < R; u++) {
+        const int i = r0 + u;
+        s[u] = (col && u < rpw && i < d) ? S[(size_t)i * d + j] : 0.f;
+    }
+    fetch(0);
+    fetch(1);
+    const int steps = n_groups + kLaWarps - 1;
+    for (int st = 0; st < steps; st++) {
+        if (st % kLaGroupsPerChunk == 0) {  // chunk st / 8 is needed from this step on
+            cp_async_wait1();
+            __syncthreads();
+        }
+        if (st >= kLaWarps - 1 && (st - (kLaWarps - 1)) % kLaGroupsPerChunk == 0)
+            fetch((st - (kLaWarps - 1)) / kLaGroupsPerChunk + 2);
+        const int g = st - w;
+        if (g >= 0 && g < n_groups) {
+            const int t0 = g * P, np = min(P, seq_len - t0);
+            const float *gb = sm + ((t0 / C) % kLaBuffers) * buf_floats + (t0 % C) * tok_floats;
+            float acc[P];
+            const float *hin = hand + (((st - 1) & 1) * kLaWarps + (w - 1)) * P * kLaCols + lane;
+#pragma unroll
+            for (int p = 0; p < P; p++) acc[p] = w == 0 ? 0.f : hin[p * kLaCols];
+            if (np == P) la_group<R, EXACT, P, true>(s, acc, gb, np, tok_floats, d, r0, rpw, lane, decay);
+            else la_group<R, EXACT, P, false>(s, acc, gb, np, tok_floats, d, r0, rpw, lane, decay);
+            if (w == kLaWarps - 1) {
+#pragma unroll
+                for (int p = 0; p < P; p++)
+                    if (p < np && col) o[(size_t)(t0 + p) * row_stride + hd + j] = acc[p];
+            } else {
+                float *hout = hand + ((st & 1) * kLaWarps + w) * P * kLaCols + lane;
+#pragma unroll
+                for (int p = 0; p < P; p++) hout[p * kLaCols] = acc[p];
             }
         }
         __syncthreads();
     }
 #pragma unroll
     for (int u = 0; u < R; u++) {
-        const int i = w + u * kLaWarps;
-        if (col && i < d) S[(size_t)i * d + j] = s[u];
+        const int i = r0 + u;
+        if (col && u < rpw && i < d) S[(size_t)i * d + j] = s[u];
     }
 }
 
@@ -172,22 +354,33 @@ bool state_ok(const QwnLinearAttentionState *st) {
     return st && st->state && st->n_heads > 0 && st->head_dim > 0 && st->head_dim <= kLaMaxDim;
 }
 
-int prefill_chunk(int d) {
-    const size_t per_tok = ((size_t)d * kLaCols + 2 * d + kLaCols) * sizeof(float);
-    return (int)std::max<size_t>(1, std::min<size_t>(kLaMaxChunk, kLaSmemBudget / per_tok));
+// dynamic shared memory above 48 KB is opted into once per kernel and device
+template <typename K>
+cudaError_t allow_smem(K kernel, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    static std::mutex mu;
+    static std::map<std::pair<const void *, int>, size_t> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    size_t &have = done[{(const void *)kernel, dev}];
+    if (have >= bytes) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) have = bytes;
+    return e;
 }
 
-template <int R>
+template <int R, bool EXACT>
 cudaError_t launch_prefill_r(const QwnLinearAttentionState *st, int seq_len, const float *q, const float *k,
                              const float *v, float decay, float *o, cudaStream_t stream) {
     const int d = st->head_dim, col_blocks = (d + kLaCols - 1) / kLaCols;
-    const int chunk = prefill_chunk(d);
-    const size_t smem = ((size_t)chunk * (2 * d + kLaCols) + (size_t)chunk * d * kLaCols) * sizeof(float);
-    cudaError_t e = cudaFuncSetAttribute(la_prefill_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    constexpr int P = group_tokens<R>();
+    const size_t smem = ((size_t)kLaBuffers * kLaGroupsPerChunk * P * (2 * d + kLaCols) +
+                         2 * kLaWarps * P * kLaCols) * sizeof(float);
+    cudaError_t e = allow_smem(la_prefill_kernel<R, EXACT>, smem);
     if (e != cudaSuccess) return e;
-    la_prefill_kernel<R><<<(unsigned)(st->n_heads * col_blocks), kLaThreads, smem, stream>>>(
-        st->state, st->n_heads, d, col_blocks, seq_len, chunk, q, k, v, decay, o);
+    la_prefill_kernel<R, EXACT><<<(unsigned)(st->n_heads * col_blocks), kLaThreads, smem, stream>>>(
+        st->state, st->n_heads, d, col_blocks, seq_len, q, k, v, decay, o);
     count_launch();
     return cudaGetLastError();
 }
@@ -195,11 +388,18 @@ cudaError_t launch_prefill_r(const QwnLinearAttentionState *st, int seq_len, con
 cudaError_t launch_decode(const QwnLinearAttentionState *st, const float *q, const float *k, const float *v,
                           float decay, float *o, cudaStream_t stream) {
     const int d = st->head_dim, col_blocks = (d + kLaCols - 1) / kLaCols;
-    const size_t smem = ((size_t)2 * d + (size_t)d * kLaCols) * sizeof(float);
-    cudaError_t e = cudaFuncSetAttribute(la_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int units = st->n_heads * col_blocks;
+    const size_t smem = 2 * ((size_t)d * kLaCols + d) * sizeof(float);
+    const bool fast = d % (kLaWarps * kLaDecodeUnroll) == 0;
+    auto kernel = fast ? la_decode_kernel<true> : la_decode_kernel<false>;
+    cudaError_t e = allow_smem(kernel, smem);
     if (e != cudaSuccess) return e;
-    la_decode_kernel<<<(unsigned)(st->n_heads * col_blocks), kLaThreads, smem, stream>>>(st->state, d, col_blocks,
-                                                                                        q, k, v, decay, o);
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kLaDecodeThreads, smem);
+    const int grid = std::min(units, sms * std::max(per_sm, 1));
+    kernel<<<(unsigned)grid, kLaDecodeThreads, smem, stream>>>(st->state, d, col_blocks, units, q, k, v, decay, o);
     count_launch();
     return cudaGetLastError();
 }
@@ -207,12 +407,23 @@ cudaError_t launch_decode(const QwnLinearAttentionState *st, const float *q, con
 cudaError_t launch_step(const QwnLinearAttentionState *st, int seq_len, const float *q, const float *k,
                         const float *v, float decay, float *o, cudaStream_t stream) {
     if (seq_len == 1) return launch_decode(st, q, k, v, decay, o, stream);
-    const int r = (st->head_dim + kLaWarps - 1) / kLaWarps;
-    if (r <= 4) return launch_prefill_r<4>(st, seq_len, q, k, v, decay, o, stream);
-    if (r <= 8) return launch_prefill_r<8>(st, seq_len, q, k, v, decay, o, stream);
-    if (r <= 16) return launch_prefill_r<16>(st, seq_len, q, k, v, decay, o, stream);
-    if (r <= 32) return launch_prefill_r<32>(st, seq_len, q, k, v, decay, o, stream);
-    return launch_prefill_r<64>(st, seq_len, q, k, v, decay, o, stream);
+    const int d = st->head_dim, r = (d + kLaWarps - 1) / kLaWarps;
+    const bool aligned = ((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16 == 0;
+    if (aligned && d % (4 * kLaWarps) == 0) {  // whole rows per warp, 16-byte staging
+        switch (d / kLaWarps) {
+            case 4: return launch_prefill_r<4, true>(st, seq_len, q, k, v, decay, o, stream);
+            case 8: return launch_prefill_r<8, true>(st, seq_len, q, k, v, decay, o, stream);
+            case 16: return launch_prefill_r<16, true>(st, seq_len, q, k, v, decay, o, stream);
+            case 32: return launch_prefill_r<32, true>(st, seq_len, q, k, v, decay, o, stream);
+            default: break;
+        }
+    }
+    if (r <= 2) return launch_prefill_r<2, false>(st, seq_len, q, k, v, decay, o, stream);
+    if (r <= 4) return launch_prefill_r<4, false>(st, seq_len, q, k, v, decay, o, stream);
+    if (r <= 8) return launch_prefill_r<8, false>(st, seq_len, q, k, v, decay, o, stream);
+    if (r <= 16) return launch_prefill_r<16, false>(st, seq_len, q, k, v, decay, o, stream);
+    if (r <= 32) return launch_prefill_r<32, false>(st, seq_len, q, k, v, decay, o, stream);
+    return launch_prefill_r<64, false>(st, seq_len, q, k, v, decay, o, stream);
 }
 
 int finish(const char *what, cudaError_t e) {

@@ -43,7 +43,7 @@ def _state_of(torch, st):
     return host
 
 
-@pytest.mark.parametrize("H,D", [(4, 128), (3, 64), (2, 256), (1, 512), (5, 24), (2, 8), (2, 96)])
+@pytest.mark.parametrize("H,D", [(4, 128), (3, 64), (2, 256), (1, 512), (5, 24), (2, 8), (2, 96), (3, 4), (300, 32)])
 def test_decode_steps_bit_exact(cuda, oracle_mod, H, D):
     from qwanto_b200.linear_attention import LinearAttentionState
     torch = cuda
@@ -62,7 +62,7 @@ def test_decode_steps_bit_exact(cuda, oracle_mod, H, D):
         assert np.array_equal(_state_of(torch, st), ref_state)
 
 
-@pytest.mark.parametrize("H,D,T", [(4, 128, 19), (3, 64, 33), (2, 256, 7), (1, 512, 5), (5, 24, 9), (2, 40, 2)])
+@pytest.mark.parametrize("H,D,T", [(4, 128, 19), (3, 64, 33), (2, 256, 7), (1, 512, 5), (5, 24, 9), (2, 40, 2), (2, 4, 11), (3, 32, 17), (2, 128, 100)])
 def test_prefill_bit_exact_and_equals_decodes(cuda, oracle_mod, H, D, T):
     """Prefill from a non-zero state (two decodes first), with a ragged last
     chunk; equals the oracle and the same tokens fed one decode at a time."""
@@ -135,3 +135,27 @@ def test_batched_heads_reset_empty_and_host_call(cuda, oracle_mod):
         st.reset()
         torch.cuda.synchronize()
         assert not _state_of(torch, st).any()
+
+
+def test_prefill_unaligned_inputs_take_the_checked_path(cuda, oracle_mod):
+    """q/k/v that start 4 bytes past a 16-byte boundary: the kernel stages
+    them with 4-byte copies and still matches the oracle bit for bit."""
+    from qwanto_b200.linear_attention import LinearAttentionState
+    torch = cuda
+    H, D, T = 3, 128, 41
+    rng = np.random.default_rng(17)
+    q, k, v = _inputs(rng, T, H, D)
+    ref_state = np.zeros((H, D, D), np.float32)
+    ref_out = _oracle_steps(oracle_mod, ref_state, q, k, v, 0.95)
+    dev = []
+    for x in (q, k, v):
+        buf = torch.empty(x.size + 1, device="cuda")
+        buf[1:] = torch.from_numpy(x.reshape(-1)).cuda()
+        dev.append(buf[1:])
+    assert all(t.data_ptr() % 16 == 4 for t in dev)
+    with LinearAttentionState(H, D) as st:
+        od = torch.empty((T, H, D), device="cuda")
+        st.prefill(*dev, 0.95, T, od)
+        torch.cuda.synchronize()
+        assert np.array_equal(od.cpu().numpy(), ref_out)
+        assert np.array_equal(_state_of(torch, st), ref_state)
