@@ -213,37 +213,45 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 
 // One group of P tokens for one warp of the prefill pipeline: update the
 // warp's rows with each token's k and v, then continue each token's output
-// chain over them.  FULL = all P tokens exist (no guards, so the P independent
-// chains interleave).
-template <int R, bool EXACT, int P, bool FULL>
-__device__ __forceinline__ void la_group(float (&s)[R], float (&acc)[P], const float *gb, int np, int tok_floats,
-                                         int d, int r0, int rpw, int lane, float decay) {
+// chain over them, for each of the thread's CPT columns (lane, lane + 32, ...).
+// FULL = all P tokens exist (no guards, so the independent chains interleave).
+template <int R, bool EXACT, int P, int CPT, bool FULL>
+__device__ __forceinline__ void la_group(float (&s)[CPT][R], float (&acc)[CPT][P], const float *gb, int np,
+                                         int tok_floats, int d, int r0, int rpw, int lane, float decay) {
 #pragma unroll
     for (int p = 0; p < P; p++) {
         if (FULL || p < np) {
             const float *tb = gb + p * tok_floats;
-            const float vj = tb[2 * d + lane];
+            float vj[CPT];
+#pragma unroll
+            for (int c = 0; c < CPT; c++) vj[c] = tb[2 * d + c * kLaCols + lane];
             if (EXACT) {
 #pragma unroll
                 for (int u = 0; u < R; u += 4) {
                     const float4 kk = *reinterpret_cast<const float4 *>(tb + r0 + u);
                     const float4 qq = *reinterpret_cast<const float4 *>(tb + d + r0 + u);
-                    s[u + 0] = __fmaf_rn(decay, s[u + 0], __fmul_rn(kk.x, vj));
-                    s[u + 1] = __fmaf_rn(decay, s[u + 1], __fmul_rn(kk.y, vj));
-                    s[u + 2] = __fmaf_rn(decay, s[u + 2], __fmul_rn(kk.z, vj));
-                    s[u + 3] = __fmaf_rn(decay, s[u + 3], __fmul_rn(kk.w, vj));
-                    acc[p] = __fmaf_rn(qq.x, s[u + 0], acc[p]);
-                    acc[p] = __fmaf_rn(qq.y, s[u + 1], acc[p]);
-                    acc[p] = __fmaf_rn(qq.z, s[u + 2], acc[p]);
-                    acc[p] = __fmaf_rn(qq.w, s[u + 3], acc[p]);
+#pragma unroll
+                    for (int c = 0; c < CPT; c++) {
+                        s[c][u + 0] = __fmaf_rn(decay, s[c][u + 0], __fmul_rn(kk.x, vj[c]));
+                        s[c][u + 1] = __fmaf_rn(decay, s[c][u + 1], __fmul_rn(kk.y, vj[c]));
+                        s[c][u + 2] = __fmaf_rn(decay, s[c][u + 2], __fmul_rn(kk.z, vj[c]));
+                        s[c][u + 3] = __fmaf_rn(decay, s[c][u + 3], __fmul_rn(kk.w, vj[c]));
+                        acc[c][p] = __fmaf_rn(qq.x, s[c][u + 0], acc[c][p]);
+                        acc[c][p] = __fmaf_rn(qq.y, s[c][u + 1], acc[c][p]);
+                        acc[c][p] = __fmaf_rn(qq.z, s[c][u + 2], acc[c][p]);
+                        acc[c][p] = __fmaf_rn(qq.w, s[c][u + 3], acc[c][p]);
+                    }
                 }
             } else {
 #pragma unroll
                 for (int u = 0; u < R; u++) {
                     const int i = r0 + u;
                     if (u < rpw && i < d) {
-                        s[u] = __fmaf_rn(decay, s[u], __fmul_rn(tb[i], vj));
-                        acc[p] = __fmaf_rn(tb[d + i], s[u], acc[p]);
+#pragma unroll
+                        for (int c = 0; c < CPT; c++) {
+                            s[c][u] = __fmaf_rn(decay, s[c][u], __fmul_rn(tb[i], vj[c]));
+                            acc[c][p] = __fmaf_rn(tb[d + i], s[c][u], acc[c][p]);
+                        }
                     }
                 }
             }
@@ -253,22 +261,24 @@ __device__ __forceinline__ void la_group(float (&s)[R], float (&acc)[P], const f
 
 // EXACT = (head_dim == 8R with R a multiple of 4) and q/k/v 16-byte aligned:
 // whole rows per warp, float4 shared reads and 16-byte cp.async; otherwise
-// every row is bounds-checked and staged with 4-byte copies.
-template <int R, bool EXACT>
-__global__ void __launch_bounds__(kLaThreads, (R <= 16 ? 2 : 1)) la_prefill_kernel(
+// every row is bounds-checked and staged with 4-byte copies.  CPT = columns
+// per thread (a CTA covers 32 x CPT columns): 2 halves the warp-uniform k/q
+// shared reads per fma, for launches with enough CTAs to fill the GPU.
+template <int R, bool EXACT, int CPT>
+__global__ void __launch_bounds__(kLaThreads, (R * CPT <= 16 ? 2 : 1)) la_prefill_kernel(
     float *__restrict__ state, int n_heads, int d_arg, int col_blocks, int seq_len, const float *__restrict__ q,
     const float *__restrict__ k, const float *__restrict__ v, float decay, float *__restrict__ o) {
     constexpr int P = group_tokens<R>();
     constexpr int C = kLaGroupsPerChunk * P;  // tokens per chunk
+    constexpr int W = kLaCols * CPT;          // columns per CTA
     const int d = EXACT ? kLaWarps * R : d_arg;
     extern __shared__ __align__(16) float sm[];
-    // buffer x: [C tokens][k d | q d | v 32]; then the hand-off sums [2][8][P][32]
-    const int tok_floats = 2 * d + kLaCols, buf_floats = C * tok_floats;
+    // buffer x: [C tokens][k d | q d | v W]; then the hand-off sums [2][8][P][W]
+    const int tok_floats = 2 * d + W, buf_floats = C * tok_floats;
     float *hand = sm + kLaBuffers * buf_floats;
     const int h = blockIdx.x / col_blocks, cb = blockIdx.x - h * col_blocks;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int j0 = cb * kLaCols, j = j0 + lane;
-    const bool col = j < d;
+    const int j0 = cb * W;
     const int rpw = EXACT ? R : (d + kLaWarps - 1) / kLaWarps;
     const int r0 = w * rpw;
     const size_t hd = (size_t)h * d, row_stride = (size_t)n_heads * d;  // token stride of q/k/v/o
@@ -279,8 +289,8 @@ __global__ void __launch_bounds__(kLaThreads, (R <= 16 ? 2 : 1)) la_prefill_kern
             float *buf = sm + (m % kLaBuffers) * buf_floats;
             const int t0 = m * C, n = min(C, seq_len - t0);
             if (EXACT) {
-                constexpr int KU = kLaWarps * R / 4;     // 16-byte units of a k (or q) row
-                constexpr int U = 2 * KU + kLaCols / 4;  // per token: k, q, v slice
+                constexpr int KU = kLaWarps * R / 4;  // 16-byte units of a k (or q) row
+                constexpr int U = 2 * KU + W / 4;     // per token: k, q, v slice
                 for (int x = threadIdx.x; x < n * U; x += kLaThreads) {
                     const int c = x / U, r = x - c * U;
                     const size_t base = (size_t)(t0 + c) * row_stride + hd;
@@ -305,11 +315,15 @@ __global__ void __launch_bounds__(kLaThreads, (R <= 16 ? 2 : 1)) la_prefill_kern
     };
 
     float *S = state + hd * d;
-    float s[R];  // this warp's rows of the slice, for the whole sequence
+    float s[CPT][R];  // this warp's rows of the thread's columns, for the whole sequence
 #pragma unroll
-    for (int u = 0; u < R; u++) {
-        const int i = r0 + u;
-        s[u] = (col && u < rpw && i < d) ? S[(size_t)i * d + j] : 0.f;
+    for (int c = 0; c < CPT; c++) {
+        const int j = j0 + c * kLaCols + lane;
+#pragma unroll
+        for (int u = 0; u < R; u++) {
+            const int i = r0 + u;
+            s[c][u] = (j < d && u < rpw && i < d) ? S[(size_t)i * d + j] : 0.f;
+        }
     }
     fetch(0);
     fetch(1);
@@ -325,28 +339,40 @@ __global__ void __launch_bounds__(kLaThreads, (R <= 16 ? 2 : 1)) la_prefill_kern
         if (g >= 0 && g < n_groups) {
             const int t0 = g * P, np = min(P, seq_len - t0);
             const float *gb = sm + ((t0 / C) % kLaBuffers) * buf_floats + (t0 % C) * tok_floats;
-            float acc[P];
-            const float *hin = hand + (((st - 1) & 1) * kLaWarps + (w - 1)) * P * kLaCols + lane;
+            float acc[CPT][P];
+            const float *hin = hand + (((st - 1) & 1) * kLaWarps + (w - 1)) * P * W + lane;
 #pragma unroll
-            for (int p = 0; p < P; p++) acc[p] = w == 0 ? 0.f : hin[p * kLaCols];
-            if (np == P) la_group<R, EXACT, P, true>(s, acc, gb, np, tok_floats, d, r0, rpw, lane, decay);
-            else la_group<R, EXACT, P, false>(s, acc, gb, np, tok_floats, d, r0, rpw, lane, decay);
+            for (int c = 0; c < CPT; c++)
+#pragma unroll
+                for (int p = 0; p < P; p++) acc[c][p] = w == 0 ? 0.f : hin[p * W + c * kLaCols];
+            if (np == P) la_group<R, EXACT, P, CPT, true>(s, acc, gb, np, tok_floats, d, r0, rpw, lane, decay);
+            else la_group<R, EXACT, P, CPT, false>(s, acc, gb, np, tok_floats, d, r0, rpw, lane, decay);
             if (w == kLaWarps - 1) {
 #pragma unroll
-                for (int p = 0; p < P; p++)
-                    if (p < np && col) o[(size_t)(t0 + p) * row_stride + hd + j] = acc[p];
-            } else {
-                float *hout = hand + ((st & 1) * kLaWarps + w) * P * kLaCols + lane;
+                for (int c = 0; c < CPT; c++) {
+                    const int j = j0 + c * kLaCols + lane;
 #pragma unroll
-                for (int p = 0; p < P; p++) hout[p * kLaCols] = acc[p];
+                    for (int p = 0; p < P; p++)
+                        if (p < np && j < d) o[(size_t)(t0 + p) * row_stride + hd + j] = acc[c][p];
+                }
+            } else {
+                float *hout = hand + ((st & 1) * kLaWarps + w) * P * W + lane;
+#pragma unroll
+                for (int c = 0; c < CPT; c++)
+#pragma unroll
+                    for (int p = 0; p < P; p++) hout[p * W + c * kLaCols] = acc[c][p];
             }
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int u = 0; u < R; u++) {
-        const int i = r0 + u;
-        if (col && u < rpw && i < d) S[(size_t)i * d + j] = s[u];
+    for (int c = 0; c < CPT; c++) {
+        const int j = j0 + c * kLaCols + lane;
+#pragma unroll
+        for (int u = 0; u < R; u++) {
+            const int i = r0 + u;
+            if (j < d && u < rpw && i < d) S[(size_t)i * d + j] = s[c][u];
+        }
     }
 }
 
@@ -370,16 +396,44 @@ cudaError_t allow_smem(K kernel, size_t bytes) {
     return e;
 }
 
-template <int R, bool EXACT>
+// SM count of the current device, and resident CTAs per SM of a kernel at a
+// shared-memory size, looked up once (launches are host-latency sensitive)
+int current_sms() {
+    static std::mutex mu;
+    static std::map<int, int> sms;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    auto it = sms.find(dev);
+    if (it != sms.end()) return it->second;
+    int n = 148;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return sms[dev] = n;
+}
+
+template <typename K>
+int resident_ctas(K kernel, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<const void *, size_t>, int> cache;
+    std::lock_guard<std::mutex> g(mu);
+    auto key = std::make_pair((const void *)kernel, smem);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess) per_sm = 1;
+    return cache[key] = std::max(per_sm, 1);
+}
+
+template <int R, bool EXACT, int CPT = 1>
 cudaError_t launch_prefill_r(const QwnLinearAttentionState *st, int seq_len, const float *q, const float *k,
                              const float *v, float decay, float *o, cudaStream_t stream) {
-    const int d = st->head_dim, col_blocks = (d + kLaCols - 1) / kLaCols;
+    const int d = st->head_dim, col_blocks = (d + kLaCols * CPT - 1) / (kLaCols * CPT);
     constexpr int P = group_tokens<R>();
-    const size_t smem = ((size_t)kLaBuffers * kLaGroupsPerChunk * P * (2 * d + kLaCols) +
-                         2 * kLaWarps * P * kLaCols) * sizeof(float);
-    cudaError_t e = allow_smem(la_prefill_kernel<R, EXACT>, smem);
+    const size_t smem = ((size_t)kLaBuffers * kLaGroupsPerChunk * P * (2 * d + kLaCols * CPT) +
+                         2 * kLaWarps * P * kLaCols * CPT) * sizeof(float);
+    cudaError_t e = allow_smem(la_prefill_kernel<R, EXACT, CPT>, smem);
     if (e != cudaSuccess) return e;
-    la_prefill_kernel<R, EXACT><<<(unsigned)(st->n_heads * col_blocks), kLaThreads, smem, stream>>>(
+    la_prefill_kernel<R, EXACT, CPT><<<(unsigned)(st->n_heads * col_blocks), kLaThreads, smem, stream>>>(
         st->state, st->n_heads, d, col_blocks, seq_len, q, k, v, decay, o);
     count_launch();
     return cudaGetLastError();
@@ -394,11 +448,7 @@ cudaError_t launch_decode(const QwnLinearAttentionState *st, const float *q, con
     auto kernel = fast ? la_decode_kernel<true> : la_decode_kernel<false>;
     cudaError_t e = allow_smem(kernel, smem);
     if (e != cudaSuccess) return e;
-    int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kLaDecodeThreads, smem);
-    const int grid = std::min(units, sms * std::max(per_sm, 1));
+    const int grid = std::min(units, current_sms() * resident_ctas(kernel, kLaDecodeThreads, smem));
     kernel<<<(unsigned)grid, kLaDecodeThreads, smem, stream>>>(st->state, d, col_blocks, units, q, k, v, decay, o);
     count_launch();
     return cudaGetLastError();
@@ -410,6 +460,15 @@ cudaError_t launch_step(const QwnLinearAttentionState *st, int seq_len, const fl
     const int d = st->head_dim, r = (d + kLaWarps - 1) / kLaWarps;
     const bool aligned = ((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16 == 0;
     if (aligned && d % (4 * kLaWarps) == 0) {  // whole rows per warp, 16-byte staging
+        // two columns per thread once the one-column grid would be over 4 waves of SMs
+        if ((long)st->n_heads * (d / kLaCols) >= 4L * current_sms() && d % (2 * kLaCols) == 0) {
+            switch (d / kLaWarps) {
+                case 8: return launch_prefill_r<8, true, 2>(st, seq_len, q, k, v, decay, o, stream);
+                case 16: return launch_prefill_r<16, true, 2>(st, seq_len, q, k, v, decay, o, stream);
+                case 32: return launch_prefill_r<32, true, 2>(st, seq_len, q, k, v, decay, o, stream);
+                default: break;
+            }
+        }
         switch (d / kLaWarps) {
             case 4: return launch_prefill_r<4, true>(st, seq_len, q, k, v, decay, o, stream);
             case 8: return launch_prefill_r<8, true>(st, seq_len, q, k, v, decay, o, stream);

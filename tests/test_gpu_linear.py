@@ -62,7 +62,8 @@ def test_decode_steps_bit_exact(cuda, oracle_mod, H, D):
         assert np.array_equal(_state_of(torch, st), ref_state)
 
 
-@pytest.mark.parametrize("H,D,T", [(4, 128, 19), (3, 64, 33), (2, 256, 7), (1, 512, 5), (5, 24, 9), (2, 40, 2), (2, 4, 11), (3, 32, 17), (2, 128, 100)])
+@pytest.mark.parametrize("H,D,T", [(4, 128, 19), (3, 64, 33), (2, 256, 7), (1, 512, 5), (5, 24, 9), (2, 40, 2), (2, 4, 11), (3, 32, 17), (2, 128, 100),
+                                   (160, 128, 70), (300, 64, 40), (80, 256, 20)])
 def test_prefill_bit_exact_and_equals_decodes(cuda, oracle_mod, H, D, T):
     """Prefill from a non-zero state (two decodes first), with a ragged last
     chunk; equals the oracle and the same tokens fed one decode at a time."""
