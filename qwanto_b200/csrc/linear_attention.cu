@@ -491,6 +491,88 @@ int finish(const char *what, cudaError_t e) {
     return QWN_CUDA_STATUS_RUNTIME_ERROR;
 }
 
+// Host-buffer prefill of a long sequence: chunks of kLaHostChunkBytes per
+// input array go through two staging slots so that the copy of chunk c+1 in,
+// the prefill of chunk c and the copy of chunk c-1 out overlap (three
+// non-blocking streams per device, created once).  Prefilling the chunks one
+// after another is the same computation as one prefill, so results do not
+// change.
+constexpr size_t kLaHostChunkBytes = 4u << 20;
+
+struct HostPipe {
+    std::mutex mu;  // one pipelined call per device at a time (the streams and events are shared)
+    bool ok = false;
+    cudaStream_t in = nullptr, comp = nullptr, out = nullptr;
+    cudaEvent_t start = nullptr, in_done[2] = {}, comp_done[2] = {}, out_done[2] = {};
+};
+
+HostPipe *host_pipe(int dev) {
+    static std::mutex mu;
+    static std::map<int, HostPipe> pipes;
+    std::lock_guard<std::mutex> g(mu);
+    HostPipe &p = pipes[dev];
+    if (!p.ok) {
+        bool good = cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking) == cudaSuccess &&
+                    cudaStreamCreateWithFlags(&p.comp, cudaStreamNonBlocking) == cudaSuccess &&
+                    cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking) == cudaSuccess &&
+                    cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming) == cudaSuccess;
+        for (int s = 0; s < 2 && good; s++)
+            good = cudaEventCreateWithFlags(&p.in_done[s], cudaEventDisableTiming) == cudaSuccess &&
+                   cudaEventCreateWithFlags(&p.comp_done[s], cudaEventDisableTiming) == cudaSuccess &&
+                   cudaEventCreateWithFlags(&p.out_done[s], cudaEventDisableTiming) == cudaSuccess;
+        p.ok = good;
+    }
+    return p.ok ? &p : nullptr;
+}
+
+int prefill_host_pipelined(QwnLinearAttentionState *st, const float *q, const float *k, const float *v, float decay,
+                           int seq_len, float *o, int chunk) {
+    const char *what = "qwn_linear_attention_prefill_host";
+    int dev = 0;
+    cudaGetDevice(&dev);
+    HostPipe *p = host_pipe(dev);
+    if (!p) return finish(what, cudaErrorUnknown);
+    std::lock_guard<std::mutex> g(p->mu);
+    const size_t tok_floats = (size_t)st->n_heads * st->head_dim, slot = 4 * (size_t)chunk * tok_floats;
+    if (st->staging_bytes < 2 * slot * sizeof(float)) {
+        if (st->staging) cudaFree(st->staging);
+        st->staging = nullptr;
+        st->staging_bytes = 0;
+        cudaError_t e = cudaMalloc(&st->staging, 2 * slot * sizeof(float));
+        if (e != cudaSuccess) {
+            set_cuda_error("qwn_linear_attention_prefill_host: cudaMalloc", e);
+            return QWN_CUDA_STATUS_OUT_OF_MEMORY;
+        }
+        st->staging_bytes = 2 * slot * sizeof(float);
+    }
+    // the state may have been written by work the caller queued on the legacy default stream
+    cudaError_t e = cudaEventRecord(p->start, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->comp, p->start, 0);
+    const int n_chunks = (seq_len + chunk - 1) / chunk;
+    for (int c = 0; c < n_chunks && e == cudaSuccess; c++) {
+        const int s = c & 1, n = std::min(chunk, seq_len - c * chunk);
+        const size_t off = (size_t)c * chunk * tok_floats, bytes = (size_t)n * tok_floats * sizeof(float);
+        float *dq = (float *)st->staging + s * slot, *dk = dq + (size_t)chunk * tok_floats,
+              *dv = dk + (size_t)chunk * tok_floats, *dout = dv + (size_t)chunk * tok_floats;
+        if (c >= 2) e = cudaStreamWaitEvent(p->in, p->out_done[s], 0);  // slot s is free again
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dq, q + off, bytes, cudaMemcpyHostToDevice, p->in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dk, k + off, bytes, cudaMemcpyHostToDevice, p->in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dv, v + off, bytes, cudaMemcpyHostToDevice, p->in);
+        if (e == cudaSuccess) e = cudaEventRecord(p->in_done[s], p->in);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->comp, p->in_done[s], 0);
+        if (e == cudaSuccess) e = launch_step(st, n, dq, dk, dv, decay, dout, p->comp);
+        if (e == cudaSuccess) e = cudaEventRecord(p->comp_done[s], p->comp);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->out, p->comp_done[s], 0);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(o + off, dout, bytes, cudaMemcpyDeviceToHost, p->out);
+        if (e == cudaSuccess) e = cudaEventRecord(p->out_done[s], p->out);
+    }
+    // drain all three streams whatever happened, so no copy outlives the call
+    cudaError_t e1 = cudaStreamSynchronize(p->in), e2 = cudaStreamSynchronize(p->comp),
+                e3 = cudaStreamSynchronize(p->out);
+    if (e == cudaSuccess) e = e1 != cudaSuccess ? e1 : (e2 != cudaSuccess ? e2 : e3);
+    return finish(what, e);
+}
+
 }  // namespace
 }  // namespace qkv
 
@@ -573,7 +655,10 @@ QWN_CUDA_ABI_API int qwn_linear_attention_prefill_host(QwnLinearAttentionState *
     }
     if (seq_len == 0) return QWN_CUDA_STATUS_OK;
     DeviceScope scope(st->device_id);
-    const size_t row = (size_t)seq_len * st->n_heads * st->head_dim * sizeof(float);
+    const size_t tok_bytes = (size_t)st->n_heads * st->head_dim * sizeof(float);
+    const int chunk = (int)std::max<size_t>(1, kLaHostChunkBytes / tok_bytes);
+    if (seq_len > chunk) return prefill_host_pipelined(st, q, k, v, decay, seq_len, o, chunk);
+    const size_t row = (size_t)seq_len * tok_bytes;
     if (st->staging_bytes < 4 * row) {
         if (st->staging) cudaFree(st->staging);
         st->staging = nullptr;

@@ -160,3 +160,25 @@ def test_prefill_unaligned_inputs_take_the_checked_path(cuda, oracle_mod):
         torch.cuda.synchronize()
         assert np.array_equal(od.cpu().numpy(), ref_out)
         assert np.array_equal(_state_of(torch, st), ref_state)
+
+
+def test_host_call_pipelines_long_sequences(cuda, oracle_mod):
+    """A host-buffer prefill longer than one staging chunk (4 MiB per input
+    array: 2048 tokens of 4 heads x 128) runs as overlapped chunks, the last
+    one a single token; the result equals the oracle bit for bit, and a
+    second call continues from the state the first one left."""
+    from qwanto_b200.linear_attention import LinearAttentionState
+    torch = cuda
+    H, D, T = 4, 128, 4097
+    rng = np.random.default_rng(23)
+    q, k, v = _inputs(rng, T + 3, H, D, 0.3)
+    ref_state = np.zeros((H, D, D), np.float32)
+    ref_out = _oracle_steps(oracle_mod, ref_state, q, k, v, 0.995)
+    with LinearAttentionState(H, D) as st:
+        out = np.full((T + 3, H, D), np.nan, np.float32)
+        st.prefill_host(np.ascontiguousarray(q[:T]), np.ascontiguousarray(k[:T]), np.ascontiguousarray(v[:T]),
+                        0.995, T, out[:T])
+        st.prefill_host(np.ascontiguousarray(q[T:]), np.ascontiguousarray(k[T:]), np.ascontiguousarray(v[T:]),
+                        0.995, 3, out[T:])
+        assert np.array_equal(out, ref_out)
+        assert np.array_equal(_state_of(torch, st), ref_state)
