@@ -10,7 +10,7 @@
  * structure layouts, constants, status codes and capability bits must be
  * byte-identical to the reference contract c/cuda/qwn_cuda_abi.h:27-274, so
  * they are restated here unchanged in meaning; the implementation behind
- * them (qwanto_b200/csrc/qwn_abi_v1.cu) is this project's own.
+ * them (qwanto_b200/csrc/abi_v1.cu) is this project's own.
  *
  * No CUDA runtime types appear here.  Every structure starts with
  * QwnCudaAbiHeader; callees accept struct_size >= the size they know.

@@ -108,7 +108,9 @@ QWN_CUDA_ABI_API int qwn_kv_pool_destroy(QwnKvPoolHandle *pool);
 QWN_CUDA_ABI_API int qwn_kv_pool_get_info(const QwnKvPoolHandle *pool, QwnKvPoolInfo *info);
 /* empty every sequence and rebuild the free stack; synchronous */
 QWN_CUDA_ABI_API int qwn_kv_pool_reset(QwnKvPoolHandle *pool);
-/* synchronise the pool's work, return and clear the latched status bits */
+/* return and clear the latched status bits (and, after a wait timeout, the
+ * split-KV merge counters an abandoned merge left behind).  The pool's work
+ * may run on any of the caller's streams, so this synchronises the device. */
 QWN_CUDA_ABI_API int qwn_kv_pool_check(QwnKvPoolHandle *pool, uint32_t *status_bits);
 
 /* Grow sequences: sequence seq_ids[i] gains counts[i] tokens (1 when
@@ -306,10 +308,13 @@ QWN_CUDA_ABI_API int qwn_kv_decode_step_host(QwnKvPoolHandle *pool,
  * It runs the qwn_kv_decode attention (no append) with its scratch in a
  * fixed device array inside the library (about 4.3 MB per device, held until
  * the process exits).  Limits: num_seqs x kv_heads <= 256; query heads per kv
- * head <= 8; head_dim 128; codecs Q8_B64_F32, Q8_HEAD_F16, Q4_G32.  All calls
- * on a device share the array: calls whose work may overlap on the GPU race
- * and must be ordered by the caller.  The first call on a device sets the
- * array up (looks up its address); make it before any stream capture. */
+ * head <= 8; head_dim 128; every codec of QwnKvCodec (Q8_B64_F32, Q8_HEAD_F16,
+ * TQ35_G64, Q4_G32, F16).  pages_dev, query_dev and output_dev must be
+ * 16-byte aligned and the int32 arrays 4-byte aligned (INVALID_ARGUMENT
+ * otherwise, before anything is launched).  All calls on a device share the
+ * array: calls whose work may overlap on the GPU race and must be ordered by
+ * the caller.  The first call on a device sets the array up (looks up its
+ * address); make it before any stream capture. */
 typedef struct {
     QwnCudaAbiHeader header;
     int32_t device_id;

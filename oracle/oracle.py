@@ -42,8 +42,10 @@ i16p = C.POINTER(C.c_int16)
 
 def build(reference: bool = True) -> None:
     """Compile the oracle (and the reference objects when the sources exist)."""
+    from oracle.refpath import reference_c
     targets = ["oracle"] + (["ref"] if reference else [])
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+    ref = reference_c() if reference else None
+    subprocess.run(["make", "-s", "-C", HERE] + targets + ([f"REF={ref}"] if ref else []), check=True)
 
 
 def _ptr(a: np.ndarray, t):

@@ -2315,6 +2315,16 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
         set_error("qwn_kv_attention_static: invalid request");
         return QWN_CUDA_STATUS_INVALID_ARGUMENT;
     }
+    // the tiles arrive by 1-D bulk copies (16-byte source and size), the query
+    // rows by 16-byte loads and the output by 16-byte stores; the int32
+    // arrays are read 4 bytes at a time
+    auto misaligned = [](const void *ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) != 0; };
+    if (misaligned(r->pages_dev, 16) || misaligned(r->query_dev, 16) || misaligned(r->output_dev, 16) ||
+        misaligned(r->page_table_dev, 4) || misaligned(r->seq_lens_dev, 4) || misaligned(r->seq_ids_dev, 4) ||
+        misaligned(r->status_dev, 4) || tb % 16) {
+        set_error("qwn_kv_attention_static: pages, query and output must be 16-byte aligned, the int32 arrays 4-byte");
+        return QWN_CUDA_STATUS_INVALID_ARGUMENT;
+    }
     if ((uint64_t)r->num_seqs * r->kv_heads > (uint64_t)kStaticSegments) {
         set_error("qwn_kv_attention_static: num_seqs x kv_heads exceeds the static scratch limit of 256 segments");
         return QWN_CUDA_STATUS_UNSUPPORTED;
@@ -2387,7 +2397,10 @@ extern "C" QWN_CUDA_ABI_API int qwn_kv_attention_static(const QwnKvStaticAttenti
         case QWN_KV_CODEC_Q8_B64_F32: e = launch_variant<QWN_KV_CODEC_Q8_B64_F32>(ctas, A, s); break;
         case QWN_KV_CODEC_Q4_G32: e = launch_variant<QWN_KV_CODEC_Q4_G32>(ctas, A, s); break;
         case QWN_KV_CODEC_F16: e = launch_variant<QWN_KV_CODEC_F16>(ctas, A, s); break;
-        default: e = launch_variant<QWN_KV_CODEC_TQ35_G64>(ctas, A, s); break;
+        case QWN_KV_CODEC_TQ35_G64: e = launch_variant<QWN_KV_CODEC_TQ35_G64>(ctas, A, s); break;
+        default:
+            set_error("qwn_kv_attention_static: unsupported codec");
+            return QWN_CUDA_STATUS_UNSUPPORTED;
     }
     count_launch();
     if (e != cudaSuccess) {

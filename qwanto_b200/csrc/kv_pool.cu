@@ -909,10 +909,18 @@ QWN_CUDA_ABI_API int qwn_kv_decode_step_host(QwnKvPoolHandle *h, const QwnKvHost
     cudaEventDestroy(t0);
     cudaEventDestroy(t1);
     if (e != cudaSuccess) { set_cuda_error("qwn_kv_decode_step_host", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    // read and clear the status word, as qwn_kv_pool_check does, so that one
+    // latched error fails this step and not every later one; an abandoned
+    // split-KV merge (wait timeout) also leaves counters that must restart at 0
     uint32_t st = 0;
-    cudaMemcpy(&st, p->status, sizeof(st), cudaMemcpyDeviceToHost);
+    e = cudaMemcpy(&st, p->status, sizeof(st), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && st) e = cudaMemset(p->status, 0, sizeof(uint32_t));
+    if (e == cudaSuccess && (st & QWN_KV_STATUS_WAIT_TIMEOUT))
+        e = cudaMemset(p->counters, 0, sizeof(uint32_t) * counter_count(p));
+    if (e != cudaSuccess) { set_cuda_error("qwn_kv_decode_step_host: status", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
     if (tel && header_ok(tel->header, sizeof(*tel))) {
-        tel->kv_cache_kernel_count += 1 + 2ull * r->num_layers;
+        // one page-allocation launch, then one fused append + attention launch per layer
+        tel->kv_cache_kernel_count += 1ull + r->num_layers;
         tel->kv_cache_upload_bytes += (uint64_t)(lq + 2 * lkv) * 4;
         tel->kv_cache_kernel_ms += ms;
         std::snprintf(tel->kv_cache_kernel_type, sizeof(tel->kv_cache_kernel_type), "paged-b200-split-kv");

@@ -12,7 +12,10 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 INCLUDE = os.path.join(ROOT, "include")
-REF_ABI = "/root/reference/c/cuda/qwn_cuda_abi.h"
+from oracle.refpath import reference_c
+
+_REF_C = reference_c()
+REF_ABI = os.path.join(_REF_C, "cuda", "qwn_cuda_abi.h") if _REF_C else ""
 
 STRUCTS = {
     "QwnCudaAbiHeader": ["struct_size", "abi_version", "reserved"],
@@ -176,3 +179,34 @@ def test_enumerate_without_device_reports_unavailable():
     import qwanto_b200
     rc, devs = qwanto_b200.CudaContext.devices()
     assert rc == -3 and devs == []
+
+
+def test_static_attention_rejects_misaligned_pointers_without_gpu():
+    """qwn_kv_attention_static takes raw device pointers from FFI callers: a
+    pages pointer off the 16-byte grid (the tiles move by 1-D bulk copies) or
+    a query/output pointer off it (16-byte loads and stores) is an argument
+    error found on the host, before anything is launched.  The addresses
+    below are never dereferenced."""
+    import qwanto_b200
+    from qwanto_b200 import _lib
+    L = qwanto_b200.lib()
+    base = 1 << 40
+
+    def req(**kw):
+        r = _lib.init(_lib.StaticAttentionRequest())
+        r.device_id, r.codec, r.layers, r.kv_heads, r.head_dim = 0, 2, 1, 8, 128
+        r.page_tokens, r.total_pages, r.max_seqs, r.max_pages_per_seq = 16, 64, 4, 16
+        r.layer, r.num_seqs, r.query_heads = 0, 2, 32
+        r.pages_dev, r.page_table_dev, r.seq_lens_dev = base, base + 4096, base + 8192
+        r.query_dev, r.output_dev = base + 12288, base + 16384
+        for k, v in kw.items():
+            setattr(r, k, v)
+        return r
+
+    for kw in [dict(pages_dev=base + 4), dict(query_dev=base + 12288 + 8), dict(output_dev=base + 16384 + 4),
+               dict(page_table_dev=base + 4096 + 2), dict(seq_lens_dev=base + 8192 + 1)]:
+        r = req(**kw)
+        assert L.qwn_kv_attention_static(C.byref(r)) == -1, kw
+        assert "aligned" in _lib.last_error()
+    r = req(codec=6)
+    assert L.qwn_kv_attention_static(C.byref(r)) == -1

@@ -3,6 +3,7 @@ the (m, l, o) exchange, run as two gloo ranks.  The partial states come from
 the CPU oracle, so this checks the partition + exchange + merge, not a kernel."""
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -91,39 +92,50 @@ def test_kv_range_split_merge_two_gloo_ranks():
     assert max(errs.values()) < 1e-5, errs
 
 
-def _dropout_main(rank, world, port, q):
-    """Rank 1 leaves between steps; rank 0 learns of it from the store before
-    its next collective instead of hanging in it."""
+def _silent_exit_main(rank, world, port, q):
+    """Rank 1 runs one step and then exits between steps without a word (no
+    store key, no message).  Rank 0 finds it through the heartbeat before its
+    next collective, then confirms that a short process-group timeout ends a
+    collective with the lost rank in an error instead of a hang."""
     import datetime
     import torch
     import torch.distributed as dist
+    from qwanto_b200.health import Heartbeat, RankLostError
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
     store = dist.distributed_c10d._get_default_store()
+    hb = Heartbeat(store, rank, world, interval=0.02).start()
     x = torch.ones(4)
+    hb.check_peers(timeout=5.0)
     dist.all_reduce(x)  # step 1 with both ranks
     if rank == 1:
-        store.set("rank1_leaving", "1")
-        q.put((rank, "left"))
-        q.close()
-        q.join_thread()
-        os._exit(0)
-    # rank 0: check the store (heartbeat) before the next step's collective
-    store.wait(["rank1_leaving"], datetime.timedelta(seconds=20))
-    q.put((rank, "saw-departure" if store.get("rank1_leaving") == b"1" else "missed"))
+        os._exit(0)  # silent: the heartbeat thread dies with the process
+    time.sleep(0.3)
+    try:
+        hb.check_peers(timeout=1.0)
+        verdict = "missed"
+    except RankLostError as e:
+        verdict = f"lost {e.ranks}"
+    t0 = time.monotonic()
+    try:
+        dist.all_reduce(x)  # what a rank without the check would do
+        coll = "completed"
+    except Exception:
+        coll = "error"
+    q.put((rank, verdict, coll, time.monotonic() - t0))
     q.close()
     q.join_thread()
     os._exit(0)
 
 
 @pytest.mark.timeout(120)
-def test_rank_departure_detected_on_host():
+def test_silent_rank_exit_detected_by_heartbeat():
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_dropout_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_silent_exit_main, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -131,5 +143,44 @@ def test_rank_departure_detected_on_host():
     for p in procs:
         if p.is_alive():
             p.kill()
-    res = dict(q.get(timeout=5) for _ in range(2))
-    assert res == {0: "saw-departure", 1: "left"}
+    rank, verdict, coll, waited = q.get(timeout=5)
+    assert (rank, verdict) == (0, "lost [1]")
+    assert coll == "error" and waited < 30
+
+
+def test_heartbeat_sees_live_peers_and_stale_ones():
+    """The check itself on one process: a peer key that keeps moving passes,
+    one that stands still raises after the timeout, a missing one too."""
+    import threading
+    from torch.distributed import HashStore
+    from qwanto_b200.health import Heartbeat, RankLostError
+    store = HashStore()
+    a = Heartbeat(store, 0, 3, interval=0.01).start()
+    b = Heartbeat(store, 1, 3, interval=0.01).start()
+    try:
+        with pytest.raises(RankLostError) as ei:
+            a.check_peers(timeout=0.2)  # rank 2 never started
+        assert ei.value.ranks == [2]
+        store.set("qwn_hb/2", "5")  # present but frozen
+        with pytest.raises(RankLostError) as ei:
+            a.check_peers(timeout=0.2)
+        assert ei.value.ranks == [2]
+        stop = threading.Event()
+
+        def beat():
+            n = 6
+            while not stop.is_set():
+                store.set("qwn_hb/2", str(n))
+                n += 1
+                time.sleep(0.01)
+        t = threading.Thread(target=beat)
+        t.start()
+        try:
+            a.check_peers(timeout=2.0)
+            b.check_peers(timeout=2.0)
+        finally:
+            stop.set()
+            t.join()
+    finally:
+        a.stop()
+        b.stop()

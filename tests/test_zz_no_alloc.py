@@ -32,11 +32,13 @@ def _static_request(pool, layer, num_seqs, query_heads, query, output, seq_ids=N
     return r
 
 
-@pytest.mark.parametrize("codec", [2, 1, 4])
-def test_static_scratch_attention_matches_decode_twice(cuda, codec):
+@pytest.mark.parametrize("codec,H", [(2, 32), (1, 32), (4, 32), (3, 32), (5, 32), (2, 64), (4, 64), (3, 64)])
+def test_static_scratch_attention_matches_decode_twice(cuda, codec, H):
+    """H = 32 runs 4 query heads per kv head (one head group), H = 64 runs 8
+    (two head groups, the kernel variant with its own grid size)."""
     import qwanto_b200 as qb
     torch = cuda
-    B, L, H, HK = 6, 2, 32, 8
+    B, L, HK = 6, 2, 8
     lens = [1, 17, 300, 1500, 4000, 64]
     pool = qb.KvPool(codec, L, HK, 16, 600, B, 300, max_query_heads=H, permutation_seed=12)
     try:
