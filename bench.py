@@ -171,6 +171,17 @@ def dist_setup():
     return world, rank, local
 
 
+def outlier_masks(wl: dict):
+    """[layers][kv_heads*128] K outlier channels (x8) of the workload, or None."""
+    if not wl["outliers"]:
+        return None
+    mask = np.zeros((wl["layers"], wl["HK"] * HD), np.uint8)
+    rng = np.random.default_rng(wl["seed"] + 17)
+    for layer in range(wl["layers"]):
+        mask[layer, rng.choice(wl["HK"] * HD, wl["outliers"], replace=False)] = 1
+    return mask
+
+
 def global_lengths(wl: dict, n_gpus: int) -> np.ndarray:
     rng = np.random.default_rng(wl["seed"])
     return rng.integers(wl["lo"], wl["hi"] + 1, size=wl["batch"] * n_gpus).astype(np.int32)
@@ -273,12 +284,7 @@ def run_ours(args, wl, world, rank, local):
     total_pages = int(sum((int(c) + grow + P - 1) // P for c in lens)) + 8
     pool = qb.KvPool(wl["codec"], L, HK, P, total_pages, B, max_pages, max_query_heads=H,
                      permutation_seed=1000 + rank, device=local)
-    mask = None
-    if wl["outliers"]:
-        mask = np.zeros((L, HK * HD), np.uint8)
-        rng = np.random.default_rng(wl["seed"] + 17)
-        for layer in range(L):
-            mask[layer, rng.choice(HK * HD, wl["outliers"], replace=False)] = 1
+    mask = outlier_masks(wl)
     seed = 1000 * wl["seed"] + rank
     pool.prefill_synthetic(list(range(B)), lens.tolist(), seed, mask, stream)
     torch.cuda.synchronize(dev)

@@ -154,6 +154,10 @@ def lib():
         _decl(L, "qor_tile_load", None, C.c_int, u8p, C.c_int, C.c_int, i16p, f32p)
         _decl(L, "qor_pool_init", C.c_int, C.POINTER(QorPool), C.c_int, C.c_int, C.c_int,
               C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64)
+        _decl(L, "qor_pool_init_ex", C.c_int, C.POINTER(QorPool), C.c_int, C.c_int, C.c_int,
+              C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_int)
+        _decl(L, "qor_pool_fill_synthetic", C.c_int, C.POINTER(QorPool), C.c_int, C.c_int, C.c_int,
+              C.c_int, C.c_int, C.c_uint64, u8p)
         _decl(L, "qor_pool_free", None, C.POINTER(QorPool))
         _decl(L, "qor_pool_append", C.c_int, C.POINTER(QorPool), C.c_int, i32p, i32p)
         _decl(L, "qor_pool_write_token", C.c_int, C.POINTER(QorPool), C.c_int, C.c_int,
@@ -315,10 +319,11 @@ class Pool:
     """Host simulation of the paged pool (page tables, free stack, tiles)."""
 
     def __init__(self, codec, layers, kv_heads, page_tokens, total_pages, max_seqs,
-                 max_pages_per_seq, perm_seed=0):
+                 max_pages_per_seq, perm_seed=0, with_pages=True):
         self.p = QorPool()
-        rc = lib().qor_pool_init(C.byref(self.p), codec, layers, kv_heads, page_tokens,
-                                 total_pages, max_seqs, max_pages_per_seq, perm_seed)
+        rc = lib().qor_pool_init_ex(C.byref(self.p), codec, layers, kv_heads, page_tokens,
+                                    total_pages, max_seqs, max_pages_per_seq, perm_seed,
+                                    1 if with_pages else 0)
         if rc != 0:
             raise MemoryError("oracle pool init failed")
         self.codec, self.layers, self.kv_heads = codec, layers, kv_heads
@@ -341,6 +346,13 @@ class Pool:
         return int(lib().qor_pool_write_token(C.byref(self.p), seq, layer, pos,
                                               _ptr(k, f32p), _ptr(v, f32p)))
 
+    def fill_synthetic(self, seq, layer, gen_layer, first, last, seed, k_outlier_mask=None) -> int:
+        """Store the synthetic K/V rows of (seed, seq, gen_layer) for
+        positions [first, last) into `layer`, in C."""
+        m = None if k_outlier_mask is None else np.ascontiguousarray(k_outlier_mask, dtype=np.uint8)
+        return int(lib().qor_pool_fill_synthetic(C.byref(self.p), seq, layer, gen_layer, first, last, seed,
+                                                 None if m is None else _ptr(m, u8p)))
+
     def attention(self, seq, layer, length, q, heads, scale, want_probs=False):
         q = np.ascontiguousarray(q, dtype=np.float32)
         out = np.zeros((heads, 128), dtype=np.float32)
@@ -359,6 +371,8 @@ class Pool:
 
     # views
     def pages(self) -> np.ndarray:
+        if not self.p.pages:
+            raise ValueError("metadata-only oracle pool has no pages")
         n = self.p.total_pages * self.p.page_bytes
         return np.ctypeslib.as_array(self.p.pages, shape=(n,)).reshape(self.p.total_pages, -1)
 

@@ -589,19 +589,26 @@ float qor_tile_dequant(int codec, const uint8_t *tile, int t, int is_value, int 
 
 int qor_pool_init(QorPool *p, int codec, int layers, int kv_heads, int page_tokens,
                   int total_pages, int max_seqs, int max_pages_per_seq, uint64_t perm_seed) {
+    return qor_pool_init_ex(p, codec, layers, kv_heads, page_tokens, total_pages, max_seqs,
+                            max_pages_per_seq, perm_seed, 1);
+}
+
+int qor_pool_init_ex(QorPool *p, int codec, int layers, int kv_heads, int page_tokens,
+                     int total_pages, int max_seqs, int max_pages_per_seq, uint64_t perm_seed,
+                     int with_pages) {
     memset(p, 0, sizeof(*p));
     if (qor_tile_bytes(codec) == 0 || page_tokens <= 0 || page_tokens % 16) return -1;
     p->codec = codec; p->layers = layers; p->kv_heads = kv_heads; p->page_tokens = page_tokens;
     p->total_pages = total_pages; p->max_seqs = max_seqs; p->max_pages_per_seq = max_pages_per_seq;
     p->tile_bytes = qor_tile_bytes(codec);
     p->page_bytes = p->tile_bytes * (size_t)(page_tokens / 16) * (size_t)layers * (size_t)kv_heads;
-    p->pages = (uint8_t *)calloc((size_t)total_pages, p->page_bytes);
+    p->pages = with_pages ? (uint8_t *)calloc((size_t)total_pages, p->page_bytes) : NULL;
     p->free_stack = (int32_t *)malloc(sizeof(int32_t) * (size_t)total_pages);
     p->page_table = (int32_t *)malloc(sizeof(int32_t) * (size_t)max_seqs * (size_t)max_pages_per_seq);
     p->lens = (int32_t *)calloc((size_t)max_seqs, sizeof(int32_t));
     p->npages = (int32_t *)calloc((size_t)max_seqs, sizeof(int32_t));
     p->page_score = (float *)calloc((size_t)max_seqs * (size_t)max_pages_per_seq, sizeof(float));
-    if (!p->pages || !p->free_stack || !p->page_table || !p->lens || !p->npages || !p->page_score) {
+    if ((with_pages && !p->pages) || !p->free_stack || !p->page_table || !p->lens || !p->npages || !p->page_score) {
         qor_pool_free(p);
         return -1;
     }
@@ -649,7 +656,7 @@ uint8_t *qor_pool_tile(QorPool *p, int seq, int layer, int kv_head, int pos) {
     int P = p->page_tokens, tiles = P / 16;
     int lp = pos / P, tile = (pos % P) / 16;
     int32_t pg = p->page_table[(size_t)seq * p->max_pages_per_seq + lp];
-    if (pg < 0) return NULL;
+    if (pg < 0 || !p->pages) return NULL;
     size_t off = (size_t)pg * p->page_bytes +
                  (((size_t)layer * p->kv_heads + kv_head) * tiles + tile) * p->tile_bytes;
     return p->pages + off;
@@ -664,6 +671,43 @@ int qor_pool_write_token(QorPool *p, int seq, int layer, int pos, const float *k
         qor_tile_store(p->codec, tile, pos % 16, k + h * 128, v + h * 128);
     }
     return 0;
+}
+
+/* The synthetic K/V rows of (seed, seq, gen_layer) for positions
+ * [first, last), stored into `layer`: K = normal(kind 2) x 8 on the channels
+ * k_outlier_mask marks, V = normal(kind 3) -- the values qwn_kv_prefill_synthetic
+ * and qwn_kv_generate_rows produce on the device. */
+static float normal_keyed(uint64_t key, uint64_t index) {
+    int64_t sum = 0;
+    for (int j = 0; j < 3; j++) {
+        uint64_t h = qor_mix64(key + 3u * index + (uint64_t)j);
+        sum += (int64_t)(h & 0xFFFF) + (int64_t)((h >> 16) & 0xFFFF) +
+               (int64_t)((h >> 32) & 0xFFFF) + (int64_t)(h >> 48);
+    }
+    return (float)(sum - 393210) * (1.0f / 65536.0f);
+}
+
+int qor_pool_fill_synthetic(QorPool *p, int seq, int layer, int gen_layer, int first, int last,
+                            uint64_t seed, const uint8_t *k_outlier_mask) {
+    if (!p->pages || first < 0 || last > p->lens[seq] || layer < 0 || layer >= p->layers) return -1;
+    const int W = p->kv_heads * 128;
+    float *k = (float *)malloc(sizeof(float) * (size_t)W);
+    float *v = (float *)malloc(sizeof(float) * (size_t)W);
+    if (!k || !v) { free(k); free(v); return -1; }
+    const uint64_t kk = qor_mix64(seed ^ qor_mix64(qor_stream(2, (uint32_t)seq, (uint32_t)gen_layer)));
+    const uint64_t kv = qor_mix64(seed ^ qor_mix64(qor_stream(3, (uint32_t)seq, (uint32_t)gen_layer)));
+    int rc = 0;
+    for (int t = first; t < last && rc == 0; t++) {
+        for (int c = 0; c < W; c++) {
+            float x = normal_keyed(kk, (uint64_t)t * (uint64_t)W + (uint64_t)c);
+            k[c] = (k_outlier_mask && k_outlier_mask[c]) ? x * 8.0f : x;
+            v[c] = normal_keyed(kv, (uint64_t)t * (uint64_t)W + (uint64_t)c);
+        }
+        rc = qor_pool_write_token(p, seq, layer, t, k, v);
+    }
+    free(k);
+    free(v);
+    return rc;
 }
 
 static const uint8_t *ctile(const QorPool *p, int seq, int layer, int kv, int pos) {
@@ -730,6 +774,7 @@ static void token_value(const QorPool *p, const uint8_t *tile, int t, float *v) 
 void qor_pool_attention(const QorPool *p, int seq, int layer, int len, const float *q,
                         int H, float scale, float *out, float *token_probs) {
     int HK = p->kv_heads;
+    if (!p->pages) { memset(out, 0, sizeof(float) * (size_t)H * 128); return; }
     float *scores = (float *)malloc(sizeof(float) * (size_t)(len > 0 ? len : 1));
     float vrow[128];
     for (int h = 0; h < H; h++) {

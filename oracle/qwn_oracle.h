@@ -110,6 +110,12 @@ typedef struct {
 int qor_pool_init(QorPool *p, int codec, int layers, int kv_heads, int page_tokens,
                   int total_pages, int max_seqs, int max_pages_per_seq,
                   uint64_t perm_seed);
+/* with_pages 0: block tables, free stack and scores only (pages NULL), for
+ * pools whose page bytes would not fit in host memory; writes and
+ * attention are then unavailable */
+int qor_pool_init_ex(QorPool *p, int codec, int layers, int kv_heads, int page_tokens,
+                     int total_pages, int max_seqs, int max_pages_per_seq,
+                     uint64_t perm_seed, int with_pages);
 void qor_pool_free(QorPool *p);
 /* add counts[i] tokens to sequence seq_ids[i], in array order, allocating
  * pages from the LIFO free stack like qwn_block_table_append_token
@@ -120,6 +126,10 @@ int qor_pool_append(QorPool *p, int n, const int32_t *seq_ids, const int32_t *co
 int qor_pool_write_token(QorPool *p, int seq, int layer, int pos, const float *k,
                          const float *v);
 uint8_t *qor_pool_tile(QorPool *p, int seq, int layer, int kv_head, int pos);
+/* store the synthetic rows of generator layer gen_layer for positions
+ * [first, last) of seq into `layer` (K x 8 where k_outlier_mask[c] != 0) */
+int qor_pool_fill_synthetic(QorPool *p, int seq, int layer, int gen_layer, int first, int last,
+                            uint64_t seed, const uint8_t *k_outlier_mask);
 /* GQA decode attention over tokens [0,len) of one sequence and layer, in
  * the reference's arithmetic order (c/qwanto_turboquant.c:678-705 for Q8,
  * :707-768 with the scalar dot/accum of :218-284 for TurboQuant).  Query

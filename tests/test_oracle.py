@@ -423,3 +423,31 @@ def test_page_eviction_oracle_properties(oracle_mod):
     kept = set(tbl[0, : p.npages()[0]])
     expect = [pg for pg in before[0, :np0] if pg not in kept]
     assert list(freed) == expect
+
+
+def test_fill_synthetic_equals_token_writes(oracle_mod):
+    """The oracle's bulk synthetic fill (used by the full-size GPU tests)
+    stores exactly the rows gen_row gives, K x 8 on outlier channels, into
+    the chosen layer; a metadata-only pool keeps tables without pages."""
+    O = oracle_mod
+    a = O.Pool(4, 2, 8, 16, 40, 3, 20, perm_seed=3)
+    b = O.Pool(4, 1, 8, 16, 40, 3, 20, perm_seed=3)
+    mask = O.outlier_mask(3, 1, 1024, 10)
+    for p in (a, b):
+        assert p.append([0, 2], [50, 33]) == 0
+    for s, n in ((0, 50), (2, 33)):
+        for t in range(n):
+            k = O.gen_row(9, 2, s, 1, t, 1024)
+            k = np.where(mask != 0, k * np.float32(8), k).astype(np.float32)
+            assert a.write(s, 1, t, k, O.gen_row(9, 3, s, 1, t, 1024)) == 0
+        assert b.fill_synthetic(s, 0, 1, 0, n, 9, mask) == 0
+        for t in range(0, n, 16):
+            for h in range(8):
+                assert np.array_equal(a.tile(s, 1, h, t), b.tile(s, 0, h, t))
+    m = O.Pool(2, 1, 8, 16, 1 << 16, 4, 64, perm_seed=5, with_pages=False)
+    full = O.Pool(2, 1, 8, 16, 1 << 16, 4, 64, perm_seed=5)
+    for p in (m, full):
+        assert p.append([1, 3], [100, 7]) == 0
+    assert np.array_equal(m.page_table(), full.page_table())
+    assert np.array_equal(m.free_stack(), full.free_stack())
+    assert m.fill_synthetic(1, 0, 0, 0, 100, 9) == -1
