@@ -18,9 +18,10 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "qwn_cuda.so")
 
-SOURCES = ["kv_pool.cu", "kv_attention.cu", "kv_evict.cu", "abi_v1.cu", "linear_attention.cu"]
-HEADERS = [os.path.join(CSRC, "kv_internal.cuh"), os.path.join(CSRC, "kv_store.cuh"), os.path.join(INCLUDE, "qwn_cuda_abi.h"),
-           os.path.join(INCLUDE, "qwn_kv_b200.h")]
+SOURCES = ["kv_pool.cu", "kv_attention.cu", "kv_evict.cu", "abi_v1.cu", "linear_attention.cu", "ref_api.cu"]
+HEADERS = [os.path.join(CSRC, "kv_internal.cuh"), os.path.join(CSRC, "kv_store.cuh")] + [
+    os.path.join(INCLUDE, h) for h in ("qwn_cuda_abi.h", "qwn_kv_b200.h", "qwn_paged_kv.h", "qwanto_turboquant.h",
+                                       "qwanto_attention.h", "qwanto_pagedeviction.h")]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -56,7 +57,9 @@ def build(verbose: bool = False, ptxas_v: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose, ptxas_v), SOURCES))
     if _stale(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs
+        # -Bsymbolic: calls inside the library bind to its own definitions even
+        # when the host program defines the same reference-named symbols
+        cmd = [NVCC] + ARCH + ["-shared", "-Xlinker", "-Bsymbolic", "-o", LIB] + objs
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -555,15 +555,15 @@ int prefill_host_pipelined(QwnLinearAttentionState *st, const float *q, const fl
         float *dq = (float *)st->staging + s * slot, *dk = dq + (size_t)chunk * tok_floats,
               *dv = dk + (size_t)chunk * tok_floats, *dout = dv + (size_t)chunk * tok_floats;
         if (c >= 2) e = cudaStreamWaitEvent(p->in, p->out_done[s], 0);  // slot s is free again
-        if (e == cudaSuccess) e = cudaMemcpyAsync(dq, q + off, bytes, cudaMemcpyHostToDevice, p->in);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(dk, k + off, bytes, cudaMemcpyHostToDevice, p->in);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(dv, v + off, bytes, cudaMemcpyHostToDevice, p->in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dq, q + off, bytes, cudaMemcpyDefault, p->in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dk, k + off, bytes, cudaMemcpyDefault, p->in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dv, v + off, bytes, cudaMemcpyDefault, p->in);
         if (e == cudaSuccess) e = cudaEventRecord(p->in_done[s], p->in);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(p->comp, p->in_done[s], 0);
         if (e == cudaSuccess) e = launch_step(st, n, dq, dk, dv, decay, dout, p->comp);
         if (e == cudaSuccess) e = cudaEventRecord(p->comp_done[s], p->comp);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(p->out, p->comp_done[s], 0);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(o + off, dout, bytes, cudaMemcpyDeviceToHost, p->out);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(o + off, dout, bytes, cudaMemcpyDefault, p->out);
         if (e == cudaSuccess) e = cudaEventRecord(p->out_done[s], p->out);
     }
     // drain all three streams whatever happened, so no copy outlives the call
@@ -673,11 +673,11 @@ QWN_CUDA_ABI_API int qwn_linear_attention_prefill_host(QwnLinearAttentionState *
     char *base = (char *)st->staging;
     float *dq = (float *)base, *dk = (float *)(base + row), *dv = (float *)(base + 2 * row),
           *dout = (float *)(base + 3 * row);
-    cudaError_t e = cudaMemcpyAsync(dq, q, row, cudaMemcpyHostToDevice, 0);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(dk, k, row, cudaMemcpyHostToDevice, 0);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(dv, v, row, cudaMemcpyHostToDevice, 0);
+    cudaError_t e = cudaMemcpyAsync(dq, q, row, cudaMemcpyDefault, 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dk, k, row, cudaMemcpyDefault, 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dv, v, row, cudaMemcpyDefault, 0);
     if (e == cudaSuccess) e = launch_step(st, seq_len, dq, dk, dv, decay, dout, 0);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(o, dout, row, cudaMemcpyDeviceToHost, 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(o, dout, row, cudaMemcpyDefault, 0);
     if (e == cudaSuccess) e = cudaStreamSynchronize(0);
     return finish("qwn_linear_attention_prefill_host", e);
 }

@@ -1,0 +1,163 @@
+"""The drop-in proof: the reference's own programs run against qwn_cuda.so.
+
+oracle/Makefile (target reflink) builds them from the reference sources into
+oracle/_ref, linked against this library where it serves the reference's
+APIs:
+
+* c/tests/test_kv_cache.c, test_turboquant.c, test_qwanto_arch.c (linear
+  attention) and test_nextgen_suite.c (token eviction), with
+  c/qwanto_turboquant.c, c/qwanto_attention.c and c/qwanto_pagedeviction.c
+  left out: their calls bind to this library, which the dynamic linker's
+  binding log confirms, and the tests' own checks must pass;
+* the stock qwnrun, which with --backend cuda dlopen()s the qwn_cuda.so next
+  to it (c/qwanto_decode.c:267-462) and offloads its per-layer Q8 KV cache
+  to it (:1658-1724): its logits must match the same binary on the CPU;
+* qwnrun relinked without c/qwn_paged_kv.c and c/qwanto_turboquant.c: its
+  fp16 paged, Q8 and TurboQuant KV caches run on this library's GPU kernels
+  through the reference C API, and its logits must match the stock CPU run.
+
+Logits compare within |d| <= 1e-3 + 1e-3 |ref| (qwnrun prints six decimals).
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import tempfile
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REFDIR = os.path.join(ROOT, "oracle", "_ref")
+LIB = os.path.join(ROOT, "qwanto_b200", "qwn_cuda.so")
+FIXTURE = os.path.join(REFDIR, "fixture_12x2.qwn")
+
+
+def _need(*names):
+    for n in names:
+        if not os.path.exists(os.path.join(REFDIR, n)):
+            pytest.skip(f"oracle/_ref/{n} not built (make -C oracle reflink where the reference is present)")
+
+
+def _bound_to_library(stderr: str, symbols) -> dict:
+    """symbol -> True when the dynamic linker bound it to qwn_cuda.so."""
+    out = {s: False for s in symbols}
+    for line in stderr.splitlines():
+        if "binding file" not in line or "qwn_cuda.so" not in line.split(" to ")[-1]:
+            continue
+        for s in symbols:
+            if f"`{s}'" in line:
+                out[s] = True
+    return out
+
+
+REFTESTS = {
+    "reftest_kv_cache": ("QWN typed KV cache reference tests passed",
+                         ["qwn_q8_cache_append", "qwn_q8_cache_attention_head", "qwn_kv_cache_mode_parse"]),
+    "reftest_turboquant": ("[SUCCESS] All TurboQuant verification tests passed",
+                           ["qwn_turboquant_quantize_token", "qwn_turboquant_attention_head",
+                            "qwn_turboquant_dot_key_avx2"]),
+    "reftest_qwanto_arch": ("Correctness validated",
+                            ["qwanto_linear_attention_prefill", "qwanto_linear_attention_init"]),
+    "reftest_nextgen": ("[SUCCESS] All Next-Gen Qwanto core subsystems passed",
+                        ["qwn_paged_eviction_insert", "qwn_paged_eviction_prune",
+                         "qwn_paged_eviction_update_scores"]),
+}
+
+
+@pytest.mark.parametrize("name", sorted(REFTESTS))
+def test_reference_test_passes_against_this_library(cuda, name):
+    _need(name)
+    marker, symbols = REFTESTS[name]
+    env = dict(os.environ, LD_DEBUG="bindings", OMP_NUM_THREADS="8")
+    r = subprocess.run([os.path.join(REFDIR, name)], capture_output=True, text=True, env=env, timeout=600,
+                       cwd=REFDIR)
+    assert r.returncode == 0, f"{name} exited {r.returncode}:\n{r.stdout[-3000:]}"
+    assert marker in r.stdout, r.stdout[-3000:]
+    bound = _bound_to_library(r.stderr, symbols)
+    assert all(bound.values()), f"not served by qwn_cuda.so: {[s for s, b in bound.items() if not b]}"
+
+
+def _serve_logits(exe: str, tokens, *flags, env=None) -> tuple[np.ndarray, str]:
+    """qwnrun's persistent protocol: one FORWARD per token, LOGITS back."""
+    stdin = "".join(f"FORWARD {t}\n" for t in tokens)
+    r = subprocess.run([exe, FIXTURE, "--serve", "--ctx-size", "512", *flags], input=stdin, capture_output=True,
+                       text=True, timeout=600, env=env)
+    assert r.returncode == 0, f"{os.path.basename(exe)} {flags} exited {r.returncode}:\n{r.stderr[-3000:]}"
+    rows, cur = [], None
+    for line in r.stdout.splitlines():
+        if line.startswith("LOGITS"):
+            cur = []
+            rows.append(cur)
+        elif cur is not None and line.strip():
+            try:
+                cur.append(float(line))
+            except ValueError:
+                cur = None
+    out = np.array(rows, dtype=np.float64)
+    assert out.shape == (len(tokens), 64), out.shape
+    return out, r.stderr
+
+
+def _close(got, ref, what):
+    err = np.abs(got - ref)
+    bad = err > 1e-3 + 1e-3 * np.abs(ref)
+    assert not bad.any(), f"{what}: {int(bad.sum())} logits off, max err {err.max():.3e}"
+
+
+TOKENS = [int(x) for x in np.random.default_rng(5).integers(0, 63, size=96)]
+
+
+@pytest.fixture(scope="module")
+def workdir():
+    """qwnrun binaries with qwn_cuda.so beside them, as qwnrun expects it."""
+    _need("qwnrun", "qwnrun_b200", "fixture_12x2.qwn")
+    d = tempfile.mkdtemp(prefix="qwnrun_")
+    for n in ("qwnrun", "qwnrun_b200"):
+        shutil.copy2(os.path.join(REFDIR, n), d)
+    shutil.copy2(LIB, d)
+    yield d
+    shutil.rmtree(d, ignore_errors=True)
+
+
+@pytest.fixture(scope="module")
+def cpu_logits(workdir):
+    """The stock reference decoder on the CPU, per KV-cache mode."""
+    return {mode: _serve_logits(os.path.join(workdir, "qwnrun"), TOKENS, "--backend", "cpu", "--kv-cache", mode)[0]
+            for mode in ("q8", "fp16", "turboquant-q4")}
+
+
+def test_stock_qwnrun_loads_library_and_offloads_q8(cuda, workdir, cpu_logits):
+    """--backend cuda --kv-cache q8: the loader accepts qwn_cuda.so (ABI v1,
+    HyperVSQ-2 74/256 and the Q8 KV capability) and every layer's KV append
+    and attention go through it; logits match the CPU decoder."""
+    exe = os.path.join(workdir, "qwnrun")
+    got, err = _serve_logits(exe, TOKENS, "--backend", "cuda", "--kv-cache", "q8")
+    assert "ABI 1 loaded" in err, err[-2000:]
+    _close(got, cpu_logits["q8"], "qwnrun --backend cuda --kv-cache q8")
+    r = subprocess.run([exe, FIXTURE, "0123456789", "--max-tokens", "8", "--ctx-size", "256", "--backend", "cuda",
+                        "--kv-cache", "q8", "--seed", "7"], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    assert "status=ok" in r.stderr
+    assert "kv_cache_kernel=q8-paged-b200" in r.stderr, [l for l in r.stderr.splitlines() if "kv_cache" in l][:3]
+
+
+@pytest.mark.parametrize("mode", ["fp16", "q8", "turboquant-q4"])
+def test_relinked_qwnrun_kv_modes_on_gpu(cuda, workdir, cpu_logits, mode):
+    """qwnrun relinked against this library instead of c/qwn_paged_kv.c and
+    c/qwanto_turboquant.c: the decoder's paged fp16 pool, Q8 cache and
+    TurboQuant cache (qwn_kv_pool_*, qwn_paged_kv_write,
+    qwn_paged_attention_gather_head, qwn_q8_cache_*, qwn_turboquant_*) run on
+    the GPU through the reference C API; logits match the stock CPU run."""
+    env = dict(os.environ, LD_DEBUG="bindings")
+    got, err = _serve_logits(os.path.join(workdir, "qwnrun_b200"), TOKENS, "--backend", "cpu", "--kv-cache", mode,
+                             env=env)
+    served = {"fp16": ["qwn_paged_kv_write", "qwn_paged_attention_gather_head", "qwn_block_table_append_token"],
+              "q8": ["qwn_q8_cache_append", "qwn_q8_cache_attention_head"],
+              "turboquant-q4": ["qwn_turboquant_quantize_token", "qwn_turboquant_attention_head"]}[mode]
+    bound = _bound_to_library(err, served)
+    assert all(bound.values()), f"not served by qwn_cuda.so: {bound}"
+    _close(got, cpu_logits[mode], f"relinked qwnrun --kv-cache {mode}")
