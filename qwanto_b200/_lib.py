@@ -259,7 +259,10 @@ def lib() -> C.CDLL:
     if _lib is None:
         if not os.path.exists(LIB_PATH):
             raise RuntimeError(f"{LIB_PATH} is missing: run __graft_entry__.build() (no CPU fallback exists)")
-        L = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
+        # RTLD_LOCAL: the library exports the reference's C API names, which
+        # must not interpose on another library of the process that defines
+        # them too (the reference's own code loaded beside it in the tests)
+        L = C.CDLL(LIB_PATH, mode=C.RTLD_LOCAL)
         for name, (res, args) in _SIGS.items():
             fn = getattr(L, name)
             fn.restype = res
