@@ -190,11 +190,16 @@ def global_lengths(wl: dict, n_gpus: int) -> np.ndarray:
 # ---------------------------------------------------------------------------
 # reference arm: the reference's own CPU code (oracle/_ref), bounded sample
 # ---------------------------------------------------------------------------
-def reference_rate(wl: dict, lens: np.ndarray, steps: int, warmup: int, layers_sample: int, threads: int = 0):
+def reference_rate(wl: dict, lens: np.ndarray, steps: int, warmup: int, layers_sample: int, threads: int = 0,
+                   budget_s: float = 0.0):
     """Decode steps of the reference CPU path on `lens` over the first
     `layers_sample` layers with `threads` OpenMP threads (0 = every host
-    core); returns (seq-steps/s scaled to all layers, seconds per sampled
-    step, threads, codec name)."""
+    core).  Each step's Q/K/V rows are generated before its timer starts (the
+    decoder's projections make them), so a step times the append and the
+    attention only.  With budget_s > 0 the timed steps stop early (after at
+    least 3) once they would run past budget_s seconds.  Returns (seq-steps/s
+    scaled to all layers, seconds per sampled step, threads, codec name,
+    timed steps)."""
     import ctypes as C
     from oracle import oracle as O
     R = O.ref()
@@ -207,20 +212,29 @@ def reference_rate(wl: dict, lens: np.ndarray, steps: int, warmup: int, layers_s
     # thread count is set explicitly (the affinity mask bounds it)
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     R.qref_set_threads(threads if threads > 0 else cores)
+    R.qref_batch_prepare.restype = C.c_int
+    R.qref_batch_prepare.argtypes = [C.c_void_p]
     ids = np.ascontiguousarray(lens, dtype=np.int32)
     h = R.qref_batch_create(codec, ids.size, ids.ctypes.data_as(C.POINTER(C.c_int32)), layers_sample,
                             wl["H"], wl["HK"], HD, steps + warmup + 1, wl["seed"])
     if not h:
         return None
     for _ in range(warmup):
+        R.qref_batch_prepare(h)
         R.qref_batch_step(h, layers_sample)
-    t0 = time.perf_counter()
-    for _ in range(steps):
+    total, done = 0.0, 0
+    for i in range(steps):
+        R.qref_batch_prepare(h)
+        t0 = time.perf_counter()
         R.qref_batch_step(h, layers_sample)
-    dt = (time.perf_counter() - t0) / steps
+        total += time.perf_counter() - t0
+        done += 1
+        if budget_s > 0 and done >= 3 and total / done * (done + 1) > budget_s:
+            break
+    dt = total / done
     R.qref_batch_destroy(h)
     rate = ids.size / (dt * wl["layers"] / layers_sample)
-    return rate, dt, int(R.qref_max_threads()), {1: "q8_b64_f32", 3: "tq35_g64", 5: "f16_paged"}[codec]
+    return (rate, dt, int(R.qref_max_threads()), {1: "q8_b64_f32", 3: "tq35_g64", 5: "f16_paged"}[codec], done)
 
 
 def one_thread_row(wl, lens: np.ndarray, steps: int, unit: str, what: str):
@@ -229,27 +243,32 @@ def one_thread_row(wl, lens: np.ndarray, steps: int, unit: str, what: str):
     res = reference_rate(wl, lens, steps, 0, 1, threads=1)
     if not res:
         return None
-    rate, dt, threads, cname = res
+    rate, dt, threads, cname, done = res
     return {"value": rate, "unit": unit, "cores": threads, "kind": "reference",
-            "sample": f"{what}, first 1 of {wl['layers']} layers, {steps} timed step(s) on one thread, "
+            "sample": f"{what}, first 1 of {wl['layers']} layers, {done} timed step(s) on one thread, "
                       f"scaled x{wl['layers']:g}; reference codec {cname}"}
 
 
 def run_reference(args, wl, world, rank):
+    """The reference's own CPU implementation of the path (oracle/_ref, built
+    from the reference sources) on every host core: exactly --steps full
+    decode steps of the workload (every sequence, every layer) after
+    --warmup untimed ones, unless a step takes so long that the run would
+    exceed ~3 minutes, in which case it stops after the steps that fit (at
+    least 3) and says so."""
     if rank != 0:
         return 0
     lens = global_lengths(wl, 1)
-    layers_sample = min(2, wl["layers"])
-    steps = max(1, min(args.steps, 20)) if wl["batch"] * wl["lo"] > 100000 else max(1, args.steps)
-    res = reference_rate(wl, lens, steps, max(0, args.warmup), layers_sample)
+    t_start = time.perf_counter()
+    res = reference_rate(wl, lens, max(1, args.steps), max(0, args.warmup), wl["layers"], budget_s=150.0)
     if res is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (the reference CPU library) is not built"}))
         return 0
-    rate, dt, threads, cname = res
-    sample = (f"{lens.size} sequences, first {layers_sample} of {wl['layers']} layers per step "
-              f"(time scaled x{wl['layers'] / layers_sample:g}), reference codec {cname}")
-    line = {"metric": METRIC, "value": rate, "unit": "seq-steps/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * dt * wl["layers"] / layers_sample,
+    rate, dt, threads, cname, done = res
+    sample = (f"{lens.size} sequences, all {wl['layers']} layers per step, {done} timed step(s) after "
+              f"{max(0, args.warmup)} warm-up; Q/K/V rows generated before each step's timer; reference codec {cname}")
+    line = {"metric": METRIC, "value": rate, "unit": "seq-steps/s", "n_gpus": world, "steps": done,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * dt,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_of(wl["codec"]),
             "data": "synthetic", "impl": "reference",
             "config": {"workload": wl["name"], "global_batch": int(lens.size), "layers": wl["layers"],
@@ -257,7 +276,8 @@ def run_reference(args, wl, world, rank):
                        "parallelism": "host cores (OpenMP over sequence x query head)"},
             "cpu_baseline": {"value": rate, "unit": "seq-steps/s", "cores": threads, "kind": "reference",
                              "sample": sample},
-            "e2e": {"value": rate, "unit": "seq-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": rate, "unit": "seq-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - t_start}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -441,7 +461,7 @@ def run_ours(args, wl, world, rank, local):
         ls = min(2, L)
         res = reference_rate(wl, lens, 2 if L > 1 else 20, 1, ls)
         if res:
-            rate, dt, threads, cname = res
+            rate, dt, threads, cname, _ = res
             line["cpu_baseline"] = {"value": rate, "unit": "seq-steps/s", "cores": threads, "kind": "reference",
                                     "sample": f"{len(lens)} sequences (same lengths), first {ls} of {L} layers, "
                                               f"{2 if L > 1 else 20} timed steps, scaled x{L / ls:g}; "
@@ -627,7 +647,7 @@ def run_split(args, wl, world, rank, local):
         if world == 1 and not args.no_cpu_baseline:
             res = reference_rate(wl, np.array([c0], np.int32), 3, 1, 1)
             if res:
-                rate, dt, threads, cname = res
+                rate, dt, threads, cname, _ = res
                 line["cpu_baseline"] = {"value": rate, "unit": "layer-steps/s", "cores": threads, "kind": "reference",
                                         "sample": f"1 sequence of {c0} tokens, 3 timed steps; reference codec {cname}"}
                 line["cpu_baseline"]["one_thread"] = one_thread_row(wl, np.array([c0], np.int32), 1, "layer-steps/s",
@@ -751,7 +771,7 @@ def run_churn(args, wl, world, rank, local):
         if world == 1 and not args.no_cpu_baseline:
             res = reference_rate(wl, lens.astype(np.int32), 2, 1, 1)
             if res:
-                rate, dt, threads, cname = res
+                rate, dt, threads, cname, _ = res
                 line["cpu_baseline"] = {"value": rate, "unit": "seq-steps/s", "cores": threads, "kind": "reference",
                                         "sample": f"{B} sequences (same lengths), append + attend, 2 timed steps, "
                                                   f"no eviction; reference codec {cname}"}

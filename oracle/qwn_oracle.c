@@ -39,9 +39,12 @@ float qor_normal(uint64_t seed, uint64_t stream, uint64_t index) {
     return (float)(sum - 393210) * (1.0f / 65536.0f);
 }
 
+static float normal_keyed(uint64_t key, uint64_t index);
+
 void qor_fill_normal(uint64_t seed, uint64_t stream, uint64_t first_index, float *out,
                      size_t n) {
-    for (size_t i = 0; i < n; i++) out[i] = qor_normal(seed, stream, first_index + i);
+    const uint64_t key = qor_mix64(seed ^ qor_mix64(stream));  /* qor_normal's key, once per row */
+    for (size_t i = 0; i < n; i++) out[i] = normal_keyed(key, first_index + i);
 }
 
 void qor_permuted_free_stack(uint64_t seed, int total, int32_t *stack) {
