@@ -69,6 +69,13 @@ struct AttnArgs {
     float *part_m, *part_l, *part_o;  // non-null: export unnormalised (m, l, o)
     const float *new_k, *new_v;       // non-null: fused append of the newest token
     uint32_t *status;
+    // 1: the host found that the kernel before this one on the stream (an
+    // attention launch of the same pool, on another layer, whose outputs this
+    // launch does not read) writes nothing this launch reads, so the setup,
+    // the tile stream and the fused append start before that kernel ends;
+    // the launch waits for it only before its first write to memory that
+    // kernel also writes (plans, partial slots, counters, outputs)
+    uint32_t early;
     // split-KV over ranks (xworld > 0): every segment's partial goes to each
     // rank's exchange buffer (xbuf[p] as mapped here) and the ranks' partials
     // of the segment merge into the output
@@ -1742,9 +1749,15 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     }
     __syncwarp();
     // let the stream's next kernel start its CTAs as SMs free up; wait for the
-    // previous kernel's results before the first global access
+    // previous kernel's results before the first global access -- or, in the
+    // early mode, before the first write that kernel could race with
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (!A.early) asm volatile("griddepcontrol.wait;" ::: "memory");
+    // (returns at once once the previous kernel has finished; reading the flag
+    // from the parameter bank keeps it out of the registers)
+    auto dep_wait = [&]() {
+        if (A.early) asm volatile("griddepcontrol.wait;" ::: "memory");
+    };
 
     const uint32_t HK = A.kv_heads;
     uint64_t W = (uint64_t)gridDim.x * kWarpsPerCta;
@@ -1757,15 +1770,29 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     // the CTA reads the sequence table.
     uint32_t *plan = A.plans ? A.plans + 32 + ((size_t)blockIdx.x * kWarpsPerCta + warp) * kPlanWords : nullptr;
     uint32_t pw0 = 0, pw1 = 0, pw2 = 0, pw3 = 0, epoch = 0;
+    bool torn = false;
     if (plan) {
-        pw0 = plan[lane]; pw1 = plan[32 + lane]; pw2 = plan[64 + lane]; pw3 = plan[96 + lane];
+        if (!A.early) {
+            pw0 = plan[lane]; pw1 = plan[32 + lane]; pw2 = plan[64 + lane]; pw3 = plan[96 + lane];
+        } else {
+            // the previous kernel may be rewriting this record: read it as a
+            // sequence lock (key, data, key again; a writer invalidates the key
+            // before the data and publishes it after with a release): a torn
+            // record fails the check and the launch computes its setup
+            const uint32_t k0 = ld_acquire_gpu(plan + (lane & 7));
+            pw0 = __ldcg(plan + lane); pw1 = __ldcg(plan + 32 + lane);
+            pw2 = __ldcg(plan + 64 + lane); pw3 = __ldcg(plan + 96 + lane);
+            __threadfence();
+            const uint32_t k1 = ld_relaxed_gpu(plan + (lane & 7));
+            torn = k0 != k1 || (lane < 8 && pw0 != k0);
+        }
         epoch = A.plans[0];
     }
     fill_len_cache(A);
     const uint32_t key = lane == 0 ? epoch : lane == 1 ? A.num_seqs : lane == 2 ? A.attend_limit
                        : lane == 3 ? A.t_begin : lane == 4 ? A.t_end : lane == 5 ? (A.new_k ? 1u : 0u)
                        : lane == 6 ? gridDim.x : 0x504C414Eu;
-    const bool hit = plan != nullptr && __all_sync(0xffffffffu, lane >= 8 || pw0 == key);
+    const bool hit = plan != nullptr && __all_sync(0xffffffffu, (lane >= 8 || pw0 == key) && !torn);
 
     Walk cons;
     uint32_t n = 0;
@@ -1776,7 +1803,10 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         auto w32 = [&](int i) { return __shfl_sync(0xffffffffu, pw0, i); };
         auto w64 = [&](int i) { return (uint64_t)w32(i) | ((uint64_t)w32(i + 1) << 32); };
         n = w32(20);
-        if (n == 0) return;
+        if (n == 0) {
+            dep_wait();  // finishing means the previous kernel has finished too
+            return;
+        }
         cons.i = w32(8); cons.h = w32(9); cons.tile = w32(10);
         cons.seg_base = w64(11); cons.vbase = w64(13);
         cons.geo.seq = (int32_t)w32(15); cons.geo.tok_lo = (int32_t)w32(16); cons.geo.tok_hi = (int32_t)w32(17);
@@ -1862,8 +1892,11 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
             window_ready();
         }
         if (plan) {  // record the plan for the following launches of this step
+            dep_wait();  // an earlier launch may still read or write this record
+            if (lane < 8) st_relaxed_gpu(plan + lane, 0xFFFFFFFFu);  // invalidate, then data, then key
+            __threadfence();
+            __syncwarp();
             if (lane == 0) {
-                for (int i = 0; i < 8; i++) plan[i] = 0xFFFFFFFFu;  // key last
                 plan[8] = cons.i; plan[9] = cons.h; plan[10] = cons.tile;
                 plan[11] = (uint32_t)cons.seg_base; plan[12] = (uint32_t)(cons.seg_base >> 32);
                 plan[13] = (uint32_t)cons.vbase; plan[14] = (uint32_t)(cons.vbase >> 32);
@@ -1879,10 +1912,14 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
                 plan[64 + lane] = win->hv[0][lane];
                 plan[96 + lane] = (uint32_t)win->app[0][lane];
             }
+            __threadfence();
             __syncwarp();
-            if (lane < 8) plan[lane] = key;
+            if (lane < 8) st_release_gpu(plan + lane, key);
         }
-        if (n == 0) return;
+        if (n == 0) {
+            dep_wait();
+            return;
+        }
     }
 
     window_resolve(A, win, 0);
@@ -1937,6 +1974,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
                 if (++s2 == (uint32_t)S) { s2 = 0; p2 ^= 1u; }
                 mbar_wait_bounded(&bars[s2], p2);
             }
+            dep_wait();
             return;
         }
         const int tile_tok0 = (int)(cons.geo.tile0 + cons.tile) * 16;
@@ -1990,6 +2028,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
 
         // end of this warp's share of the segment?
         if (cons.tile + nt == cons.geo.ntiles || k + nt == n) {
+            dep_wait();  // its slot (or output rows) may still be read by the previous kernel
             const uint32_t s_idx = cons.i * HK + cons.h;
             const uint32_t np = finish_segment<OPS, XCHG>(A, state, s_idx, cons.vbase, cons.geo.ntiles, Tv, W, wid);
             if (XCHG && np == 1) xpend |= 1ull << s_idx;
@@ -2222,6 +2261,34 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
     A.new_k = a.new_k;
     A.new_v = a.new_v;
     A.status = p->status;
+    // Early start.  Every other kernel of this library is an ordinary launch
+    // (the next launch waits for it to finish), so this attention kernel can
+    // overlap only an attention kernel of the stream that precedes it
+    // directly.  That kernel writes its layer's newest-token tiles, its output
+    // rows, the pool's partial slots, counters and plans.  When the previous
+    // attention launch of this pool on this stream was of another layer,
+    // exported no page mass or partials, and its output rows do not overlap
+    // this launch's query, new K/V or output, this launch reads nothing it
+    // writes before the kernel's dependency wait, which then sits before the
+    // first write of slots, counters, plans or outputs.  (An operation queued
+    // in between only delays the start, so the check stays sound.)
+    {
+        const size_t qbytes = (size_t)a.num_seqs * a.query_heads * kHeadDim * sizeof(float);
+        const size_t kvbytes = (size_t)a.num_seqs * p->kv_heads * kHeadDim * sizeof(float);
+        const uintptr_t q0 = (uintptr_t)a.query, o0 = (uintptr_t)a.output;
+        const uintptr_t k0 = (uintptr_t)a.new_k, v0 = (uintptr_t)a.new_v;
+        const bool eligible = !a.part_o && !a.peers && !a.page_mass && a.output;
+        std::lock_guard<std::mutex> lk(p->last_mu);
+        const Pool::LastAttention &L = p->last_attn;
+        auto clear = [&](uintptr_t lo, size_t n) { return lo + n <= L.out_lo || lo >= L.out_hi; };
+        A.early = eligible && L.valid && L.stream == s && L.layer != a.layer && clear(q0, qbytes) &&
+                  clear(o0, qbytes) && (!a.new_k || (clear(k0, kvbytes) && clear(v0, kvbytes)));
+        p->last_attn.valid = eligible;
+        p->last_attn.stream = s;
+        p->last_attn.layer = a.layer;
+        p->last_attn.out_lo = o0;
+        p->last_attn.out_hi = o0 + qbytes;
+    }
     if (a.peers) {
         for (uint32_t r = 0; r < a.peers->world; r++) A.xbuf[r] = static_cast<uint8_t *>(a.peers->buffers[r]);
         A.xrank = a.peers->rank;

@@ -81,6 +81,15 @@ struct Pool {
     cudaEvent_t *layer_in_ev = nullptr, *layer_out_ev = nullptr;
     uint32_t layer_events = 0;
     std::mutex mu;
+    // the pool's last attention launch, for the next launch's early start
+    // (AttnArgs::early): its stream, layer and output range
+    struct LastAttention {
+        bool valid = false;
+        cudaStream_t stream = nullptr;
+        uint32_t layer = 0;
+        uintptr_t out_lo = 0, out_hi = 0;
+    } last_attn;
+    std::mutex last_mu;
 };
 
 constexpr int kPartialFloats = kMaxGroup * kHeadDim + 2 * kMaxGroup;  // room for o[G][128], m[G], l[G]
@@ -223,6 +232,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     for (uint32_t it = 0; it < kWaitLimit; ++it)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu(uint32_t *p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
     uint32_t old;

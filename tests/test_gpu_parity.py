@@ -486,3 +486,59 @@ def test_hypervsq2_gemv_matches_reference_cpu(cuda, oracle_mod):
         _lib.check("release", qb.lib().qwn_cuda_abi_release_tensor(C.byref(ctx.h), C.byref(th)))
     finally:
         ctx.close()
+
+
+@pytest.mark.parametrize("codec", [2, 4, 5])
+def test_back_to_back_layer_launches_parity(cuda, codec):
+    """The layers of a step launched back to back on one stream, as a decoder
+    issues them: each launch starts its setup, tile stream and fused append
+    while the previous layer's kernel finishes (early start), the first
+    launch after the page allocation records the step's plan while the
+    second may already read it.  Every layer's output equals the oracle,
+    tables and pages stay bit-exact; then the same step with one output
+    buffer shared by all layers (which disables the early start) leaves the
+    last layer's rows in it."""
+    import qwanto_b200 as qb
+    torch = cuda
+    L, H, HK = 6, 32, 8
+    lens = [1500, 37, 900, 2100, 1, 640, 1203, 16]
+    n = len(lens)
+    tw = Twin(cuda, codec, layers=L, kv_heads=HK, page_tokens=16, total_pages=800, max_seqs=n, max_pages=160,
+              query_heads=H, perm_seed=9, seed=17)
+    try:
+        tw.prefill(list(range(n)), lens)
+        W, Wq = HK * 128, H * 128
+        ids = torch.arange(n, dtype=torch.int32, device="cuda")
+        for step in range(3):
+            tw.gpu.seq_append(n)
+            assert tw.ora.append(list(range(n)), [1] * n) == 0
+            pos_host = tw.ora.lens().copy() - 1
+            pos = torch.tensor(pos_host, dtype=torch.int32, device="cuda")
+            q = torch.empty((L, n, Wq), device="cuda")
+            k = torch.empty((L, n, W), device="cuda")
+            v = torch.empty((L, n, W), device="cuda")
+            for layer in range(L):
+                qb.generate_rows(q[layer], n, Wq, 1, tw.seed, layer, ids, pos)
+                qb.generate_rows(k[layer], n, W, 2, tw.seed, layer, ids, pos)
+                qb.generate_rows(v[layer], n, W, 3, tw.seed, layer, ids, pos)
+            torch.cuda.synchronize()
+            shared = step == 2
+            out = torch.zeros((1 if shared else L, n, Wq), device="cuda")
+            for layer in range(L):
+                tw.gpu.decode(layer, n, H, q[layer], out[0 if shared else layer], key=k[layer], value=v[layer])
+            torch.cuda.synchronize()
+            assert tw.gpu.check() == 0
+            for layer in range(L):
+                for s in range(n):
+                    p = int(pos_host[s])
+                    assert tw.ora.write(s, layer, p, tw.row(2, s, layer, p, W), tw.row(3, s, layer, p, W)) == 0
+                if shared and layer != L - 1:
+                    continue
+                ref = np.stack([tw.ora.attention(s, layer, int(pos_host[s]) + 1, tw.row(1, s, layer, int(pos_host[s]), Wq),
+                                                 H, 1.0 / np.sqrt(128.0)) for s in range(n)])
+                got = out[0 if shared else layer].cpu().numpy().reshape(n, H, 128)
+                assert_close(got, ref, f"codec {codec} step {step} layer {layer}")
+            tw.assert_state_equal()
+        tw.assert_pages_equal()
+    finally:
+        tw.close()
