@@ -28,6 +28,7 @@
 #include "kv_store.cuh"
 
 #include <float.h>
+#include <cstring>
 
 namespace qkv {
 namespace {
@@ -1770,29 +1771,17 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     // the CTA reads the sequence table.
     uint32_t *plan = A.plans ? A.plans + 32 + ((size_t)blockIdx.x * kWarpsPerCta + warp) * kPlanWords : nullptr;
     uint32_t pw0 = 0, pw1 = 0, pw2 = 0, pw3 = 0, epoch = 0;
-    bool torn = false;
     if (plan) {
-        if (!A.early) {
-            pw0 = plan[lane]; pw1 = plan[32 + lane]; pw2 = plan[64 + lane]; pw3 = plan[96 + lane];
-        } else {
-            // the previous kernel may be rewriting this record: read it as a
-            // sequence lock (key, data, key again; a writer invalidates the key
-            // before the data and publishes it after with a release): a torn
-            // record fails the check and the launch computes its setup
-            const uint32_t k0 = ld_acquire_gpu(plan + (lane & 7));
-            pw0 = __ldcg(plan + lane); pw1 = __ldcg(plan + 32 + lane);
-            pw2 = __ldcg(plan + 64 + lane); pw3 = __ldcg(plan + 96 + lane);
-            __threadfence();
-            const uint32_t k1 = ld_relaxed_gpu(plan + (lane & 7));
-            torn = k0 != k1 || (lane < 8 && pw0 != k0);
-        }
+        // (in the early mode the host has checked that the previous kernel does
+        // not record plans, so the records are stable while they are read)
+        pw0 = plan[lane]; pw1 = plan[32 + lane]; pw2 = plan[64 + lane]; pw3 = plan[96 + lane];
         epoch = A.plans[0];
     }
     fill_len_cache(A);
     const uint32_t key = lane == 0 ? epoch : lane == 1 ? A.num_seqs : lane == 2 ? A.attend_limit
                        : lane == 3 ? A.t_begin : lane == 4 ? A.t_end : lane == 5 ? (A.new_k ? 1u : 0u)
                        : lane == 6 ? gridDim.x : 0x504C414Eu;
-    const bool hit = plan != nullptr && __all_sync(0xffffffffu, (lane >= 8 || pw0 == key) && !torn);
+    const bool hit = plan != nullptr && __all_sync(0xffffffffu, lane >= 8 || pw0 == key);
 
     Walk cons;
     uint32_t n = 0;
@@ -1892,11 +1881,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
             window_ready();
         }
         if (plan) {  // record the plan for the following launches of this step
-            dep_wait();  // an earlier launch may still read or write this record
-            if (lane < 8) st_relaxed_gpu(plan + lane, 0xFFFFFFFFu);  // invalidate, then data, then key
-            __threadfence();
-            __syncwarp();
+            dep_wait();  // the previous kernel may still be reading this record
             if (lane == 0) {
+                for (int i = 0; i < 8; i++) plan[i] = 0xFFFFFFFFu;  // key last
                 plan[8] = cons.i; plan[9] = cons.h; plan[10] = cons.tile;
                 plan[11] = (uint32_t)cons.seg_base; plan[12] = (uint32_t)(cons.seg_base >> 32);
                 plan[13] = (uint32_t)cons.vbase; plan[14] = (uint32_t)(cons.vbase >> 32);
@@ -1912,9 +1899,8 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
                 plan[64 + lane] = win->hv[0][lane];
                 plan[96 + lane] = (uint32_t)win->app[0][lane];
             }
-            __threadfence();
             __syncwarp();
-            if (lane < 8) st_release_gpu(plan + lane, key);
+            if (lane < 8) plan[lane] = key;
         }
         if (n == 0) {
             dep_wait();
@@ -2267,7 +2253,8 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
     // directly.  That kernel writes its layer's newest-token tiles, its output
     // rows, the pool's partial slots, counters and plans.  When the previous
     // attention launch of this pool on this stream was of another layer,
-    // exported no page mass or partials, and its output rows do not overlap
+    // recorded no plans (the records this launch reads early), exported no
+    // page mass or partials, and its output rows do not overlap
     // this launch's query, new K/V or output, this launch reads nothing it
     // writes before the kernel's dependency wait, which then sits before the
     // first write of slots, counters, plans or outputs.  (An operation queued
@@ -2279,11 +2266,23 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
         const uintptr_t k0 = (uintptr_t)a.new_k, v0 = (uintptr_t)a.new_v;
         const bool eligible = !a.part_o && !a.peers && !a.page_mass && a.output;
         std::lock_guard<std::mutex> lk(p->last_mu);
+        // does this launch record plans?  The kernel records on a key miss; the
+        // host mirrors the key (the epoch part through plan_valid, which every
+        // kernel that changes lengths or tables clears)
+        const uint32_t pkey[6] = {a.num_seqs, a.attend_limit, a.t_begin, a.t_end, a.new_k ? 1u : 0u,
+                                  A.group > 4 ? 2u : 1u};
+        bool records = false;
+        if (A.plans) {
+            records = !p->plan_valid || std::memcmp(pkey, p->plan_key, sizeof(pkey)) != 0;
+            p->plan_valid = true;
+            std::memcpy(p->plan_key, pkey, sizeof(pkey));
+        }
         const Pool::LastAttention &L = p->last_attn;
         auto clear = [&](uintptr_t lo, size_t n) { return lo + n <= L.out_lo || lo >= L.out_hi; };
-        A.early = eligible && L.valid && L.stream == s && L.layer != a.layer && clear(q0, qbytes) &&
+        A.early = eligible && L.valid && !L.recorded && L.stream == s && L.layer != a.layer && clear(q0, qbytes) &&
                   clear(o0, qbytes) && (!a.new_k || (clear(k0, kvbytes) && clear(v0, kvbytes)));
         p->last_attn.valid = eligible;
+        p->last_attn.recorded = records;
         p->last_attn.stream = s;
         p->last_attn.layer = a.layer;
         p->last_attn.out_lo = o0;

@@ -187,6 +187,7 @@ cudaError_t launch_page_mass(Pool *p, uint32_t n, const int32_t *seq_ids, uint32
 cudaError_t launch_evict(Pool *p, uint32_t n, const int32_t *seq_ids, const float *mass, const uint8_t *flags,
                          uint32_t budget, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
+    plans_invalidated(p);  // compaction moves the plans' epoch
     evict_rank_kernel<<<n, 256, 0, s>>>(n, seq_ids, mass, flags, budget, p->seq_lens, p->seq_pages,
                                         p->page_scores, p->evict_dead, p->evict_count, p->page_tokens,
                                         p->max_pages_per_seq);

@@ -85,12 +85,22 @@ struct Pool {
     // (AttnArgs::early): its stream, layer and output range
     struct LastAttention {
         bool valid = false;
+        bool recorded = false;  // it (re)wrote the plan records
         cudaStream_t stream = nullptr;
         uint32_t layer = 0;
         uintptr_t out_lo = 0, out_hi = 0;
     } last_attn;
+    // host mirror of the plan records' key: plan_valid is cleared by every
+    // launch that changes lengths or tables (the device epoch moves)
+    bool plan_valid = false;
+    uint32_t plan_key[6] = {};
     std::mutex last_mu;
 };
+// a launch that changes lengths or page tables (the plans' epoch) was queued
+inline void plans_invalidated(Pool *p) {
+    std::lock_guard<std::mutex> lk(p->last_mu);
+    p->plan_valid = false;
+}
 
 constexpr int kPartialFloats = kMaxGroup * kHeadDim + 2 * kMaxGroup;  // room for o[G][128], m[G], l[G]
 // launch plans: a 32-word header (word 0 = epoch), then kPlanWords per warp
@@ -233,22 +243,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_relaxed_gpu(uint32_t *p, uint32_t v) {
-    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
     uint32_t old;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");

@@ -270,6 +270,7 @@ template <int C> struct PrefillL {
 cudaError_t launch_seq_append(Pool *p, uint32_t n, const int32_t *seq_ids, const int32_t *counts,
                               cudaStream_t s) {
     if (n == 0) return cudaSuccess;
+    plans_invalidated(p);
     seq_append_kernel<<<1, 32, 0, s>>>(n, seq_ids, counts, p->seq_lens, p->seq_pages, p->page_table,
                                          p->page_scores, p->free_stack, p->free_top, p->page_tokens,
                                          p->max_pages_per_seq, p->max_seqs, p->status, p->plans);
@@ -315,6 +316,7 @@ cudaError_t launch_pool_init_state(Pool *p, cudaStream_t s) {
     if ((e = cudaMemsetAsync(p->status, 0, sizeof(uint32_t), s))) return e;
     if ((e = cudaMemsetAsync(p->counters, 0, sizeof(uint32_t) * counter_count(p), s))) return e;
     // no cached attention plan survives (epoch 0, every record's key invalid)
+    plans_invalidated(p);
     if ((e = cudaMemsetAsync(p->plans, 0xFF, sizeof(uint32_t) * plan_words(p), s))) return e;
     if ((e = cudaMemsetAsync(p->plans, 0, sizeof(uint32_t), s))) return e;
     // free stack: total-1-i, optionally permuted (Fisher-Yates on the host)
