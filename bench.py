@@ -862,6 +862,98 @@ def run_gemv(args) -> int:
     return 0
 
 
+def run_abi_kv(args) -> int:
+    """cfg1 through ABI v1 exactly as qwnrun's CUDA backend drives its Q8 KV
+    cache (c/qwanto_decode.c:1658-1724): per decode step one
+    qwn_cuda_abi_kv_cache_append of the token's K/V rows and one
+    qwn_cuda_abi_kv_cache_attention of the 12 query heads, host buffers and
+    synchronous calls, for this library and for the reference's own GPU
+    library (oracle/_ref/qwn_cuda_ref.so, built from
+    c/cuda/qwn_hypervsq2_cuda_abi.cu; kernel qwn_q8_attention at :175-223) on
+    the same inputs: 2048 tokens prefilled, then 256 timed steps.  Wall time
+    per step (the calls return after their results are on the host) and the
+    libraries' own kernel time (telemetry); outputs are cross-checked.  One
+    JSON line."""
+    import ctypes as C
+    from qwanto_b200 import _lib
+    wl = workload(1)
+    H, HK, T0 = wl["H"], wl["HK"], wl["lo"]
+    steps = args.steps if args.steps > 0 else wl["steps"]
+    libs = {"ours": os.path.join(ROOT, "qwanto_b200", "qwn_cuda.so"),
+            "reference_gpu": os.path.join(ROOT, "oracle", "_ref", "qwn_cuda_ref.so")}
+    P = C.POINTER
+    rng = np.random.default_rng(wl["seed"])
+    ch = HK * HD
+    keys = rng.standard_normal((T0 + steps, ch)).astype(np.float32)
+    vals = rng.standard_normal((T0 + steps, ch)).astype(np.float32)
+    qs = rng.standard_normal((steps, H * HD)).astype(np.float32)
+    line = {"abi_v1_kv": {"workload": wl["name"], "query_heads": H, "kv_heads": HK, "head_dim": HD,
+                          "prefill_tokens": T0, "steps": steps,
+                          "path": "qwn_cuda_abi_kv_cache_append + qwn_cuda_abi_kv_cache_attention per step, "
+                                  "host buffers, synchronous (qwnrun --backend cuda --kv-cache q8)"}}
+    outs = {}
+    for name, path in libs.items():
+        if not os.path.exists(path):
+            line[name] = "not built"
+            continue
+        L = C.CDLL(path, mode=os.RTLD_LOCAL)
+        for fn, argt in (("qwn_cuda_abi_context_create", [P(_lib.ContextOptions), P(_lib.Handle)]),
+                         ("qwn_cuda_abi_context_destroy", [P(_lib.Handle)]),
+                         ("qwn_cuda_abi_kv_cache_create", [P(_lib.Handle), P(_lib.KvCacheOptions), P(_lib.Handle)]),
+                         ("qwn_cuda_abi_kv_cache_destroy", [P(_lib.Handle), P(_lib.Handle)]),
+                         ("qwn_cuda_abi_kv_cache_append", [P(_lib.Handle), P(_lib.KvAppendRequest), P(_lib.Telemetry)]),
+                         ("qwn_cuda_abi_kv_cache_attention", [P(_lib.Handle), P(_lib.KvAttentionRequest),
+                                                              P(_lib.Telemetry)])):
+            getattr(L, fn).restype = C.c_int
+            getattr(L, fn).argtypes = argt
+        o = _lib.init(_lib.ContextOptions())
+        ctx = _lib.init(_lib.Handle())
+        assert L.qwn_cuda_abi_context_create(C.byref(o), C.byref(ctx)) == 0
+        ko = _lib.init(_lib.KvCacheOptions())
+        ko.max_tokens, ko.kv_heads, ko.head_dim = T0 + steps + 16, HK, HD
+        cache = _lib.init(_lib.Handle())
+        assert L.qwn_cuda_abi_kv_cache_create(C.byref(ctx), C.byref(ko), C.byref(cache)) == 0
+        tel = _lib.init(_lib.Telemetry())
+        ap = _lib.init(_lib.KvAppendRequest())
+        ap.cache, ap.n_channels = cache, ch
+        at = _lib.init(_lib.KvAttentionRequest())
+        at.cache, at.query_heads, at.kv_heads, at.head_dim, at.scale = cache, H, HK, HD, 1.0 / math.sqrt(HD)
+        out = np.zeros(H * HD, np.float32)
+        at.host_output = out.ctypes.data_as(P(C.c_float))
+        for t in range(T0):
+            ap.host_key = keys[t].ctypes.data_as(P(C.c_float))
+            ap.host_value = vals[t].ctypes.data_as(P(C.c_float))
+            ap.token = t
+            assert L.qwn_cuda_abi_kv_cache_append(C.byref(ctx), C.byref(ap), C.byref(tel)) == 0
+        k0 = tel.kv_cache_kernel_ms
+        res = np.zeros((steps, H * HD), np.float32)
+        t0 = time.perf_counter()
+        for i in range(steps):
+            t = T0 + i
+            ap.host_key = keys[t].ctypes.data_as(P(C.c_float))
+            ap.host_value = vals[t].ctypes.data_as(P(C.c_float))
+            ap.token = t
+            assert L.qwn_cuda_abi_kv_cache_append(C.byref(ctx), C.byref(ap), C.byref(tel)) == 0
+            at.host_query = qs[i].ctypes.data_as(P(C.c_float))
+            at.position = t
+            assert L.qwn_cuda_abi_kv_cache_attention(C.byref(ctx), C.byref(at), C.byref(tel)) == 0
+            res[i] = out
+        wall = (time.perf_counter() - t0) / steps
+        line[name] = {"steps_per_s": 1.0 / wall, "wall_us_per_step": wall * 1e6,
+                      "kernel_us_per_step": (tel.kv_cache_kernel_ms - k0) * 1000.0 / steps,
+                      "kernel_type": tel.kv_cache_kernel_type.decode(errors="replace")}
+        outs[name] = res
+        L.qwn_cuda_abi_kv_cache_destroy(C.byref(ctx), C.byref(cache))
+        L.qwn_cuda_abi_context_destroy(C.byref(ctx))
+    if len(outs) == 2:
+        a, b = outs["ours"], outs["reference_gpu"]
+        line["max_abs_diff"] = float(np.abs(a - b).max())
+        line["speedup_wall"] = line["ours"]["steps_per_s"] / line["reference_gpu"]["steps_per_s"]
+        line["speedup_kernel"] = line["reference_gpu"]["kernel_us_per_step"] / max(line["ours"]["kernel_us_per_step"], 1e-9)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_linear(args) -> int:
     """Linear attention (qwn_linear_attention_*): decode over a batch of
     sequences' states and prefill of one long sequence, each timed with CUDA
@@ -975,6 +1067,8 @@ def main():
                     help="cfg4 at N>1: partials exchanged in-kernel over NVLink (p2p) or by an NCCL all-gather")
     ap.add_argument("--layers", type=int, default=0, help="override the config's layer count (profiling)")
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling)")
+    ap.add_argument("--abi-kv", action="store_true",
+                    help="cfg1 through ABI v1 (qwnrun's CUDA Q8 KV calls): this library vs the reference GPU library")
     ap.add_argument("--linear", action="store_true",
                     help="time linear-attention decode/prefill against the reference CPU code (one line per shape)")
     args = ap.parse_args()
@@ -982,6 +1076,8 @@ def main():
         return run_gemv(args)
     if args.linear:
         return run_linear(args)
+    if args.abi_kv:
+        return run_abi_kv(args)
     if args.warmup < 3:
         args.warmup = 3  # the timing rules want >= 3 warm-up steps
     wl = with_codec(workload(args.config), args.codec)

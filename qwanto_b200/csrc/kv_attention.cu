@@ -45,6 +45,11 @@ constexpr uint32_t kVirtualEnd = 2;
 // segments split into more parts merge in two levels: groups of this many
 // parts first, then the group results
 constexpr uint32_t kMergeGroup = 16;
+// a small launch (one short sequence, say) whose longest segment would be
+// split into more than kMergeGroup parts uses fewer warps -- every segment
+// then merges in one level -- as long as a warp streams at most this many
+// tiles: a second merge level costs more than streaming these serially
+constexpr uint64_t kOneLevelTilesPerWarp = 24;
 constexpr float kNuFloor = 7.888609052210118e-31f;  // 2^-100
 constexpr float kNuHeadroom = 16384.0f;            // rescale only when a scale exceeds nu * 2^14
 
@@ -1811,22 +1816,34 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         // real units T of the batch and virtual units Tv (each non-empty
         // segment counts kVirtualUnits more)
         uint64_t T = 0;
+        uint32_t seg_v = 0;  // virtual units of the longest segment
         for (uint32_t base = 0; base < A.num_seqs; base += 32) {
             const uint32_t i = base + lane;
             const uint32_t nt = i < A.num_seqs ? geo_of(A, i).ntiles : 0;
-            uint32_t u = nt * HK, uv = nt ? (nt + kVirtualUnits + virtual_tail(A)) * HK : 0;
+            const uint32_t sv = nt ? nt + kVirtualUnits + virtual_tail(A) : 0;
+            uint32_t u = nt * HK, uv = sv * HK, mv = sv;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
                 u += __shfl_xor_sync(0xffffffffu, u, o);
                 uv += __shfl_xor_sync(0xffffffffu, uv, o);
+                mv = max(mv, __shfl_xor_sync(0xffffffffu, mv, o));
             }
             T += u;
             Tv += uv;
+            seg_v = max(seg_v, mv);
         }
-        if (T != 0 && (T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp < W) {
+        uint64_t Wsmall = W;
+        if (T != 0 && (T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp < Wsmall)
+            Wsmall = (T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
+        if (T != 0) {
+            // at most kMergeGroup - 1 warp ranges start inside the longest segment
+            const uint64_t W1 = (uint64_t)(kMergeGroup - 1) * Tv / seg_v;
+            if (W1 >= 1 && W1 < Wsmall && T <= W1 * kOneLevelTilesPerWarp) Wsmall = W1;
+        }
+        if (Wsmall < W) {
             // a small batch: fewer, longer warp ranges (every split is a partial
             // to merge), spread over the SMs by numbering warps across CTAs
-            W = (T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
+            W = Wsmall;
             wid = (uint64_t)warp * gridDim.x + blockIdx.x;
         }
         // this warp's virtual range [v0, v1)
