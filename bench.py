@@ -843,14 +843,23 @@ def run_gemv(args) -> int:
             tel = _lib.init(_lib.Telemetry())
             per = []
             n = 10 if wb.size > 50e6 else 60
-            for i in range(n + 3):
+            for i in range(3):
+                assert L.qwn_cuda_abi_hypervsq2_gemm(C.byref(ctx), C.byref(rq), C.byref(tel)) == 0
+            # at least n calls and --soak-ms of them, with the clocks sampled meanwhile
+            clocks = ClockSampler(0)
+            clocks.start()
+            time.sleep(0.3)
+            w0 = time.perf_counter()
+            while len(per) < n or time.perf_counter() - w0 < args.soak_ms / 1000.0:
                 before = tel.gpu_kernel_ms
                 assert L.qwn_cuda_abi_hypervsq2_gemm(C.byref(ctx), C.byref(rq), C.byref(tel)) == 0
-                if i >= 3:
-                    per.append(tel.gpu_kernel_ms - before)
+                per.append(tel.gpu_kernel_ms - before)
+            w1 = time.perf_counter()
+            clocks.stop()
             us = 1000.0 * float(np.median(per))
             moved = wb.size + act.size + 4 * out.size
-            line[name] = {"kernel_us": us, "gbs": moved / (us * 1e-6) / 1e9}
+            line[name] = {"kernel_us": us, "gbs": moved / (us * 1e-6) / 1e9, "calls": len(per),
+                          "clocks": clocks.summary(w0, w1)}
             outs[name] = out.copy()
             L.qwn_cuda_abi_release_tensor(C.byref(ctx), C.byref(th))
             L.qwn_cuda_abi_context_destroy(C.byref(ctx))
@@ -927,21 +936,34 @@ def run_abi_kv(args) -> int:
             assert L.qwn_cuda_abi_kv_cache_append(C.byref(ctx), C.byref(ap), C.byref(tel)) == 0
         k0 = tel.kv_cache_kernel_ms
         res = np.zeros((steps, H * HD), np.float32)
+        # the 256 steps are timed as rounds until --soak-ms have passed (at
+        # least one round): every round re-appends tokens T0.. with the same
+        # rows, so each round computes the same outputs, and the clock
+        # samples fall inside the timed region
+        clocks = ClockSampler(0)
+        clocks.start()
+        time.sleep(0.3)
+        rounds = 0
         t0 = time.perf_counter()
-        for i in range(steps):
-            t = T0 + i
-            ap.host_key = keys[t].ctypes.data_as(P(C.c_float))
-            ap.host_value = vals[t].ctypes.data_as(P(C.c_float))
-            ap.token = t
-            assert L.qwn_cuda_abi_kv_cache_append(C.byref(ctx), C.byref(ap), C.byref(tel)) == 0
-            at.host_query = qs[i].ctypes.data_as(P(C.c_float))
-            at.position = t
-            assert L.qwn_cuda_abi_kv_cache_attention(C.byref(ctx), C.byref(at), C.byref(tel)) == 0
-            res[i] = out
-        wall = (time.perf_counter() - t0) / steps
+        while rounds == 0 or time.perf_counter() - t0 < args.soak_ms / 1000.0:
+            for i in range(steps):
+                t = T0 + i
+                ap.host_key = keys[t].ctypes.data_as(P(C.c_float))
+                ap.host_value = vals[t].ctypes.data_as(P(C.c_float))
+                ap.token = t
+                assert L.qwn_cuda_abi_kv_cache_append(C.byref(ctx), C.byref(ap), C.byref(tel)) == 0
+                at.host_query = qs[i].ctypes.data_as(P(C.c_float))
+                at.position = t
+                assert L.qwn_cuda_abi_kv_cache_attention(C.byref(ctx), C.byref(at), C.byref(tel)) == 0
+                res[i] = out
+            rounds += 1
+        t1 = time.perf_counter()
+        clocks.stop()
+        wall = (t1 - t0) / (steps * rounds)
         line[name] = {"steps_per_s": 1.0 / wall, "wall_us_per_step": wall * 1e6,
-                      "kernel_us_per_step": (tel.kv_cache_kernel_ms - k0) * 1000.0 / steps,
-                      "kernel_type": tel.kv_cache_kernel_type.decode(errors="replace")}
+                      "kernel_us_per_step": (tel.kv_cache_kernel_ms - k0) * 1000.0 / (steps * rounds),
+                      "kernel_type": tel.kv_cache_kernel_type.decode(errors="replace"), "rounds": rounds,
+                      "clocks": clocks.summary(t0, t1)}
         outs[name] = res
         L.qwn_cuda_abi_kv_cache_destroy(C.byref(ctx), C.byref(cache))
         L.qwn_cuda_abi_context_destroy(C.byref(ctx))
@@ -990,6 +1012,14 @@ def run_linear(args) -> int:
         torch.cuda.synchronize()
         n = steps if T == 1 else max(3, steps // 4)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        # a probe sizes the timed loop so that it lasts at least --soak-ms:
+        # the clock samples (every 100 ms) then fall inside the timed region
+        ev[0].record()
+        for i in range(n):
+            st.prefill(q[i % ring], k[i % ring], v[i % ring], decay, T, o[i % ring])
+        ev[1].record()
+        torch.cuda.synchronize()
+        n = max(n, int(args.soak_ms / max(ev[0].elapsed_time(ev[1]) / n, 1e-3)) + 1)
         clocks = ClockSampler(0)
         clocks.start()
         time.sleep(0.3)
