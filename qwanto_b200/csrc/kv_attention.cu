@@ -50,6 +50,10 @@ constexpr uint32_t kMergeGroup = 16;
 // then merges in one level -- as long as a warp streams at most this many
 // tiles: a second merge level costs more than streaming these serially
 constexpr uint64_t kOneLevelTilesPerWarp = 24;
+// ... namely at most this many warp ranges start inside the longest segment:
+// with the CTA-level merge (four interior warps count as one part) that
+// keeps a segment within kMergeGroup parts
+constexpr uint64_t kOneLevelWarps = 32;
 constexpr float kNuFloor = 7.888609052210118e-31f;  // 2^-100
 constexpr float kNuHeadroom = 16384.0f;            // rescale only when a scale exceeds nu * 2^14
 
@@ -122,8 +126,8 @@ template <int CODEC, int HG>
 struct Int8T {
     static constexpr bool kB64 = CODEC == QWN_KV_CODEC_Q8_B64_F32;
     static constexpr int kX = kB64 ? 2 : 1;  // scale groups along head_dim
-    // two head groups keep twice the state: 2 CTAs per SM, deeper pipelines
-    static constexpr int kBytes = kB64 ? 4352 : 4160, kStages = HG == 1 ? 4 : 6;
+    // every variant fits 3 CTAs per SM (168 registers; two head groups too)
+    static constexpr int kBytes = kB64 ? 4352 : 4160, kStages = 4;
     static constexpr int kTilesPerStep = 1;
     // QK^T n-blocks: columns (head, slice), three query slices per head.
     // C column e (0, 1) of n-block nb held by a lane belongs to head group
@@ -511,7 +515,7 @@ struct LowBitT {
     static constexpr bool kTQ = CODEC == QWN_KV_CODEC_TQ35_G64;
     static constexpr int kC = 4;               // classes of 32 dims
     static constexpr int kG = kTQ ? 2 : 4;     // groups (min values)
-    static constexpr int kBytes = kTQ ? 2048 : 2560, kStages = HG == 1 ? (kTQ ? 8 : 6) : (kTQ ? 12 : 9);
+    static constexpr int kBytes = kTQ ? 2048 : 2560, kStages = kTQ ? 8 : 6;
     // tiles per loop iteration: pairs for the 4-bit single-head-group kernel
     // (long contexts gain ~3%; TurboQuant's larger step does not)
     static constexpr int kTilesPerStep = (HG == 1 && !kTQ) ? 2 : 1;
@@ -1019,7 +1023,7 @@ struct LowBitT {
 // ---------------------------------------------------------------------------
 template <int HG>
 struct F16T {
-    static constexpr int kBytes = 8192, kStages = HG == 1 ? 2 : 3;
+    static constexpr int kBytes = 8192, kStages = 2;
     static constexpr int kTilesPerStep = 1;
     struct Frag {
         uint32_t b[HG][8][2];  // B: [head group][k-block of 16 dims][reg]
@@ -1449,6 +1453,51 @@ __device__ __noinline__ void fused_append(const float *new_k, const float *new_v
 // and l[G]; one bulk copy of slot_bytes(G) moves it.
 __device__ __forceinline__ uint32_t slot_bytes(uint32_t G) { return (G * (kHeadDim + 2) * 4 + 15u) & ~15u; }
 
+// The parts of a segment: the warps wa..wb whose ranges meet its tiles
+// (warp of virtual unit u is ((u+1)W-1)/T, T the virtual total; the kernel
+// caps W so that every warp range holds real units), except that the four
+// warps of an "interior" CTA -- all of them strictly between wa and wb, so
+// their ranges hold this segment's tiles and nothing else -- merge in shared
+// memory first and count as one part.  Warps are numbered CTA by CTA (warp w
+// is warp w % 4 of CTA w / 4).  Part order: the warps before the first
+// interior CTA, the interior CTAs, the warps after; the slot of a part is
+// the one of its (first) warp.
+struct Parts {
+    uint64_t wa, c0;          // first warp; first interior CTA
+    uint32_t pre, ncta, n;    // parts before the interior CTAs; interior CTAs; all parts
+};
+__device__ __forceinline__ Parts parts_of(uint64_t Us, uint64_t ns, uint64_t T, uint64_t W) {
+    Parts P;
+    P.wa = warp_of_unit(Us + kVirtualUnits, T, W);
+    const uint64_t wb = warp_of_unit(Us + kVirtualUnits + ns - 1, T, W);
+    P.c0 = P.wa / kWarpsPerCta + 1;
+    const uint64_t c_end = wb / kWarpsPerCta;  // CTAs c < c_end have 4c + 3 < wb
+    P.ncta = c_end > P.c0 ? (uint32_t)(c_end - P.c0) : 0u;
+    if (P.ncta == 0) {
+        P.pre = P.n = (uint32_t)(wb - P.wa + 1);
+    } else {
+        P.pre = (uint32_t)(kWarpsPerCta * P.c0 - P.wa);
+        P.n = P.pre + P.ncta + (uint32_t)(wb - kWarpsPerCta * c_end + 1);
+    }
+    return P;
+}
+// the warp whose slot holds part i
+__device__ __forceinline__ uint64_t part_warp(const Parts &P, uint32_t i) {
+    if (i < P.pre) return P.wa + i;
+    if (i < P.pre + P.ncta) return kWarpsPerCta * (P.c0 + (i - P.pre));
+    return kWarpsPerCta * (P.c0 + P.ncta) + (i - P.pre - P.ncta);
+}
+__device__ __forceinline__ bool interior_warp(const Parts &P, uint64_t w) {
+    return P.ncta != 0 && w >= kWarpsPerCta * P.c0 && w < kWarpsPerCta * (P.c0 + P.ncta);
+}
+// part index of warp w (for an interior warp: of its CTA)
+__device__ __forceinline__ uint32_t part_index(const Parts &P, uint64_t w) {
+    if (w < P.wa + P.pre) return (uint32_t)(w - P.wa);
+    const uint64_t cend = kWarpsPerCta * (P.c0 + P.ncta);
+    if (w < cend) return P.pre + (uint32_t)(w / kWarpsPerCta - P.c0);
+    return P.pre + P.ncta + (uint32_t)(w - cend);
+}
+
 // ---------------------------------------------------------------------------
 // split-KV exchange between ranks (peer memory over NVLink)
 // ---------------------------------------------------------------------------
@@ -1577,23 +1626,23 @@ __device__ __forceinline__ void exchange_merge(const AttnArgs &A, uint32_t s_idx
     }
 }
 
-// Merge the nparts partial slots of segment s_idx into its output rows
-// (row0 = s_idx * G).  The slots were written by other warps, so each read is
-// an L2 round trip made while DRAM is saturated by the streaming warps; the
-// merging warp therefore pulls up to `cap` whole slots into its idle pipeline
-// stages (buf, SB bytes) with bulk copies completed on one mbarrier -- one
-// round trip per chunk -- and combines them from shared memory.  GG >= G is
-// the compile-time row count.  Returns false when the wait gave up.
+// merge_small: the merge of a segment (or group) whose parts all fit in one
+// warp's stage memory, so that every merger -- a lone warp or a CTA's -- does
+// it in one round with the same arithmetic.  The merging warp pulls the
+// nparts slots (written by other warps) into shared memory (buf, SB bytes)
+// with bulk copies completed on one mbarrier and combines them there, its
+// rows unrolled: GG >= G is the compile-time row count.  Output as for
+// merge_chunked.  Returns false when the wait gave up.
 template <int GG, bool XCHG>
-__device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, uint64_t base_w, uint32_t stride_w,
-                                           uint32_t nparts, float *dst_slot, uint8_t *buf, uint32_t SB,
-                                           uint64_t *bar, uint32_t &par) {
+__device__ __forceinline__ bool merge_small(const AttnArgs &A, uint32_t s_idx, const Parts &P, uint32_t first,
+                                           uint32_t stride, uint32_t nparts, float *dst_slot, uint8_t *buf,
+                                           uint32_t SB, uint64_t *bar, uint32_t &par) {
     const int lane = threadIdx.x & 31;
     const uint32_t G = A.group;
     const uint32_t PB = slot_bytes(G), rowf = G * kHeadDim;
     const uint32_t cap = SB / PB < 32u ? SB / PB : 32u;
     auto slot_of = [&](uint32_t pp) -> const float * {
-        return A.partials + (size_t)(base_w + (uint64_t)pp * stride_w + s_idx) * kPartialFloats;
+        return A.partials + (size_t)(part_warp(P, first + pp * stride) + s_idx) * kPartialFloats;
     };
     // the slots were written by generic stores of other warps (ordered by the
     // acquire on the segment counter); the bulk copies read them through the
@@ -1687,31 +1736,222 @@ __device__ __forceinline__ bool merge_rows(const AttnArgs &A, uint32_t s_idx, ui
     return true;
 }
 
+// one round of slot copies: parts i0 .. i0+nq-1 into cbuf, PB bytes apart,
+// completed on bar; false (status latched) when the wait gave up
+template <class SlotOf>
+__device__ __forceinline__ bool copy_round(const AttnArgs &A, uint8_t *cbuf, uint32_t PB, uint32_t i0, uint32_t nq,
+                                           const SlotOf &slot_of, uint64_t *bar, uint32_t &par) {
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) mbar_expect_tx(bar, nq * PB);
+    __syncwarp();
+    if ((uint32_t)lane < nq) bulk_g2s(cbuf + lane * PB, slot_of(i0 + lane), PB, bar);
+    if (!mbar_wait_bounded(bar, par)) {
+        if (lane == 0) latch(A.status, QWN_KV_STATUS_WAIT_TIMEOUT);
+        mbar_wait_bounded(bar, par);  // the copies into buf must land before the warp leaves
+        return false;
+    }
+    par ^= 1u;
+    return true;
+}
+
+// merge_chunked: merge nparts partial slots of segment s_idx -- part i of the map P at slot
+// part_warp(P, first + i * stride) + s_idx -- into the segment's output rows
+// (row0 = s_idx * G), or, given dst_slot, into one unnormalised partial
+// there.  Returns false when a wait gave up.
+//
+// The arithmetic depends on the part order only, so every launch gives the
+// same bits whichever warp merges and however much shared memory it has:
+// the parts are taken in logical chunks of 32 (lane q <-> part q), each
+// chunk's (m, l) read straight from L2 into a table, the chunk maximum,
+// weights and sum of l per row computed from the table, the running o rows
+// rescaled once per chunk, and then the o rows of the chunk's parts added in
+// part order.  Those rows arrive by bulk copies into shared memory, as many
+// slots per round trip as the buffer holds (a CTA's merger has four warps'
+// stages, a lone warp its own).  Rows are handled in loops that are not
+// unrolled: a merge runs once per segment at the end of a launch with its
+// instructions fetched cold, so its code is kept short.
+//
+// buf layout: o[G][128] running rows, M[8], L[8], alpha[8], then per (row,
+// part) the tables m, l, w (rows kTStride floats apart, so that lanes reading
+// different rows hit different banks), then the copied slots.
 template <bool XCHG>
-__device__ __forceinline__ bool merge_parts(const AttnArgs &A, uint32_t s_idx, uint64_t base_w, uint32_t stride_w,
-                                            uint32_t nparts, float *dst_slot, uint8_t *buf, uint32_t SB,
-                                            uint64_t *bar, uint32_t &par) {
-    if (A.group <= 2) return merge_rows<2, XCHG>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
-    if (A.group <= 4) return merge_rows<4, XCHG>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
-    return merge_rows<8, XCHG>(A, s_idx, base_w, stride_w, nparts, dst_slot, buf, SB, bar, par);
+__device__ __forceinline__ bool merge_chunked(const AttnArgs &A, uint32_t s_idx, const Parts &P, uint32_t first,
+                                              uint32_t stride, uint32_t nparts, float *dst_slot, uint8_t *buf,
+                                              uint32_t SB, uint64_t *bar, uint32_t &par) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t G = A.group;
+    const uint32_t PB = slot_bytes(G), rowf = G * kHeadDim;
+    float *run = reinterpret_cast<float *>(buf);
+    constexpr uint32_t kTStride = 33;
+    float *Mr = run + kMaxGroup * kHeadDim, *Lr = Mr + kMaxGroup, *Ar = Lr + kMaxGroup;
+    float *Tm = Ar + kMaxGroup, *Tl = Tm + kMaxGroup * kTStride, *Tw = Tl + kMaxGroup * kTStride;
+    uint8_t *cbuf = buf + ((reinterpret_cast<uint8_t *>(Tw + kMaxGroup * kTStride) - buf + 15) & ~(ptrdiff_t)15);
+    const uint32_t hdr = (uint32_t)(cbuf - buf);
+    uint32_t cap = (SB - hdr) / PB;
+    if (cap > 32u) cap = 32u;
+    const size_t row0 = (size_t)s_idx * G;
+    auto slot_of = [&](uint32_t i) -> const float * {
+        return A.partials + (size_t)(part_warp(P, first + i * stride) + s_idx) * kPartialFloats;
+    };
+    // the slots were written by generic stores of other warps (ordered by the
+    // acquire on the segment counter); the bulk copies read them through the
+    // async proxy
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    for (uint32_t lc = 0; lc < nparts; lc += 32) {
+        const uint32_t nl = nparts - lc < 32u ? nparts - lc : 32u;
+        // a chunk that fits the buffer is copied in one round, before its
+        // (m, l) are needed; otherwise the copies go round by round below
+        const bool one_round = nl <= cap;
+        if (one_round && !copy_round(A, cbuf, PB, lc, nl, slot_of, bar, par)) return false;
+        // (m, l) of the chunk's parts: lane q takes part lc + q's rows, from
+        // its copy or straight from L2
+        {
+            float mq[kMaxGroup], lq[kMaxGroup];
+            const float *sl = (uint32_t)lane >= nl ? nullptr
+                              : one_round ? reinterpret_cast<const float *>(cbuf + lane * PB) + rowf
+                                          : slot_of(lc + lane) + rowf;
+#pragma unroll
+            for (int g = 0; g < kMaxGroup; g++) {
+                mq[g] = sl && (uint32_t)g < G ? (one_round ? sl[g] : __ldcg(sl + g)) : -INFINITY;
+                lq[g] = sl && (uint32_t)g < G ? (one_round ? sl[G + g] : __ldcg(sl + G + g)) : 0.f;
+            }
+#pragma unroll
+            for (int g = 0; g < kMaxGroup; g++) {
+                Tm[g * kTStride + lane] = mq[g];
+                Tl[g * kTStride + lane] = lq[g];
+            }
+        }
+        __syncwarp();
+        // per row (lane g): the chunk maximum, the parts' weights and their sum of l
+        if ((uint32_t)lane < G) {
+            const uint32_t g = lane;
+            float cm = -INFINITY;
+            for (uint32_t q = 0; q < nl; q++) cm = fmaxf(cm, Tm[g * kTStride + q]);
+            const float m_old = lc == 0 ? -INFINITY : Mr[g];
+            const float nm = fmaxf(m_old, cm);
+            float ls = 0.f;
+#pragma unroll 4
+            for (uint32_t q = 0; q < nl; q++) {
+                const float mq = Tm[g * kTStride + q];
+                const float wq = mq == -INFINITY ? 0.f : ex2(mq - nm);
+                Tw[g * kTStride + q] = wq;
+                ls = fmaf(Tl[g * kTStride + q], wq, ls);
+            }
+            const float alpha = m_old == -INFINITY ? 0.f : ex2(m_old - nm);
+            Lr[g] = lc == 0 ? ls : fmaf(Lr[g], alpha, ls);
+            Mr[g] = nm;
+            Ar[g] = alpha;
+        }
+        __syncwarp();
+        // the running rows, rescaled to the new maxima (zero before the first chunk)
+#pragma unroll 1
+        for (uint32_t g = 0; g < G; g++) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (lc != 0) {
+                const float alpha = Ar[g];
+                acc = reinterpret_cast<const float4 *>(run + g * kHeadDim)[lane];
+                acc.x *= alpha; acc.y *= alpha; acc.z *= alpha; acc.w *= alpha;
+            }
+            reinterpret_cast<float4 *>(run + g * kHeadDim)[lane] = acc;
+        }
+        // the chunk's o rows, weighted, in part order
+        for (uint32_t pc = 0; pc < nl; pc += cap) {
+            const uint32_t nq = nl - pc < cap ? nl - pc : cap;
+            __syncwarp();  // every lane is done with the previous round's slots
+            if (!one_round && !copy_round(A, cbuf, PB, lc + pc, nq, slot_of, bar, par)) return false;
+#pragma unroll 1
+            for (uint32_t g = 0; g < G; g++) {
+                float4 acc = reinterpret_cast<const float4 *>(run + g * kHeadDim)[lane];
+                const uint8_t *vq = cbuf + g * (kHeadDim * 4) + lane * 16;
+                const float *wg = Tw + g * kTStride + pc;
+#pragma unroll 4
+                for (uint32_t q = 0; q < nq; q++) {
+                    const float w = wg[q];
+                    const float4 v = *reinterpret_cast<const float4 *>(vq + q * PB);
+                    acc.x = fmaf(v.x, w, acc.x); acc.y = fmaf(v.y, w, acc.y);
+                    acc.z = fmaf(v.z, w, acc.z); acc.w = fmaf(v.w, w, acc.w);
+                }
+                reinterpret_cast<float4 *>(run + g * kHeadDim)[lane] = acc;
+            }
+        }
+        __syncwarp();
+    }
+    // the merged rows to their destination
+#pragma unroll 1
+    for (uint32_t g = 0; g < G; g++) {
+        const float4 acc = reinterpret_cast<const float4 *>(run + g * kHeadDim)[lane];
+        const float nm = Mr[g], ls = Lr[g];
+        const size_t row = row0 + g;
+        if (dst_slot) {  // a merged group, stored as one unnormalised partial
+            reinterpret_cast<float4 *>(dst_slot + g * kHeadDim)[lane] = acc;
+            if (lane == 0) { dst_slot[rowf + g] = nm; dst_slot[rowf + G + g] = ls; }
+            continue;
+        }
+        if constexpr (XCHG) {
+            for (uint32_t r = 0; r < A.xworld; r++) {
+                float *blk = xblock(A.xbuf[r], A.xepoch & 1u, A.xrank, A.xrows);
+                reinterpret_cast<float4 *>(blk + row * kHeadDim)[lane] = acc;
+                if (lane == 0) {
+                    blk[(size_t)A.xrows * kHeadDim + row] = nm;
+                    blk[(size_t)A.xrows * (kHeadDim + 1) + row] = ls;
+                }
+            }
+        } else if (A.part_o) {
+            reinterpret_cast<float4 *>(A.part_o + row * kHeadDim)[lane] = acc;
+            if (lane == 0) { A.part_m[row] = nm; A.part_l[row] = ls; }
+        } else {
+            const float inv = ls > 0.f ? 1.0f / ls : 0.f;
+            reinterpret_cast<float4 *>(A.output + row * kHeadDim)[lane] =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        }
+        if (A.seg_ml && lane == 0) A.seg_ml[(size_t)s_idx * kMaxGroup + g] = make_float2(nm, ls);
+    }
+    __syncwarp();  // buf is free again when the warp goes on
+    if constexpr (XCHG) {
+        if (!dst_slot) exchange_merge(A, s_idx, row0);
+    }
+    return true;
+}
+
+
+// The merge of a segment's (or group's) parts.  In the one-head-group
+// kernels (G <= 4), parts that fit in one warp's stage memory (warp_sb
+// bytes) are merged in one round by merge_small, whatever warp merges;
+// larger merges, and every merge of the two-head-group kernels (where the
+// unrolled rows cost more than they save), take merge_chunked.  The choice
+// depends on the kernel and the part count only, so the result bits never
+// depend on which warp merges.
+template <int HG, bool XCHG>
+__device__ __forceinline__ bool merge_parts(const AttnArgs &A, uint32_t s_idx, const Parts &P, uint32_t first,
+                                            uint32_t stride, uint32_t nparts, float *dst_slot, uint8_t *buf,
+                                            uint32_t SB, uint32_t warp_sb, uint64_t *bar, uint32_t &par) {
+    if constexpr (HG == 1) {
+        if (nparts * slot_bytes(A.group) <= warp_sb) {
+            if (A.group <= 2)
+                return merge_small<2, XCHG>(A, s_idx, P, first, stride, nparts, dst_slot, buf, SB, bar, par);
+            return merge_small<4, XCHG>(A, s_idx, P, first, stride, nparts, dst_slot, buf, SB, bar, par);
+        }
+    }
+    return merge_chunked<XCHG>(A, s_idx, P, first, stride, nparts, dst_slot, buf, SB, bar, par);
 }
 
 // End of a warp's share of segment s_idx (first unit Us, ns units).  A warp
-// that saw the whole segment writes the output and returns 0.  Otherwise it
-// writes its partial (m, l, o) to slot wid + s_idx and returns the number of
-// parts.  The warp counts itself on the segment's counter only after its
-// streaming loop (a release there waits for the slot stores to reach L2, a
-// round trip the loop should not take mid-stream); the warp that draws
-// nparts-1 merges, also after its loop.
+// that saw the whole segment writes the output and returns 0.  A warp of an
+// interior CTA (parts_of) writes its partial (m, l, o) into its own stage
+// memory, sets in_cta and returns the number of parts; any other warp writes
+// it to slot wid + s_idx and returns the number of parts.  The warp counts
+// itself on the segment's counter only after its streaming loop (a release
+// there waits for the slot stores to reach L2, a round trip the loop should
+// not take mid-stream); the warp that draws nparts-1 merges, also after its
+// loop.
 template <class OPS, bool XCHG>
 __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const typename OPS::State &st, uint32_t s_idx,
-                                                   uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid) {
-    // warps whose range meets the segment's tiles (virtual units Us+V ..
-    // Us+V+ns-1): warp of virtual unit u is ((u+1)W-1)/T, T the virtual total;
-    // the kernel caps W so that every warp range holds real units
-    const uint64_t wa = warp_of_unit(Us + kVirtualUnits, T, W), wb = warp_of_unit(Us + kVirtualUnits + ns - 1, T, W);
-    const uint32_t nparts = (uint32_t)(wb - wa + 1);
+                                                   uint64_t Us, uint64_t ns, uint64_t T, uint64_t W, uint64_t wid,
+                                                   uint8_t *wsm, bool &in_cta) {
+    const Parts P = parts_of(Us, ns, T, W);
+    const uint32_t nparts = P.n;
     const size_t row0 = (size_t)s_idx * A.group;
+    in_cta = false;
     // split-KV over ranks: a whole segment is a partial too (its slot is
     // published to the ranks after the streaming loop)
     if (nparts == 1 && !XCHG) {
@@ -1723,24 +1963,59 @@ __device__ __forceinline__ uint32_t finish_segment(const AttnArgs &A, const type
         return 0;
     }
     float *slot = A.partials + (size_t)(wid + s_idx) * kPartialFloats;
+    if (interior_warp(P, wid)) {  // the CTA merges its four warps first, in shared memory
+        slot = reinterpret_cast<float *>(wsm);
+        in_cta = true;
+    }
     OPS::store_rows(A, st, slot, slot + A.group * kHeadDim, slot + A.group * (kHeadDim + 1), false, nullptr);
     return nparts;
 }
 
-// counter a part of segment s_idx (nparts parts, first unit Us) counts on:
-// the segment's when it merges in one level, else its merge group's
-__device__ __forceinline__ uint32_t *part_counter(const AttnArgs &A, uint32_t s_idx, uint32_t nparts, uint64_t Us,
-                                                  uint64_t T, uint64_t W, uint64_t wid) {
-    if (nparts <= kMergeGroup) return &A.counters[s_idx];
-    const uint64_t wa = warp_of_unit(Us + kVirtualUnits, T, W);
-    return &A.gcounters[wa + ((wid - wa) / kMergeGroup) * kMergeGroup + s_idx];
+// counter a part (index idx of P.n) of segment s_idx counts on: the
+// segment's when it merges in one level, else its merge group's (kept at the
+// slot index of the group's first part)
+__device__ __forceinline__ uint32_t *part_counter(const AttnArgs &A, uint32_t s_idx, const Parts &P, uint32_t idx) {
+    if (P.n <= kMergeGroup) return &A.counters[s_idx];
+    return &A.gcounters[part_warp(P, (idx / kMergeGroup) * kMergeGroup) + s_idx];
+}
+
+// The four warps of a CTA whose ranges lie inside one segment merged their
+// states into their own stage memory (a slot at the start of each warp's
+// stages, `stride` bytes apart); the last of them to arrive combines the four
+// in warp order into the CTA's partial slot `dst` (unnormalised o, m, l).
+__device__ __forceinline__ void merge_cta_slots(const AttnArgs &A, const uint8_t *base, uint32_t stride, float *dst) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t G = A.group, rowf = G * kHeadDim;
+#pragma unroll 1
+    for (uint32_t g = 0; g < G; g++) {  // not unrolled: cold code, kept short
+        float m[kWarpsPerCta], l[kWarpsPerCta], M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarpsPerCta; w++) {
+            const float *sl = reinterpret_cast<const float *>(base + w * stride);
+            m[w] = sl[rowf + g];
+            l[w] = sl[rowf + G + g];
+            M = fmaxf(M, m[w]);
+        }
+        float ls = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < kWarpsPerCta; w++) {
+            const float wt = m[w] == -INFINITY ? 0.f : ex2(m[w] - M);
+            const float4 v = reinterpret_cast<const float4 *>(base + w * stride)[g * (kHeadDim / 4) + lane];
+            ls = fmaf(l[w], wt, ls);
+            acc.x = fmaf(v.x, wt, acc.x); acc.y = fmaf(v.y, wt, acc.y);
+            acc.z = fmaf(v.z, wt, acc.z); acc.w = fmaf(v.w, wt, acc.w);
+        }
+        reinterpret_cast<float4 *>(dst + g * kHeadDim)[lane] = acc;
+        if (lane == 0) { dst[rowf + g] = M; dst[rowf + G + g] = ls; }
+    }
 }
 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 template <int CODEC, int HG, bool XCHG>
-__global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kernel(const AttnArgs A) {
+__global__ void __launch_bounds__(kWarpsPerCta * 32, 3) attn_kernel(const AttnArgs A) {
     using OPS = Ops<CODEC, HG>;
     constexpr int S = OPS::kStages, B = OPS::kBytes;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1782,7 +2057,10 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         pw0 = plan[lane]; pw1 = plan[32 + lane]; pw2 = plan[64 + lane]; pw3 = plan[96 + lane];
         epoch = A.plans[0];
     }
-    fill_len_cache(A);
+    // arrivals of the CTA's warps at the shared-memory merge (interior CTAs)
+    __shared__ uint32_t cta_arrivals;
+    if (threadIdx.x == 0) cta_arrivals = 0u;
+    fill_len_cache(A);  // (its CTA barrier also publishes cta_arrivals)
     const uint32_t key = lane == 0 ? epoch : lane == 1 ? A.num_seqs : lane == 2 ? A.attend_limit
                        : lane == 3 ? A.t_begin : lane == 4 ? A.t_end : lane == 5 ? (A.new_k ? 1u : 0u)
                        : lane == 6 ? gridDim.x : 0x504C414Eu;
@@ -1837,15 +2115,12 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
             Wsmall = (T + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
         if (T != 0) {
             // at most kMergeGroup - 1 warp ranges start inside the longest segment
-            const uint64_t W1 = (uint64_t)(kMergeGroup - 1) * Tv / seg_v;
+            const uint64_t W1 = (uint64_t)kOneLevelWarps * Tv / seg_v;
             if (W1 >= 1 && W1 < Wsmall && T <= W1 * kOneLevelTilesPerWarp) Wsmall = W1;
         }
-        if (Wsmall < W) {
-            // a small batch: fewer, longer warp ranges (every split is a partial
-            // to merge), spread over the SMs by numbering warps across CTAs
-            W = Wsmall;
-            wid = (uint64_t)warp * gridDim.x + blockIdx.x;
-        }
+        // a small batch: fewer, longer warp ranges (every split is a partial
+        // to merge); the first W / 4 CTAs run (the others leave at once)
+        if (Wsmall < W) W = Wsmall;
         // this warp's virtual range [v0, v1)
         const uint64_t v0 = muldiv_floor(wid, Tv, W), v1 = muldiv_floor(wid + 1, Tv, W);
         if (T != 0 && wid < W && v0 < v1) {
@@ -1943,7 +2218,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     // partials this warp wrote (at most two); the first is counted on its
     // segment a few tiles after it was written (its stores have landed by then,
     // so the release costs nothing), the last after the loop
-    uint32_t pend_n = 0, pend_s0 = 0, pend_n0 = 0, pend_s1 = 0, pend_n1 = 0, pend_k0 = 0, tk0 = 0;
+    uint32_t pend_n = 0, pend_s0 = 0, pend_s1 = 0, pend_k0 = 0, tk0 = 0;
+    uint32_t pend_ns0 = 0, pend_ns1 = 0;  // the pending segments' tile counts
+    bool pend_cta = false;                // the (only) partial waits in shared memory for the CTA merge
     uint64_t xpend = 0;  // split-KV: segments this warp saw whole, to publish and merge after the loop
     bool counted0 = false;
     uint64_t pend_u0 = 0, pend_u1 = 0;
@@ -1955,7 +2232,10 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         const uint32_t nt = (OPS::kTilesPerStep == 2 && cons.tile + 1 < cons.geo.ntiles && k + 1 < n) ? 2u : 1u;
         if (pend_n && !counted0 && k >= pend_k0 + 4u) {
             __syncwarp();
-            if (lane == 0) tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, pend_n0, pend_u0, Tv, W, wid), 1u);
+            if (lane == 0) {
+                const Parts P0 = parts_of(pend_u0, pend_ns0, Tv, W);
+                tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, P0, part_index(P0, wid)), 1u);
+            }
             counted0 = true;  // the ticket is read after the loop
         }
         if (cons.tile + 4u <= cons.geo.ntiles && cons.geo.ntiles < cons.tile + 4u + nt) {
@@ -2033,12 +2313,18 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         if (cons.tile + nt == cons.geo.ntiles || k + nt == n) {
             dep_wait();  // its slot (or output rows) may still be read by the previous kernel
             const uint32_t s_idx = cons.i * HK + cons.h;
-            const uint32_t np = finish_segment<OPS, XCHG>(A, state, s_idx, cons.vbase, cons.geo.ntiles, Tv, W, wid);
+            bool in_cta = false;
+            const uint32_t np =
+                finish_segment<OPS, XCHG>(A, state, s_idx, cons.vbase, cons.geo.ntiles, Tv, W, wid, wsm, in_cta);
             if (XCHG && np == 1) xpend |= 1ull << s_idx;
             else if (np) {
                 const int e = pend_n++;  // at most two: the segment the range starts in and the one it ends in
-                if (e == 0) { pend_s0 = s_idx; pend_n0 = np; pend_u0 = cons.vbase; pend_k0 = k; }
-                else { pend_s1 = s_idx; pend_n1 = np; pend_u1 = cons.vbase; }
+                if (e == 0) {
+                    pend_s0 = s_idx; pend_u0 = cons.vbase; pend_k0 = k; pend_ns0 = cons.geo.ntiles;
+                    pend_cta = in_cta;  // an interior warp has this one partial only, at its last unit
+                } else {
+                    pend_s1 = s_idx; pend_u1 = cons.vbase; pend_ns1 = cons.geo.ntiles;
+                }
             }
         }
         // next unit
@@ -2050,15 +2336,43 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
     }
     // the pipeline is drained: its stages hold the partials being merged,
     // completed on the next barrier in the ring
+    __syncwarp();
+    uint8_t *buf = wsm;  // where merges stage the slots they read
+    uint32_t SB = (uint32_t)(S * B);
+    // the CTA's part (all four warps inside one segment): the last of its
+    // warps to get here combines the four shared-memory slots into the
+    // CTA's slot and counts it; the others are done.  (No CTA barrier: a
+    // warp that gave up on a wait never arrives, and the segment's result is
+    // then marked invalid by the latched status.)
+    uint64_t pw = wid;  // the warp whose slot holds this warp's first part
+    if (pend_cta) {
+        uint32_t t = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            t = atomicAdd(&cta_arrivals, 1u);
+            __threadfence_block();
+        }
+        t = __shfl_sync(0xffffffffu, t, 0);
+        if (t != kWarpsPerCta - 1) return;
+        __syncwarp();
+        pw = wid - wid % kWarpsPerCta;
+        float *cslot = A.partials + (size_t)(pw + pend_s0) * kPartialFloats;
+        const uint32_t stride = (uint32_t)(S * B);
+        merge_cta_slots(A, smem, stride, cslot);
+        // every warp of the CTA is done: its whole stage memory serves the merges
+        buf = smem;
+        SB = (uint32_t)(kWarpsPerCta * S * B);
+        __syncwarp();
+    }
     // count this warp's partials on their segments: the warp barrier orders
     // the lanes' slot stores before lane 0's release, the acquire orders the
     // last arriver's reads of the other slots
-    __syncwarp();
+    const Parts P0 = parts_of(pend_u0, pend_ns0, Tv, W), P1 = parts_of(pend_u1, pend_ns1, Tv, W);
+    const uint32_t idx0 = pend_n > 0 ? part_index(P0, pw) : 0u, idx1 = pend_n > 1 ? part_index(P1, wid) : 0u;
     uint32_t tk1 = 0;
     if (lane == 0) {
-        if (pend_n > 0 && !counted0)
-            tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, pend_n0, pend_u0, Tv, W, wid), 1u);
-        if (pend_n > 1) tk1 = atom_add_acq_rel_gpu(part_counter(A, pend_s1, pend_n1, pend_u1, Tv, W, wid), 1u);
+        if (pend_n > 0 && !counted0) tk0 = atom_add_acq_rel_gpu(part_counter(A, pend_s0, P0, idx0), 1u);
+        if (pend_n > 1) tk1 = atom_add_acq_rel_gpu(part_counter(A, pend_s1, P1, idx1), 1u);
     }
     tk0 = __shfl_sync(0xffffffffu, tk0, 0);
     tk1 = __shfl_sync(0xffffffffu, tk1, 0);
@@ -2071,34 +2385,42 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, HG == 1 ? 3 : 2) attn_kerne
         }
     }
     for (uint32_t e = 0; e < pend_n; e++) {
-        const uint32_t np = e ? pend_n1 : pend_n0, s_idx = e ? pend_s1 : pend_s0;
-        const uint64_t wa = warp_of_unit((e ? pend_u1 : pend_u0) + kVirtualUnits, Tv, W);
+        const Parts &P = e ? P1 : P0;
+        const uint32_t np = P.n, s_idx = e ? pend_s1 : pend_s0, idx = e ? idx1 : idx0;
         const uint32_t tk = e ? tk1 : tk0;
-        uint8_t *buf = wsm;
-        const uint32_t SB = (uint32_t)(S * B);
-        if (np <= kMergeGroup) {
-            if (tk != np - 1) continue;  // not the last arrival
-            if (!merge_parts<XCHG>(A, s_idx, wa, 1, np, nullptr, buf, SB, &bars[st], par)) return;
-            if (lane == 0) A.counters[s_idx] = 0u;  // ready for the next launch
-            continue;
+        // the merge the last arrival runs: the whole segment (one level), or
+        // this part's group of kMergeGroup consecutive parts, whose result
+        // goes to the group's first slot and counts on the segment; the last
+        // group then merges the groups (one call site keeps the code short)
+        uint32_t mfirst = 0, mstride = 1, mn = np;
+        float *mdst = nullptr;
+        uint32_t *mctr = &A.counters[s_idx];
+        if (np > kMergeGroup) {
+            mfirst = (idx / kMergeGroup) * kMergeGroup;
+            mn = min(kMergeGroup, np - mfirst);
+            const uint64_t gw = part_warp(P, mfirst);
+            mdst = A.partials + (size_t)(gw + s_idx) * kPartialFloats;
+            mctr = &A.gcounters[gw + s_idx];
         }
-        // two levels: this warp's group of kMergeGroup consecutive parts
-        const uint64_t gbase = wa + ((wid - wa) / kMergeGroup) * kMergeGroup;
-        const uint32_t gsize = (uint32_t)min((uint64_t)kMergeGroup, wa + np - gbase);
-        if (tk != gsize - 1) continue;
-        float *gslot = A.partials + (size_t)(gbase + s_idx) * kPartialFloats;
-        if (!merge_parts<XCHG>(A, s_idx, gbase, 1, gsize, gslot, buf, SB, &bars[st], par)) return;
-        if (lane == 0) A.gcounters[gbase + s_idx] = 0u;
-        // publish the group result (in its first part's slot) and count it
-        __syncwarp();
-        uint32_t t2 = 0;
-        if (lane == 0) t2 = atom_add_acq_rel_gpu(&A.counters[s_idx], 1u);
-        t2 = __shfl_sync(0xffffffffu, t2, 0);
-        if (t2 != (np + kMergeGroup - 1) / kMergeGroup - 1) continue;
-        if (!merge_parts<XCHG>(A, s_idx, wa, kMergeGroup, (np + kMergeGroup - 1) / kMergeGroup, nullptr, buf, SB,
-                         &bars[st], par))
-            return;
-        if (lane == 0) A.counters[s_idx] = 0u;
+        if (tk != mn - 1) continue;  // not the last arrival
+        for (;;) {
+            if (!merge_parts<HG, XCHG>(A, s_idx, P, mfirst, mstride, mn, mdst, buf, SB, (uint32_t)(S * B),
+                                       &bars[st], par))
+                return;
+            if (lane == 0) *mctr = 0u;  // ready for the next launch
+            if (!mdst) break;
+            __syncwarp();
+            uint32_t t2 = 0;
+            if (lane == 0) t2 = atom_add_acq_rel_gpu(&A.counters[s_idx], 1u);
+            t2 = __shfl_sync(0xffffffffu, t2, 0);
+            const uint32_t ngroups = (np + kMergeGroup - 1) / kMergeGroup;
+            if (t2 != ngroups - 1) break;
+            mfirst = 0;
+            mstride = kMergeGroup;
+            mn = ngroups;
+            mdst = nullptr;
+            mctr = &A.counters[s_idx];
+        }
     }
 }
 

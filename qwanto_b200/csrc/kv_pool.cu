@@ -159,6 +159,10 @@ __global__ void __launch_bounds__(32) seq_append_kernel(uint32_t n, const int32_
                                                         int32_t *free_top, uint32_t P, uint32_t mp,
                                                         uint32_t max_seqs, uint32_t *status, uint32_t *epoch) {
     const int lane = threadIdx.x;
+    // the attention launch that follows (a programmatic dependent) may bring
+    // its CTAs up now; it waits for this kernel's completion before its first
+    // global access (the host never lets it start early after this kernel)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     int total = 0;
     uint32_t bad = 0;
     for (uint32_t base = 0; base < n; base += 32) {
@@ -271,6 +275,12 @@ cudaError_t launch_seq_append(Pool *p, uint32_t n, const int32_t *seq_ids, const
                               cudaStream_t s) {
     if (n == 0) return cudaSuccess;
     plans_invalidated(p);
+    {
+        // this kernel lets the next launch start its CTAs early, so the next
+        // attention launch must not read anything before its dependency wait
+        std::lock_guard<std::mutex> lk(p->last_mu);
+        p->last_attn.valid = false;
+    }
     seq_append_kernel<<<1, 32, 0, s>>>(n, seq_ids, counts, p->seq_lens, p->seq_pages, p->page_table,
                                          p->page_scores, p->free_stack, p->free_top, p->page_tokens,
                                          p->max_pages_per_seq, p->max_seqs, p->status, p->plans);
