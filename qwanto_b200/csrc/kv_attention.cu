@@ -2587,9 +2587,11 @@ cudaError_t launch_attention(Pool *p, const AttnLaunch &a, cudaStream_t s) {
     A.new_v = a.new_v;
     A.status = p->status;
     // Early start.  Every other kernel of this library is an ordinary launch
-    // (the next launch waits for it to finish), so this attention kernel can
-    // overlap only an attention kernel of the stream that precedes it
-    // directly.  That kernel writes its layer's newest-token tiles, its output
+    // (the next launch waits for it to finish) -- except seq_append_kernel,
+    // which lets the next launch start at once and therefore clears
+    // last_attn, so that the launch after it is never early -- so this
+    // attention kernel can overlap only an attention kernel of the stream that
+    // precedes it directly.  That kernel writes its layer's newest-token tiles, its output
     // rows, the pool's partial slots, counters and plans.  When the previous
     // attention launch of this pool on this stream was of another layer,
     // recorded no plans (the records this launch reads early), exported no
