@@ -980,7 +980,9 @@ def run_abi_kv(args) -> int:
         a, b = outs["ours"], outs["reference_gpu"]
         line["max_abs_diff"] = float(np.abs(a - b).max())
         line["speedup_wall"] = line["ours"]["steps_per_s"] / line["reference_gpu"]["steps_per_s"]
-        line["speedup_kernel"] = line["reference_gpu"]["kernel_us_per_step"] / max(line["ours"]["kernel_us_per_step"], 1e-9)
+        # (the reference library's telemetry may leave its kernel time at 0)
+        rk = line["reference_gpu"]["kernel_us_per_step"]
+        line["speedup_kernel"] = rk / max(line["ours"]["kernel_us_per_step"], 1e-9) if rk > 0 else None
     print(json.dumps(line), flush=True)
     return 0
 

@@ -280,9 +280,12 @@ typedef struct {
 QWN_CUDA_ABI_API int qwn_kv_evict(QwnKvPoolHandle *pool, const QwnKvEvictRequest *request);
 
 /* End-to-end decode step through host buffers (the plugin path with copies
- * inside): grows every sequence 0..num_seqs-1 by one token, copies each
- * layer's inputs host->device, runs qwn_kv_decode per layer and copies the
- * outputs back; returns after the last copy.  Host arrays are
+ * inside): grows every sequence 0..num_seqs-1 by one token, copies the
+ * layers' inputs host->device, runs qwn_kv_decode per layer and copies the
+ * outputs back; returns after the last copy.  The layers move in up to seven
+ * chunks (the first and the last layer alone): each chunk's layers launch
+ * back to back while the next chunk's inputs and the previous chunk's
+ * outputs are in flight on two copy streams.  Host arrays are
  * [layers][num_seqs][heads][128] fp32 (heads = query_heads for query/output,
  * kv_heads for key/value); pinned host memory gives overlapped copies. */
 typedef struct {

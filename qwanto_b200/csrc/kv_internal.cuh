@@ -54,7 +54,8 @@ struct Pool {
     uint64_t perm_seed = 0;
     size_t tile_bytes = 0, page_bytes = 0, pool_bytes = 0, scratch_bytes = 0;
     cudaStream_t stream = nullptr;      // default stream of the pool
-    cudaStream_t copy_stream = nullptr; // host-step copies
+    cudaStream_t copy_stream = nullptr; // host-step copies in
+    cudaStream_t out_stream = nullptr;  // host-step copies out (both copy directions at once)
     // device state
     uint8_t *pages = nullptr;
     int32_t *page_table = nullptr, *seq_lens = nullptr, *seq_pages = nullptr;
@@ -80,6 +81,8 @@ struct Pool {
     size_t stage_q_elems = 0, stage_kv_elems = 0;
     cudaEvent_t *layer_in_ev = nullptr, *layer_out_ev = nullptr;
     uint32_t layer_events = 0;
+    cudaEvent_t step_t0 = nullptr, step_t1 = nullptr;  // host-step timing (created on first use)
+    uint32_t *status_host = nullptr;                    // pinned copy of the status word for the host step
     std::mutex mu;
     // the pool's last attention launch, for the next launch's early start
     // (AttnArgs::early): its stream, layer and output range

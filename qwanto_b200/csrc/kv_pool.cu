@@ -382,6 +382,9 @@ static void pool_release(Pool *p) {
     cudaFree(p->partials); cudaFree(p->counters); cudaFree(p->plans); cudaFree(p->tile_mass); cudaFree(p->seg_ml);
     cudaFree(p->evict_dead); cudaFree(p->evict_count); cudaFree(p->ident);
     cudaFree(p->stage_q); cudaFree(p->stage_k); cudaFree(p->stage_v); cudaFree(p->stage_o);
+    if (p->status_host) cudaFreeHost(p->status_host);
+    if (p->step_t0) cudaEventDestroy(p->step_t0);
+    if (p->step_t1) cudaEventDestroy(p->step_t1);
     for (uint32_t i = 0; i < p->layer_events; i++) {
         cudaEventDestroy(p->layer_in_ev[i]);
         cudaEventDestroy(p->layer_out_ev[i]);
@@ -390,6 +393,7 @@ static void pool_release(Pool *p) {
     delete[] p->layer_out_ev;
     if (p->stream) cudaStreamDestroy(p->stream);
     if (p->copy_stream) cudaStreamDestroy(p->copy_stream);
+    if (p->out_stream) cudaStreamDestroy(p->out_stream);
     delete p;
 }
 
@@ -469,6 +473,7 @@ QWN_CUDA_ABI_API int qwn_kv_pool_create(const QwnKvPoolOptions *o, QwnKvPoolHand
     }
     bool ok = cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking) == cudaSuccess &&
               cudaStreamCreateWithFlags(&p->copy_stream, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&p->out_stream, cudaStreamNonBlocking) == cudaSuccess &&
               cudaMalloc(&p->pages, p->pool_bytes) == cudaSuccess &&
               cudaMalloc(&p->page_table, sizeof(int32_t) * table_elems) == cudaSuccess &&
               cudaMalloc(&p->seq_lens, sizeof(int32_t) * o->max_seqs) == cudaSuccess &&
@@ -876,57 +881,87 @@ QWN_CUDA_ABI_API int qwn_kv_decode_step_host(QwnKvPoolHandle *h, const QwnKvHost
         }
         p->layer_events = r->num_layers;
     }
-    cudaEvent_t t0, t1;
-    cudaEventCreate(&t0);
-    cudaEventCreate(&t1);
+    if (!p->step_t0) {
+        if ((e = cudaEventCreate(&p->step_t0)) || (e = cudaEventCreate(&p->step_t1)) ||
+            (e = cudaMallocHost(&p->status_host, sizeof(uint32_t)))) {
+            set_cuda_error("qwn_kv_decode_step_host: set-up", e);
+            return QWN_CUDA_STATUS_RUNTIME_ERROR;
+        }
+    }
+    cudaEvent_t t0 = p->step_t0, t1 = p->step_t1;
     cudaEventRecord(t0, p->stream);
-    // per-layer inputs on the copy stream, compute waits per layer, outputs back per layer
-    for (uint32_t L = 0; L < r->num_layers && e == cudaSuccess; L++) {
-        e = cudaMemcpyAsync(p->stage_q + L * q_el, r->host_query + L * q_el, q_el * 4, cudaMemcpyHostToDevice,
+    // The layers go in chunks: the first and the last of one layer, the rest
+    // in about five spans.  Each chunk's inputs arrive on the copy stream, the
+    // compute stream waits for them once and then launches the chunk's layers
+    // back to back -- with no stream operation between two attention
+    // launches, so each may start early on the SMs the one before leaves --
+    // and the chunk's outputs go back on the output stream as soon as its
+    // last layer is done, while the next chunk computes.
+    const uint32_t NL = r->num_layers;
+    constexpr uint32_t kChunks = 7;  // at most: the first layer, five spans, the last layer
+    uint32_t bounds[kChunks + 1];
+    uint32_t nchunks = 0;
+    bounds[0] = 0;
+    {
+        const uint32_t mid = NL > 2 ? NL - 2 : 0;  // layers between the first and the last
+        const uint32_t span = mid ? (mid + kChunks - 3) / (kChunks - 2) : 1;
+        uint32_t at = 1;
+        bounds[++nchunks] = 1;  // the first layer alone: compute starts after one layer's copy
+        while (NL > 1 && at < NL - 1) {
+            at = at + span < NL - 1 ? at + span : NL - 1;
+            bounds[++nchunks] = at;
+        }
+        if (NL > 1) bounds[++nchunks] = NL;  // the last layer alone: its copy out is the only tail
+    }
+    for (uint32_t c = 0; c < nchunks && e == cudaSuccess; c++) {
+        const uint32_t a = bounds[c], n = bounds[c + 1] - a;
+        e = cudaMemcpyAsync(p->stage_q + a * q_el, r->host_query + a * q_el, n * q_el * 4, cudaMemcpyHostToDevice,
                             p->copy_stream);
         if (e == cudaSuccess)
-            e = cudaMemcpyAsync(p->stage_k + L * kv_el, r->host_key + L * kv_el, kv_el * 4,
+            e = cudaMemcpyAsync(p->stage_k + a * kv_el, r->host_key + a * kv_el, n * kv_el * 4,
                                 cudaMemcpyHostToDevice, p->copy_stream);
         if (e == cudaSuccess)
-            e = cudaMemcpyAsync(p->stage_v + L * kv_el, r->host_value + L * kv_el, kv_el * 4,
+            e = cudaMemcpyAsync(p->stage_v + a * kv_el, r->host_value + a * kv_el, n * kv_el * 4,
                                 cudaMemcpyHostToDevice, p->copy_stream);
-        if (e == cudaSuccess) e = cudaEventRecord(p->layer_in_ev[L], p->copy_stream);
+        if (e == cudaSuccess) e = cudaEventRecord(p->layer_in_ev[c], p->copy_stream);
     }
     if (e == cudaSuccess) e = launch_seq_append(p, r->num_seqs, nullptr, nullptr, p->stream);
-    for (uint32_t L = 0; L < r->num_layers && e == cudaSuccess; L++) {
-        e = cudaStreamWaitEvent(p->stream, p->layer_in_ev[L], 0);
-        QwnKvDecodeRequest d{};
-        qwn_cuda_abi_header_init(&d.header, sizeof(d));
-        d.layer = L;
-        d.num_seqs = r->num_seqs;
-        d.query_heads = r->query_heads;
-        d.scale = r->scale;
-        d.query_dev = p->stage_q + L * q_el;
-        d.key_dev = p->stage_k + L * kv_el;
-        d.value_dev = p->stage_v + L * kv_el;
-        d.output_dev = p->stage_o + L * q_el;
-        if (e == cudaSuccess && decode_impl(p, &d, p->stream) != QWN_CUDA_STATUS_OK) e = cudaErrorLaunchFailure;
-        if (e == cudaSuccess) e = cudaEventRecord(p->layer_out_ev[L], p->stream);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->copy_stream, p->layer_out_ev[L], 0);
+    for (uint32_t c = 0; c < nchunks && e == cudaSuccess; c++) {
+        e = cudaStreamWaitEvent(p->stream, p->layer_in_ev[c], 0);
+        for (uint32_t L = bounds[c]; L < bounds[c + 1] && e == cudaSuccess; L++) {
+            QwnKvDecodeRequest d{};
+            qwn_cuda_abi_header_init(&d.header, sizeof(d));
+            d.layer = L;
+            d.num_seqs = r->num_seqs;
+            d.query_heads = r->query_heads;
+            d.scale = r->scale;
+            d.query_dev = p->stage_q + L * q_el;
+            d.key_dev = p->stage_k + L * kv_el;
+            d.value_dev = p->stage_v + L * kv_el;
+            d.output_dev = p->stage_o + L * q_el;
+            if (decode_impl(p, &d, p->stream) != QWN_CUDA_STATUS_OK) e = cudaErrorLaunchFailure;
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(p->layer_out_ev[c], p->stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->out_stream, p->layer_out_ev[c], 0);
         if (e == cudaSuccess)
-            e = cudaMemcpyAsync(r->host_output + L * q_el, p->stage_o + L * q_el, q_el * 4,
-                                cudaMemcpyDeviceToHost, p->copy_stream);
+            e = cudaMemcpyAsync(r->host_output + bounds[c] * q_el, p->stage_o + bounds[c] * q_el,
+                                (bounds[c + 1] - bounds[c]) * q_el * 4, cudaMemcpyDeviceToHost, p->out_stream);
     }
+    // the status word comes back with the step (no separate synchronous read)
+    if (e == cudaSuccess) e = cudaMemcpyAsync(p->status_host, p->status, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                              p->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(t1, p->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(p->copy_stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(p->out_stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(p->stream);
-    cudaEventRecord(t1, p->stream);
-    cudaEventSynchronize(t1);
     float ms = 0.f;
-    cudaEventElapsedTime(&ms, t0, t1);
-    cudaEventDestroy(t0);
-    cudaEventDestroy(t1);
+    if (e == cudaSuccess) cudaEventElapsedTime(&ms, t0, t1);
     if (e != cudaSuccess) { set_cuda_error("qwn_kv_decode_step_host", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
-    // read and clear the status word, as qwn_kv_pool_check does, so that one
-    // latched error fails this step and not every later one; an abandoned
-    // split-KV merge (wait timeout) also leaves counters that must restart at 0
-    uint32_t st = 0;
-    e = cudaMemcpy(&st, p->status, sizeof(st), cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess && st) e = cudaMemset(p->status, 0, sizeof(uint32_t));
+    // clear a latched status word, as qwn_kv_pool_check does, so that one
+    // error fails this step and not every later one; an abandoned split-KV
+    // merge (wait timeout) also leaves counters that must restart at 0
+    const uint32_t st = *p->status_host;
+    if (st) e = cudaMemset(p->status, 0, sizeof(uint32_t));
     if (e == cudaSuccess && (st & QWN_KV_STATUS_WAIT_TIMEOUT))
         e = cudaMemset(p->counters, 0, sizeof(uint32_t) * counter_count(p));
     if (e != cudaSuccess) { set_cuda_error("qwn_kv_decode_step_host: status", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }

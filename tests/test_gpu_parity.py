@@ -253,12 +253,14 @@ def test_page_mass_and_eviction_bit_exact(cuda):
         tw.close()
 
 
-def test_host_step_matches_device_step(cuda):
+@pytest.mark.parametrize("L", [3, 12])
+def test_host_step_matches_device_step(cuda, L):
     """The e2e entry point (host buffers, copies inside) gives the same
-    outputs as the device-resident path."""
+    outputs as the device-resident path.  It moves the layers in chunks (the
+    first and last alone, the rest in spans): 12 layers make spans of two."""
     import qwanto_b200 as qb
     torch = cuda
-    L, B, H, HK = 3, 4, 32, 8
+    B, H, HK = 4, 32, 8
     pools = [qb.KvPool(2, L, HK, 16, 300, B, 64, max_query_heads=H, permutation_seed=2) for _ in range(2)]
     try:
         for p in pools:
