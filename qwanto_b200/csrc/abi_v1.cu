@@ -64,6 +64,9 @@ struct Context {
     float *d_out = nullptr, *d_scales = nullptr;
     size_t in_cap = 0, out_cap = 0, sc_cap = 0;
     QwnCudaTelemetry tel{};
+    // paged attention with a query-to-kv-head map that is not uniform: the
+    // query and output rows in the padded kv_heads x G' layout (host side)
+    std::vector<float> pad_q, pad_o;
 };
 
 Context *ctx_from(const QwnCudaContextHandle *h) {
@@ -786,21 +789,50 @@ QWN_CUDA_ABI_API int qwn_cuda_abi_kv_cache_attention(QwnCudaContextHandle *h, co
         set_error("invalid Q8 KV-cache attention request");
         return QWN_CUDA_STATUS_INVALID_ARGUMENT;
     }
-    const bool uniform = r->query_heads % r->kv_heads == 0 && r->query_heads / r->kv_heads <= (uint32_t)kMaxGroup;
-    if (k->paged && !uniform) {
-        set_error("paged Q8 attention needs query_heads = kv_heads x G with G <= 8");
+    // Query head h reads kv head (h * kv_heads) / query_heads, as in the
+    // reference (c/cuda/qwn_hypervsq2_cuda_abi.cu:184).  The paged kernel
+    // takes G query heads per kv head; when the map is not uniform, the rows
+    // go through a padded kv_heads x G' layout (G' = the largest group, the
+    // spare rows zero and their outputs dropped).
+    const uint32_t Hq = r->query_heads, HK = r->kv_heads;
+    const bool uniform = Hq % HK == 0;
+    uint32_t Gp = uniform ? Hq / HK : 0;
+    std::vector<uint32_t> slot;  // padded row of query head h (non-uniform map)
+    if (!uniform) {
+        std::vector<uint32_t> cnt(HK, 0);
+        slot.resize(Hq);
+        for (uint32_t h = 0; h < Hq; h++) {
+            const uint32_t kv = (uint32_t)(((uint64_t)h * HK) / Hq);
+            slot[h] = cnt[kv]++;  // index within its group; the group base is added below
+        }
+        for (uint32_t j = 0; j < HK; j++) Gp = cnt[j] > Gp ? cnt[j] : Gp;
+        for (uint32_t h = 0; h < Hq; h++) slot[h] += (uint32_t)(((uint64_t)h * HK) / Hq) * Gp;
+    }
+    if (k->paged && Gp > (uint32_t)kMaxGroup) {
+        set_error("paged Q8 attention takes at most 8 query heads per kv head");
         return QWN_CUDA_STATUS_UNSUPPORTED;
     }
+    const bool padded = k->paged && !uniform;
     std::lock_guard<std::mutex> lk(g_abi_mu);
     cudaSetDevice(c->device);
-    const size_t qn = (size_t)r->query_heads * k->head_dim;
+    const uint32_t Hrows = padded ? HK * Gp : Hq;  // query rows the device sees
+    const size_t qn = (size_t)Hrows * k->head_dim;
+    const float *q_src = r->host_query;
+    if (padded) {
+        c->pad_q.assign(qn, 0.f);
+        c->pad_o.resize(qn);
+        for (uint32_t h = 0; h < Hq; h++)
+            std::memcpy(&c->pad_q[(size_t)slot[h] * k->head_dim], r->host_query + (size_t)h * k->head_dim,
+                        k->head_dim * sizeof(float));
+        q_src = c->pad_q.data();
+    }
     if (!grow((void **)&c->d_q, &c->q_cap, qn * 4) || !grow((void **)&c->d_o, &c->o_cap, qn * 4)) {
         set_error("Q8 KV attention: staging allocation failed");
         return QWN_CUDA_STATUS_OUT_OF_MEMORY;
     }
     float *d_o = c->d_o;
     const auto t0 = std::chrono::steady_clock::now();
-    cudaError_t e = cudaMemcpyAsync(c->d_q, r->host_query, qn * 4, cudaMemcpyHostToDevice, c->stream);
+    cudaError_t e = cudaMemcpyAsync(c->d_q, q_src, qn * 4, cudaMemcpyHostToDevice, c->stream);
     uint64_t launches = 0;
     if (e == cudaSuccess) e = cudaEventRecord(c->ev0, c->stream);
     if (e == cudaSuccess) {
@@ -809,7 +841,7 @@ QWN_CUDA_ABI_API int qwn_cuda_abi_kv_cache_attention(QwnCudaContextHandle *h, co
             AttnLaunch a{};
             a.layer = 0;
             a.num_seqs = 1;
-            a.query_heads = r->query_heads;
+            a.query_heads = Hrows;
             a.attend_limit = r->position + 1;
             a.query = c->d_q;
             a.output = d_o;
@@ -834,14 +866,26 @@ QWN_CUDA_ABI_API int qwn_cuda_abi_kv_cache_attention(QwnCudaContextHandle *h, co
         }
     }
     if (e == cudaSuccess) e = cudaEventRecord(c->ev1, c->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(r->host_output, d_o, qn * 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(padded ? c->pad_o.data() : r->host_output, d_o, qn * 4, cudaMemcpyDeviceToHost,
+                            c->stream);
+    // the paged pool's status word, read on this stream (no device-wide sync)
+    uint32_t st = 0;
+    Pool *pp = k->paged ? pool_from(&k->pool) : nullptr;
+    if (e == cudaSuccess && pp) e = cudaMemcpyAsync(&st, pp->status, sizeof(st), cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) { set_cuda_error("Q8 KV attention", e); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
-    if (k->paged) {
-        uint32_t st = 0;
-        qwn_kv_pool_check(&k->pool, &st);
-        if (st) { set_error("Q8 KV attention: device status error"); return QWN_CUDA_STATUS_RUNTIME_ERROR; }
+    if (st) {  // clear it, as qwn_kv_pool_check does, and fail this call
+        cudaMemsetAsync(pp->status, 0, sizeof(uint32_t), c->stream);
+        if (st & QWN_KV_STATUS_WAIT_TIMEOUT) cudaMemsetAsync(pp->counters, 0, sizeof(uint32_t) * counter_count(pp), c->stream);
+        cudaStreamSynchronize(c->stream);
+        set_error("Q8 KV attention: device status error");
+        return QWN_CUDA_STATUS_RUNTIME_ERROR;
     }
+    if (padded)
+        for (uint32_t h = 0; h < Hq; h++)
+            std::memcpy(r->host_output + (size_t)h * k->head_dim, &c->pad_o[(size_t)slot[h] * k->head_dim],
+                        k->head_dim * sizeof(float));
     float ms = 0.f;
     cudaEventElapsedTime(&ms, c->ev0, c->ev1);
     c->tel.kv_cache_kernel_count += launches;

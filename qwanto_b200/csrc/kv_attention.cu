@@ -330,11 +330,14 @@ struct Int8T {
         for (int kb = 0; kb < 4; kb++)
 #pragma unroll
             for (int nb = 0; nb < kNB; nb++) {
-                if (kb & 1)
-                    imma16832(acc[nb][kb >> 1], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3], f.b[nb][kb][0],
+                // per 64-channel scales (codec 1): one sum per half of the
+                // head; per-head scale (codec 2): one chain over all 128 dims
+                const int half = kB64 ? (kb >> 1) : 0;
+                if (kB64 ? (kb & 1) : kb != 0)
+                    imma16832(acc[nb][half], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3], f.b[nb][kb][0],
                               f.b[nb][kb][1]);
                 else
-                    imma16832_z(acc[nb][kb >> 1], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3], f.b[nb][kb][0],
+                    imma16832_z(acc[nb][half], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3], f.b[nb][kb][0],
                                 f.b[nb][kb][1]);
             }
         float s[HG][2];
@@ -356,7 +359,7 @@ struct Int8T {
                         raw[hg][kX - 1] =
                             fmaf(small_int_to_float(acc[nb][1][c], f.magic[kX - 1][j]), f.sc[j], raw[hg][kX - 1]);
                     } else {
-                        raw[hg][0] = fmaf(small_int_to_float(acc[nb][0][c] + acc[nb][1][c], f.magic[0][j]), f.sc[j],
+                        raw[hg][0] = fmaf(small_int_to_float(acc[nb][0][c], f.magic[0][j]), f.sc[j],
                                           raw[hg][0]);
                     }
                 }

@@ -314,15 +314,18 @@ def _cpu_attention_q8(keys, values, ks, vs, query, H, HK, hd, pos, scale):
 
 
 @pytest.mark.parametrize("head_dim", [4, 128])
-def test_abi_v1_mirrors_reference_cuda_q8_test(cuda, oracle_mod, head_dim):
+@pytest.mark.parametrize("H,HK", [(4, 2), (6, 4), (12, 8), (2, 4)])
+def test_abi_v1_mirrors_reference_cuda_q8_test(cuda, oracle_mod, head_dim, H, HK):
     """c/tests/test_cuda_q8_kv.cu:82-167 through the ABI v1 entry points:
     2 tokens, 4 query heads, 2 kv heads, scale 0.5; max error <= 1e-4 and the
     resident bytes return to 0 after destroy.  head_dim 4 runs the generic
-    kernels, head_dim 128 the paged B200 kernels."""
+    kernels, head_dim 128 the paged B200 kernels.  The other head counts map
+    query head h to kv head h * HK / H unevenly, as the reference allows (the
+    paged path pads the groups)."""
     import qwanto_b200 as qb
     ctx = qb.CudaContext(0)
     try:
-        tokens, H, HK, hd = 2, 4, 2, head_dim
+        tokens, hd = 2, head_dim
         ch = HK * hd
         cache = ctx.kv_cache_create(8, HK, hd)
         key = np.array([(i - 3) * 0.17 for i in range(tokens * ch)], np.float32)
