@@ -294,9 +294,12 @@ struct Int8T {
         for (int x = 0; x < kX; x++) { st.nu[x] = 0.f; st.inv_nu[x] = 0.f; }
     }
 
-    __device__ static void step(const uint8_t *tile, const Frag &f, State &st, int t_lo, int t_hi,
-                                float (&psum)[HG]) {
+    // scores of one tile (base 2, masked to -inf outside [t_lo, t_hi)) and
+    // the V scales of its tokens gid, gid+8 (zero outside the range)
+    __device__ static void scores(const uint8_t *tile, const Frag &f, int t_lo, int t_hi, float (&s)[HG][2],
+                                  float (&vs)[kX][2]) {
         const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+        (void)tig;
         // ---- K fragments: token rows gid and gid+8
         const int sw = (gid & 1) << 2;
         const uint8_t *r0 = tile + 128 * gid, *r1 = tile + 128 * (gid + 8);
@@ -309,7 +312,7 @@ struct Int8T {
                                    {k01.x, k11.x, k01.y, k11.y},
                                    {k01.z, k11.z, k01.w, k11.w}};
         // ---- scales of tokens gid, gid+8
-        float ks[kX][2], vs[kX][2];
+        float ks[kX][2];
         if constexpr (kB64) {
             const float4 k4 = *reinterpret_cast<const float4 *>(tile + 4096 + 16 * gid);
             const float4 v4 = *reinterpret_cast<const float4 *>(tile + 4224 + 16 * gid);
@@ -340,7 +343,6 @@ struct Int8T {
                     imma16832_z(acc[nb][half], ka[kb][0], ka[kb][1], ka[kb][2], ka[kb][3], f.b[nb][kb][0],
                                 f.b[nb][kb][1]);
             }
-        float s[HG][2];
 #pragma unroll
         for (int tk = 0; tk < 2; tk++) {
             float raw[HG][kX];
@@ -370,59 +372,18 @@ struct Int8T {
                 s[hg][tk] = (tk ? ok1 : ok0) ? sc : -INFINITY;
             }
         }
-        // ---- online softmax per head (reduction over the 8 token lanes gid)
-        float p[HG][2];
-#pragma unroll
-        for (int hg = 0; hg < HG; hg++) {
-            float tmax = fmaxf(s[hg][0], s[hg][1]);
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
-            const float m_new = fmaxf(st.m[hg], tmax);
-            if (__any_sync(0xffffffffu, m_new > st.m[hg])) {
-                const float alpha = ex2(st.m[hg] - m_new);
-                st.l[hg] *= alpha;
-#pragma unroll
-                for (int mb = 0; mb < 8; mb++) {
-                    st.o[hg][mb][0] *= alpha; st.o[hg][mb][1] *= alpha;
-                    st.o[hg][mb][2] *= alpha; st.o[hg][mb][3] *= alpha;
-                }
-                st.m[hg] = m_new;
-            }
-            p[hg][0] = ex2(s[hg][0] - st.m[hg]);
-            p[hg][1] = ex2(s[hg][1] - st.m[hg]);
-            st.l[hg] += p[hg][0] + p[hg][1];
-            psum[hg] = p[hg][0] + p[hg][1];
-        }
-        // ---- V scales -> normaliser nu (shared by all heads)
+
 #pragma unroll
         for (int x = 0; x < kX; x++) {
             vs[x][0] = ok0 ? vs[x][0] : 0.f;
             vs[x][1] = ok1 ? vs[x][1] : 0.f;
-            const float lmax = fmaxf(vs[x][0], vs[x][1]);
-            const bool first = st.nu[x] == 0.f;
-            if (__any_sync(0xffffffffu, first || lmax > st.nu[x] * kNuHeadroom)) {
-                float vmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, 4));
-                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 8));
-                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 16));
-                const float nn = fmaxf(pow2ceil(vmax), kNuFloor);
-                if (first) {
-                    st.nu[x] = nn;
-                } else if (nn > st.nu[x]) {
-                    const float r = st.nu[x] / nn;
-#pragma unroll
-                    for (int hg = 0; hg < HG; hg++)
-#pragma unroll
-                        for (int mb = 0; mb < 8; mb++) {
-                            if (kB64 && (mb >> 2) != x) continue;
-                            st.o[hg][mb][0] *= r; st.o[hg][mb][1] *= r;
-                            st.o[hg][mb][2] *= r; st.o[hg][mb][3] *= r;
-                        }
-                    st.nu[x] = nn;
-                }
-                st.inv_nu[x] = 1.0f / st.nu[x];
-            }
         }
+    }
+
+    // P x V of one tile: P' = p * vs / nu as f16 hi+lo, transposed into the
+    // B operand; V codes -> exact f16 A fragments
+    __device__ static void pv(const uint8_t *tile, State &st, const float (&p)[HG][2], const float (&vs)[kX][2]) {
+        const int lane = threadIdx.x & 31;
         // ---- P' = p * vs / nu as f16 hi+lo, transposed into the PV B operand
         uint32_t bp[HG][kX][2];
 #pragma unroll
@@ -456,6 +417,86 @@ struct Int8T {
                 for (int hg = 0; hg < HG; hg++) mma16816(st.o[hg][mb], a, bp[hg][x][0], bp[hg][x][1]);
             }
         }
+    }
+
+    // NT consecutive tiles of one segment: their scores, one online-softmax
+    // update and one normaliser check for all of them, then P x V per tile
+    template <int NT>
+    __device__ static void stepn(const uint8_t *const (&tiles)[NT], const Frag &f, State &st,
+                                 const int (&t_lo)[NT], const int (&t_hi)[NT], float (&psum)[NT][HG]) {
+        float s[NT][HG][2], vs[NT][kX][2];
+#pragma unroll
+        for (int u = 0; u < NT; u++) scores(tiles[u], f, t_lo[u], t_hi[u], s[u], vs[u]);
+        // ---- online softmax per head (reduction over the 8 token lanes gid)
+        float p[NT][HG][2];
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) {
+            float tmax = fmaxf(s[0][hg][0], s[0][hg][1]);
+#pragma unroll
+            for (int u = 1; u < NT; u++) tmax = fmaxf(tmax, fmaxf(s[u][hg][0], s[u][hg][1]));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+            const float m_new = fmaxf(st.m[hg], tmax);
+            if (__any_sync(0xffffffffu, m_new > st.m[hg])) {
+                const float alpha = ex2(st.m[hg] - m_new);
+                st.l[hg] *= alpha;
+#pragma unroll
+                for (int mb = 0; mb < 8; mb++) {
+                    st.o[hg][mb][0] *= alpha; st.o[hg][mb][1] *= alpha;
+                    st.o[hg][mb][2] *= alpha; st.o[hg][mb][3] *= alpha;
+                }
+                st.m[hg] = m_new;
+            }
+#pragma unroll
+            for (int u = 0; u < NT; u++) {
+                p[u][hg][0] = ex2(s[u][hg][0] - st.m[hg]);
+                p[u][hg][1] = ex2(s[u][hg][1] - st.m[hg]);
+                psum[u][hg] = p[u][hg][0] + p[u][hg][1];
+                st.l[hg] += psum[u][hg];
+            }
+        }
+        // ---- V scales -> normaliser nu (shared by all heads)
+#pragma unroll
+        for (int x = 0; x < kX; x++) {
+            float lmax = fmaxf(vs[0][x][0], vs[0][x][1]);
+#pragma unroll
+            for (int u = 1; u < NT; u++) lmax = fmaxf(lmax, fmaxf(vs[u][x][0], vs[u][x][1]));
+            const bool first = st.nu[x] == 0.f;
+            if (__any_sync(0xffffffffu, first || lmax > st.nu[x] * kNuHeadroom)) {
+                float vmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, 4));
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 8));
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 16));
+                const float nn = fmaxf(pow2ceil(vmax), kNuFloor);
+                if (first) {
+                    st.nu[x] = nn;
+                } else if (nn > st.nu[x]) {
+                    const float r = st.nu[x] / nn;
+#pragma unroll
+                    for (int hg = 0; hg < HG; hg++)
+#pragma unroll
+                        for (int mb = 0; mb < 8; mb++) {
+                            if (kB64 && (mb >> 2) != x) continue;
+                            st.o[hg][mb][0] *= r; st.o[hg][mb][1] *= r;
+                            st.o[hg][mb][2] *= r; st.o[hg][mb][3] *= r;
+                        }
+                    st.nu[x] = nn;
+                }
+                st.inv_nu[x] = 1.0f / st.nu[x];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < NT; u++) pv(tiles[u], st, p[u], vs[u]);
+    }
+
+    __device__ static void step(const uint8_t *tile, const Frag &f, State &st, int t_lo, int t_hi,
+                                float (&psum)[HG]) {
+        const uint8_t *const tiles[1] = {tile};
+        const int lo[1] = {t_lo}, hi[1] = {t_hi};
+        float ps[1][HG];
+        stepn<1>(tiles, f, st, lo, hi, ps);
+#pragma unroll
+        for (int hg = 0; hg < HG; hg++) psum[hg] = ps[0][hg];
     }
 
     // tile probability mass and running max per head (eviction scores)
