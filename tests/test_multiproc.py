@@ -72,23 +72,27 @@ def _rank_main(rank, world, port, seed, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.timeout(120)
-def test_kv_range_split_merge_two_gloo_ranks():
+@pytest.mark.timeout(180)
+@pytest.mark.parametrize("world", [2, 4])
+def test_kv_range_split_merge_gloo_ranks(world):
+    """One context split into `world` page-aligned ranges, a partial (m, l, o)
+    per rank, all-gathered and merged on every rank: equal to the whole
+    attention on every rank (the host side of the split-KV path)."""
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, 7, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, 7, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=100)
+        p.join(timeout=150)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
             p.kill()
-    assert codes == [0, 0], codes
-    errs = dict(q.get(timeout=5) for _ in range(2))
+    assert codes == [0] * world, codes
+    errs = dict(q.get(timeout=5) for _ in range(world))
     assert max(errs.values()) < 1e-5, errs
 
 
